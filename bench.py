@@ -1,0 +1,464 @@
+#!/usr/bin/env python3
+"""Benchmark: AES-128-GCM seal + authenticated open of Llama-3-8B KV chunks.
+
+One step = seal a batch of 32 KV objects [2, 32 layers, 256 tokens, 8 KV heads,
+128] bf16 (32 MiB each, N(0,1), seeded; inputs resident in HBM) into frames
+[1 | IV | ct | tag], then open all 32 frames with tag verification. Each GPU
+(one process per GPU under torchrun) seals its own 32 objects: no collective
+on the data path, weak scaling. value = plaintext bytes sealed + opened by all
+ranks / max-over-ranks device time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's own OpenSSL CPU backend
+(lmcache_aes128gcm_seal/open from oracle/_ref/libcpu_seal.so) on the host
+cores with one thread per core, on the same objects, metric and unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "AES-GCM seal/open GB/s (32 MiB KV objects) at 1/2/4/8 B200 vs OpenSSL host"
+UNIT = "GB/s"
+SHAPE = (2, 32, 256, 8, 128)
+OBJECTS = 32
+SEED = 2
+WORKLOAD = "llama3_8b_kv_chunk_32MiB_x32_seal_then_open"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-objects", type=int, default=0,
+                    help="objects per OpenSSL thread in the cpu_baseline sample (0 = auto)")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def load_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes from a committed ncu summary, if present."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- ours
+
+def run_ours(args, rank, world, local):
+    import torch
+
+    from confkv_b200 import build, workloads
+    from confkv_b200.gpu_aesgcm import GpuAes128GcmKey, GpuAesGcmLibrary
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if rank == 0:
+        build.build()
+    if world > 1:
+        torch.distributed.barrier()
+    lib = GpuAesGcmLibrary()
+
+    P = workloads.nbytes_of(SHAPE)
+    frame_len = P + 29
+    stride = (frame_len + 255) // 256 * 256
+    key_bytes = workloads.make_key(SEED)
+    ivs = workloads.make_ivs(SEED * 100 + rank, OBJECTS)
+    key = GpuAes128GcmKey(lib, key_bytes, device=local)
+    key.reserve(P)
+
+    plain = workloads.bf16_batch(SHAPE, OBJECTS, seed=SEED * 100 + rank, device=dev)  # [32, ...] bf16
+    plain_u8 = plain.view(torch.uint8).reshape(OBJECTS, P)
+    frames = torch.empty((OBJECTS, stride), dtype=torch.uint8, device=dev)
+    opened = torch.empty((OBJECTS, P), dtype=torch.uint8, device=dev)
+    auth = torch.zeros((OBJECTS,), dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+
+    def seal_all():
+        for k in range(OBJECTS):
+            key.seal_async(src_ptr=plain_u8[k].data_ptr(), plaintext_len=P, dst_ptr=frames[k].data_ptr(),
+                           dst_capacity=stride, iv=ivs[k], stream_ptr=sp)
+
+    def open_all():
+        for k in range(OBJECTS):
+            key.open_async(src_ptr=frames[k].data_ptr(), frame_len=frame_len, dst_ptr=opened[k].data_ptr(),
+                           plaintext_len=P, auth_ok_ptr=auth[k:k + 1].data_ptr(), stream_ptr=sp)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        seal_all()
+        open_all()
+    barrier()
+    assert bool((auth == 1).all()), "warm-up open failed authentication"
+    assert torch.equal(opened, plain_u8), "warm-up round trip mismatch"
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    with torch.cuda.stream(stream):
+        for s in range(args.steps):
+            ev[s][0].record(stream)
+            seal_all()
+            ev[s][1].record(stream)
+            open_all()
+            ev[s][2].record(stream)
+    barrier()
+    clk = clocks.stop()
+    seal_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    open_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    total_ms = sum(a + b for a, b in zip(seal_ms, open_ms))
+    ok = bool((auth == 1).all()) and torch.equal(opened, plain_u8)
+
+    # e2e through the public API: pinned host plaintext -> H2D -> seal -> D2H
+    # frames, then open -> D2H auth flags; copies overlapped across objects.
+    e2e = run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args)
+
+    t = torch.tensor([total_ms, sum(seal_ms), sum(open_ms), e2e["ms"], float(ok)], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        mn = t.clone()
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+        total_ms, seal_sum, open_sum, e2e_ms = mx[0].item(), mx[1].item(), mx[2].item(), mx[3].item()
+        ok = mn[4].item() == 1.0
+    else:
+        seal_sum, open_sum, e2e_ms = sum(seal_ms), sum(open_ms), e2e["ms"]
+
+    if rank == 0:
+        bytes_per_step = 2 * OBJECTS * P * world  # sealed + opened plaintext, all ranks
+        ms_per_step = total_ms / args.steps
+        value = bytes_per_step / (ms_per_step * 1e-3) / 1e9
+        seal_gbs = OBJECTS * P * world / (seal_sum / args.steps * 1e-3) / 1e9
+        open_gbs = OBJECTS * P * world / (open_sum / args.steps * 1e-3) / 1e9
+        peak, peak_kind = load_peaks()
+        # dominant kernel: seal_kernel, one launch per object; algorithmic
+        # bytes = read P + write P + 29.
+        seal_launch_ms = seal_sum / args.steps / OBJECTS
+        achieved = (2 * P + 29) / (seal_launch_ms * 1e-3) / 1e9
+        traffic = profile_traffic("seal_kernel_kv_llama8b.txt")
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "u8",
+            "data": "synthetic: bf16 N(0,1) KV chunks from fixed seeds, resident in HBM",
+            "config": {"workload": WORKLOAD, "objects_per_gpu": OBJECTS, "object_shape": list(SHAPE),
+                       "object_bytes": P, "step": "seal 32 objects then open 32 frames with tag check",
+                       "l2": "inputs larger than L2 (1 GiB plaintext per GPU)",
+                       "parallelism": f"independent objects per GPU x{world}, no collective"},
+            "seal_gbs": round(seal_gbs, 2),
+            "open_gbs": round(open_gbs, 2),
+            "round_trip_ok": ok,
+            "roofline": {"bound": "hbm", "kernel": "seal_kernel", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                         "algorithmic_bytes_per_launch": 2 * P + 29,
+                         "traffic": traffic},
+            "e2e": {"value": round(e2e["gbs"] * world, 2) if world == 1 else
+                    round(2 * OBJECTS * P * world / (e2e_ms * 1e-3) / 1e9, 2),
+                    "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                    "what": "pinned host plaintext -> H2D -> seal -> D2H frames; open -> D2H auth; "
+                            "copies overlapped across objects on three streams"},
+            "gpu_launches": 3 * OBJECTS * args.steps,
+            "clocks": clk,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(args)
+        print(json.dumps(line), flush=True)
+
+    key.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
+    """Same step through the public API with host buffers and copies timed."""
+    n = plain_u8.shape[0]
+    host_in = torch.empty((n, P), dtype=torch.uint8, pin_memory=True)
+    host_in.copy_(plain_u8.cpu())
+    host_frames = torch.empty((n, stride), dtype=torch.uint8, pin_memory=True)
+    host_auth = torch.empty((n,), dtype=torch.int32, pin_memory=True)
+    d_in = torch.empty_like(plain_u8)
+    d_frames = torch.empty((n, stride), dtype=torch.uint8, device=dev)
+    d_out = torch.empty_like(plain_u8)
+    d_auth = torch.zeros((n,), dtype=torch.int32, device=dev)
+    s_h2d, s_cmp, s_d2h = (torch.cuda.Stream(device=dev) for _ in range(3))
+    frame_len = P + 29
+
+    def step():
+        for k in range(n):
+            e_in = torch.cuda.Event()
+            with torch.cuda.stream(s_h2d):
+                d_in[k].copy_(host_in[k], non_blocking=True)
+                e_in.record(s_h2d)
+            s_cmp.wait_event(e_in)
+            key.seal_async(src_ptr=d_in[k].data_ptr(), plaintext_len=P, dst_ptr=d_frames[k].data_ptr(),
+                           dst_capacity=stride, iv=ivs[k], stream_ptr=s_cmp.cuda_stream)
+            e_seal = torch.cuda.Event()
+            e_seal.record(s_cmp)
+            s_d2h.wait_event(e_seal)
+            with torch.cuda.stream(s_d2h):
+                host_frames[k].copy_(d_frames[k], non_blocking=True)
+        for k in range(n):
+            key.open_async(src_ptr=d_frames[k].data_ptr(), frame_len=frame_len, dst_ptr=d_out[k].data_ptr(),
+                           plaintext_len=P, auth_ok_ptr=d_auth[k:k + 1].data_ptr(), stream_ptr=s_cmp.cuda_stream)
+        e_open = torch.cuda.Event()
+        e_open.record(s_cmp)
+        s_d2h.wait_event(e_open)
+        with torch.cuda.stream(s_d2h):
+            host_auth.copy_(d_auth, non_blocking=True)
+
+    steps = max(2, min(args.steps, 5))
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(s_h2d)
+    s_cmp.wait_event(t0)
+    s_d2h.wait_event(t0)
+    for _ in range(steps):
+        step()
+    e_c, e_d = torch.cuda.Event(), torch.cuda.Event()
+    e_c.record(s_cmp)
+    e_d.record(s_d2h)
+    s_h2d.wait_event(e_c)
+    s_h2d.wait_event(e_d)
+    t1.record(s_h2d)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / steps
+    assert bool((host_auth == 1).all())
+    return {"ms": ms, "gbs": 2 * n * P / (ms * 1e-3) / 1e9, "h2d": n * P, "d2h": n * (stride) + 4 * n}
+
+
+# ------------------------------------------------------- CPU (reference)
+
+def load_ref_lib():
+    so = ROOT / "oracle" / "_ref" / "libcpu_seal.so"
+    if not so.exists():
+        subprocess.run(["make", "-C", str(ROOT / "oracle"), "ref"], capture_output=True)
+    if not so.exists():
+        return None
+    lib = ctypes.CDLL(str(so))
+    vp, sz = ctypes.c_void_p, ctypes.c_size_t
+    lib.lmcache_aes128gcm_seal.argtypes = [vp, vp, sz, vp, sz]
+    lib.lmcache_aes128gcm_seal.restype = ctypes.c_int
+    lib.lmcache_aes128gcm_open.argtypes = [vp, vp, sz, vp, sz]
+    lib.lmcache_aes128gcm_open.restype = ctypes.c_int
+    return lib
+
+
+def openssl_threads_run(lib, key: bytes, objects_per_thread: int, threads: int, P: int) -> float:
+    """Each thread seals then opens `objects_per_thread` objects of P bytes
+    (its own bf16 N(0,1) buffer); returns wall seconds for the whole batch."""
+    from confkv_b200 import workloads
+
+    src = workloads.bf16_batch(SHAPE, 1, seed=SEED * 100).view(-1).view(__import__("torch").uint8).numpy()
+    bufs = []
+    for _ in range(threads):
+        s = np.array(src, copy=True)
+        f = np.empty(P + 29, dtype=np.uint8)
+        o = np.empty(P, dtype=np.uint8)
+        f[:] = 0
+        o[:] = 0
+        bufs.append((s, f, o))
+    errors = []
+    start_evt = threading.Barrier(threads + 1)
+
+    def worker(t):
+        s, f, o = bufs[t]
+        start_evt.wait()
+        for _ in range(objects_per_thread):
+            if lib.lmcache_aes128gcm_seal(key, s.ctypes.data, P, f.ctypes.data, P + 29) != 0:
+                errors.append("seal")
+            if lib.lmcache_aes128gcm_open(key, f.ctypes.data, P + 29, o.ctypes.data, P) != 0:
+                errors.append("open")
+
+    ths = [threading.Thread(target=worker, args=(t,)) for t in range(threads)]
+    for th in ths:
+        th.start()
+    start_evt.wait()
+    t0 = time.perf_counter()
+    for th in ths:
+        th.join()
+    dt = time.perf_counter() - t0
+    assert not errors, errors[:3]
+    assert np.array_equal(bufs[0][2], bufs[0][0])
+    return dt
+
+
+def cpu_baseline(args) -> dict:
+    lib = load_ref_lib()
+    if lib is None:
+        return {"unavailable": "oracle/_ref/libcpu_seal.so missing"}
+    from confkv_b200 import workloads
+
+    P = workloads.nbytes_of(SHAPE)
+    threads = len(os.sched_getaffinity(0))
+    per = args.cpu_sample_objects or max(1, 64 // threads)
+    key = workloads.make_key(SEED)
+    openssl_threads_run(lib, key, 1, threads, P)  # warm-up: page-in buffers
+    dt = openssl_threads_run(lib, key, per, threads, P)
+    gbs = 2 * per * threads * P / dt / 1e9
+    return {"value": round(gbs, 2), "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{per} x 32 MiB bf16 KV object(s) sealed+opened per thread, {threads} threads, "
+                      f"reference lmcache_aes128gcm_seal/open (OpenSSL EVP)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    lib = load_ref_lib()
+    if lib is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference OpenSSL backend could not be built"}))
+        return
+    from confkv_b200 import workloads
+
+    P = workloads.nbytes_of(SHAPE)
+    threads = len(os.sched_getaffinity(0))
+    key = workloads.make_key(SEED)
+    # each step: the 32 objects x world ranks, spread over all host threads
+    total_objects = OBJECTS * world
+    per = max(1, -(-total_objects // threads))
+    for _ in range(args.warmup):
+        openssl_threads_run(lib, key, per, threads, P)
+    times = [openssl_threads_run(lib, key, per, threads, P) for _ in range(args.steps)]
+    objs_done = per * threads
+    ms = statistics.mean(times) * 1e3
+    value = 2 * objs_done * P / (ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic: bf16 N(0,1) KV chunk, host buffers",
+        "config": {"workload": WORKLOAD, "objects_per_step": objs_done, "object_bytes": P,
+                   "step": "seal then open each object on host threads"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"{objs_done} x 32 MiB objects per step over {threads} threads"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

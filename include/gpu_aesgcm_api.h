@@ -1,0 +1,90 @@
+/*
+ * B200 (sm_100a) AES-128-GCM seal/open engine for persistent KV-cache objects.
+ *
+ * Drop-in C-ABI for ConfKV's GPU seal path. Every declaration below keeps the
+ * name, argument list, return convention and memory-space contract of the
+ * reference header experiments/gpu_kv_seal/gpu/gpu_aesgcm_api.h; the line cited
+ * beside each is the declaration it replaces.
+ *
+ * Frame written by seal and consumed by open (reference gpu_aesgcm.cu:14-20):
+ *
+ *     [version = 1][12-byte IV][ciphertext, P bytes][16-byte GCM tag]
+ *
+ * AAD is empty, IVs are 96-bit (J0 = IV || 0^31 || 1).
+ */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque key handle (reference gpu_aesgcm_api.h:10). */
+typedef void* lmcache_gpu_aesgcm_key_t;
+
+/* Return codes (reference gpu_aesgcm_api.h:12-18). Authentication failure is
+ * NOT a return code: open reports it through *auth_ok and a zeroed dst. */
+enum {
+    LMCACHE_GPU_AESGCM_OK = 0,
+    LMCACHE_GPU_AESGCM_ERR_ARGUMENT = -1,
+    LMCACHE_GPU_AESGCM_ERR_ALLOC = -2,
+    LMCACHE_GPU_AESGCM_ERR_CUDA = -3,
+    LMCACHE_GPU_AESGCM_ERR_INTERNAL = -4,
+};
+
+/* P + 29 (reference gpu_aesgcm_api.h:20-22). Needs no GPU. */
+size_t lmcache_gpu_aesgcm_frame_size(size_t plaintext_len);
+
+/*
+ * Expand a 16-byte AES key for `device` (reference gpu_aesgcm_api.h:24-29).
+ * Computes H = E_K(0^128) and the GHASH multiplication tables on the host,
+ * uploads them once, and synchronises the device before returning.
+ * key_len != 16, a null key or a null out -> ERR_ARGUMENT.
+ */
+int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_len, int device,
+                                     lmcache_gpu_aesgcm_key_t* out);
+
+/* Free the handle's device memory; a null handle is OK
+ * (reference gpu_aesgcm_api.h:31-33). */
+int lmcache_gpu_aes128gcm_key_destroy(lmcache_gpu_aesgcm_key_t key);
+
+/*
+ * Pre-size per-call workspace for objects up to max_plaintext_len bytes
+ * (reference gpu_aesgcm_api.h:35-44). The workspace here is a fixed-size
+ * per-handle ring that key_create already allocates, so this only validates
+ * the handle and the size limit; seal/open never call cudaMalloc.
+ */
+int lmcache_gpu_aes128gcm_reserve(lmcache_gpu_aesgcm_key_t key, size_t max_plaintext_len);
+
+/*
+ * Enqueue seal of P = plaintext_len bytes on `stream` (reference
+ * gpu_aesgcm_api.h:46-66). src and dst are DEVICE pointers of any alignment;
+ * iv is a HOST pointer to exactly 12 bytes, copied before return; stream is a
+ * cudaStream_t cast to void* (null = legacy default stream).
+ * dst_capacity < P + 29 or more than 2^32 - 2 blocks -> ERR_ARGUMENT.
+ * rc reports only enqueue errors; the caller synchronises.
+ */
+int lmcache_gpu_aes128gcm_seal_async(lmcache_gpu_aesgcm_key_t key, const void* src,
+                                     size_t plaintext_len, void* dst, size_t dst_capacity,
+                                     const uint8_t* iv, void* stream);
+
+/*
+ * Enqueue authentication-gated open (reference gpu_aesgcm_api.h:68-88).
+ * src (frame), dst (plaintext) and auth_ok are DEVICE pointers. frame_len may
+ * exceed P + 29 (padded frames); the tag is read at offset 13 + P.
+ * *auth_ok becomes 1 when the tag and version byte match, else 0 and the P
+ * bytes of dst are zero-filled. Plaintext is written only after the tag has
+ * been verified on the device, in stream order.
+ */
+int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, const void* src,
+                                     size_t frame_len, void* dst, size_t plaintext_len,
+                                     int* auth_ok, void* stream);
+
+/* rc -> static string (reference gpu_aesgcm_api.h:90-92). */
+const char* lmcache_gpu_aesgcm_strerror(int rc);
+
+#ifdef __cplusplus
+}
+#endif
