@@ -36,7 +36,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "AES-GCM seal/open GB/s (32 MiB KV objects) at 1/2/4/8 B200 vs OpenSSL host"
 UNIT = "GB/s"
 SHAPE = (2, 32, 256, 8, 128)
-OBJECTS = 32
+OBJECTS = 32  # objects per GPU per step in the benchmarked workload
 SEED = 2
 WORKLOAD = "llama3_8b_kv_chunk_32MiB_x32_seal_then_open"
 
@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling runs)")
+    ap.add_argument("--objects", type=int, default=OBJECTS, help="objects per GPU per step (profiling runs)")
     ap.add_argument("--cpu-sample-objects", type=int, default=0,
                     help="objects per OpenSSL thread in the cpu_baseline sample (0 = auto)")
     return ap.parse_args()
@@ -158,25 +160,26 @@ def run_ours(args, rank, world, local):
     frame_len = P + 29
     stride = (frame_len + 255) // 256 * 256
     key_bytes = workloads.make_key(SEED)
-    ivs = workloads.make_ivs(SEED * 100 + rank, OBJECTS)
+    nobj = args.objects
+    ivs = workloads.make_ivs(SEED * 100 + rank, nobj)
     key = GpuAes128GcmKey(lib, key_bytes, device=local)
     key.reserve(P)
 
-    plain = workloads.bf16_batch(SHAPE, OBJECTS, seed=SEED * 100 + rank, device=dev)  # [32, ...] bf16
-    plain_u8 = plain.view(torch.uint8).reshape(OBJECTS, P)
-    frames = torch.empty((OBJECTS, stride), dtype=torch.uint8, device=dev)
-    opened = torch.empty((OBJECTS, P), dtype=torch.uint8, device=dev)
-    auth = torch.zeros((OBJECTS,), dtype=torch.int32, device=dev)
+    plain = workloads.bf16_batch(SHAPE, nobj, seed=SEED * 100 + rank, device=dev)  # [n, ...] bf16
+    plain_u8 = plain.view(torch.uint8).reshape(nobj, P)
+    frames = torch.empty((nobj, stride), dtype=torch.uint8, device=dev)
+    opened = torch.empty((nobj, P), dtype=torch.uint8, device=dev)
+    auth = torch.zeros((nobj,), dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)
     sp = stream.cuda_stream
 
     def seal_all():
-        for k in range(OBJECTS):
+        for k in range(nobj):
             key.seal_async(src_ptr=plain_u8[k].data_ptr(), plaintext_len=P, dst_ptr=frames[k].data_ptr(),
                            dst_capacity=stride, iv=ivs[k], stream_ptr=sp)
 
     def open_all():
-        for k in range(OBJECTS):
+        for k in range(nobj):
             key.open_async(src_ptr=frames[k].data_ptr(), frame_len=frame_len, dst_ptr=opened[k].data_ptr(),
                            plaintext_len=P, auth_ok_ptr=auth[k:k + 1].data_ptr(), stream_ptr=sp)
 
@@ -212,7 +215,8 @@ def run_ours(args, rank, world, local):
 
     # e2e through the public API: pinned host plaintext -> H2D -> seal -> D2H
     # frames, then open -> D2H auth flags; copies overlapped across objects.
-    e2e = run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args)
+    e2e = {"ms": float("nan"), "gbs": float("nan"), "h2d": 0, "d2h": 0} if args.no_e2e else \
+        run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args)
 
     t = torch.tensor([total_ms, sum(seal_ms), sum(open_ms), e2e["ms"], float(ok)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -228,15 +232,15 @@ def run_ours(args, rank, world, local):
         seal_sum, open_sum, e2e_ms = sum(seal_ms), sum(open_ms), e2e["ms"]
 
     if rank == 0:
-        bytes_per_step = 2 * OBJECTS * P * world  # sealed + opened plaintext, all ranks
+        bytes_per_step = 2 * nobj * P * world  # sealed + opened plaintext, all ranks
         ms_per_step = total_ms / args.steps
         value = bytes_per_step / (ms_per_step * 1e-3) / 1e9
-        seal_gbs = OBJECTS * P * world / (seal_sum / args.steps * 1e-3) / 1e9
-        open_gbs = OBJECTS * P * world / (open_sum / args.steps * 1e-3) / 1e9
+        seal_gbs = nobj * P * world / (seal_sum / args.steps * 1e-3) / 1e9
+        open_gbs = nobj * P * world / (open_sum / args.steps * 1e-3) / 1e9
         peak, peak_kind = load_peaks()
         # dominant kernel: seal_kernel, one launch per object; algorithmic
         # bytes = read P + write P + 29.
-        seal_launch_ms = seal_sum / args.steps / OBJECTS
+        seal_launch_ms = seal_sum / args.steps / nobj
         achieved = (2 * P + 29) / (seal_launch_ms * 1e-3) / 1e9
         traffic = profile_traffic("seal_kernel_kv_llama8b.txt")
         line = {
@@ -252,7 +256,7 @@ def run_ours(args, rank, world, local):
             "vs_baseline": None,
             "dtype": "u8",
             "data": "synthetic: bf16 N(0,1) KV chunks from fixed seeds, resident in HBM",
-            "config": {"workload": WORKLOAD, "objects_per_gpu": OBJECTS, "object_shape": list(SHAPE),
+            "config": {"workload": WORKLOAD, "objects_per_gpu": nobj, "object_shape": list(SHAPE),
                        "object_bytes": P, "step": "seal 32 objects then open 32 frames with tag check",
                        "l2": "inputs larger than L2 (1 GiB plaintext per GPU)",
                        "parallelism": f"independent objects per GPU x{world}, no collective"},
@@ -265,11 +269,11 @@ def run_ours(args, rank, world, local):
                          "algorithmic_bytes_per_launch": 2 * P + 29,
                          "traffic": traffic},
             "e2e": {"value": round(e2e["gbs"] * world, 2) if world == 1 else
-                    round(2 * OBJECTS * P * world / (e2e_ms * 1e-3) / 1e9, 2),
+                    round(2 * nobj * P * world / (e2e_ms * 1e-3) / 1e9, 2),
                     "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                     "what": "pinned host plaintext -> H2D -> seal -> D2H frames; open -> D2H auth; "
                             "copies overlapped across objects on three streams"},
-            "gpu_launches": 3 * OBJECTS * args.steps,
+            "gpu_launches": 3 * nobj * args.steps,
             "clocks": clk,
         }
         if not args.no_cpu_baseline and world == 1:

@@ -27,11 +27,13 @@ namespace dev {
 // ------------------------------------------------------------ seal kernel
 //
 // CTA c owns blocks [n - (G-c)*J*T, n - (G-1-c)*J*T) (only CTA 0 may start
-// below block 0; those leading slots are skipped). In iteration it thread t
-// handles block base + it*T + t, so a warp touches 512 contiguous bytes.
-// Thread t's GHASH chain is Q_t = sum_it C * H^(T*(J-1-it)); the CTA's share
-// of the tag hash is (sum_t Q_t H^(T-1-t)) * H^(d_c), d_c = n + 2 - e_c, where
-// the power warp computes H^(d_c) while the other warps run the main loop.
+// below block 0; those leading slots are skipped). Row r of a CTA is blocks
+// base + r*T + t, t = thread, so a warp touches 512 contiguous bytes per row.
+// Each thread keeps kSealChains GHASH chains (rows r = k mod R, multiplier
+// H^(R*T)) and combines them into Q_t = sum_r C_r H^(T*(J-1-r)); the CTA's
+// share of GHASH is (sum_t Q_t H^(T-1-t)) * H^(d_c), d_c = n + 2 - e_c. The
+// power warp computes H^(d_c), E_K(J0) and L*H while the other warps run the
+// main loop; the last CTA to finish writes the tag.
 //
 // SQ selects the ciphertext store: 4 = ciphertext pointer 16-B aligned;
 // 0..3 = word part of the funnel that builds an aligned 16-B chunk from this
@@ -40,17 +42,15 @@ template <int SQ, bool PT_ALIGNED>
 __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem[];
-    uint8_t* aes_tab = smem + kSealAes;
-    uint8_t* gh_tab = smem + kSealGh;
     uint4* part = reinterpret_cast<uint4*>(smem + kSealPart);
-    uint32_t* misc = reinterpret_cast<uint32_t*>(smem + kSealMisc);
+    constexpr int R = kSealChains;
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
 
-    fill_aes_smem(aes_tab, a.kt.aes_t);
-    fill_gh_smem(gh_tab, a.kt.gh_main);
+    fill_aes_smem(smem + kSealAes, a.kt.aes_t);
+    fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
     if (blockIdx.x == 0 && tid == 0) {
         a.frame[0] = 1;
         for (int b = 0; b < 12; ++b) {
@@ -65,90 +65,113 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
     const int64_t base = n - static_cast<int64_t>(a.grid - blockIdx.x) * span;
     uint8_t* ct = a.frame + 13;
 
-    unsigned long long uhi = 0, ulo = 0;  // power warp: U_p = M * x^(4p)
-    uint4 q = make_uint4(0, 0, 0, 0);
+    unsigned long long uhi = 0, ulo = 0;  // power warp: U_p = H^(d_c) * x^(4p)
+    uint4 ej0 = make_uint4(0, 0, 0, 0);   // power warp: E_K(J0)
+    uint4 lh = make_uint4(0, 0, 0, 0);    // power warp: length block * H
 
     if (warp == kPowerWarp) {
+        uint32_t lb[4];
+        aes_lane_bases(lb, lane);
+        uint32_t w[4] = {a.ivw[0] ^ a.rk[0], a.ivw[1] ^ a.rk[1], a.ivw[2] ^ a.rk[2], bswap32(1u) ^ a.rk[3]};
+        aes_rounds_smem<kSealAes>(w, a.rk, lb);
+        ej0 = make_uint4(w[0], w[1], w[2], w[3]);
+        lh = warp_gh_mul_global(be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull), a.kt.gh_pow2, lane);
         const unsigned long long d = static_cast<unsigned long long>(a.grid - 1 - blockIdx.x) *
                                          static_cast<unsigned long long>(span) + 2ull;
-        const uint4 m = warp_h_pow(a.kt.gh_pow2, d, lane);
-        warp_lane_basis(m, lane, uhi, ulo);
+        warp_lane_basis(warp_h_pow(a.kt.gh_pow2, d, lane), lane, uhi, ulo);
     } else {
         uint32_t lb[4];
         aes_lane_bases(lb, lane);
         const uint32_t lb_lo = static_cast<uint32_t>(lane & 7) << 4;
         const uint32_t lb_hi = 0x80u | lb_lo;
-        const uint32_t w0 = a.ivw[0] ^ a.rk[0];
-        const uint32_t w1 = a.ivw[1] ^ a.rk[1];
-        const uint32_t w2 = a.ivw[2] ^ a.rk[2];
+        const uint32_t s012[3] = {a.ivw[0] ^ a.rk[0], a.ivw[1] ^ a.rk[1], a.ivw[2] ^ a.rk[2]};
+        const uint32_t rk3x = bswap32(a.rk[3]);
         const uint32_t fsel = funnel_sel(a.store_r);
         const uint32_t s = (SQ < 4) ? 4u * SQ + a.store_r : 16u;  // 16 - (ct & 15)
-
-#pragma unroll 1
-        for (uint32_t it = 0; it < a.iters; ++it) {
-            const int64_t i = base + static_cast<int64_t>(it) * kHornerThreads + tid;
-            const bool valid = i >= 0;
-            const uint64_t off = static_cast<uint64_t>(i) * 16u;
-            uint4 c = make_uint4(0, 0, 0, 0);
-            int nbytes = 0;
-            if (valid) {
-                const uint64_t rem = P - off;
-                nbytes = rem >= 16 ? 16 : static_cast<int>(rem);
-                uint4 p;
-                if (PT_ALIGNED && nbytes == 16) {
-                    p = __ldg(reinterpret_cast<const uint4*>(a.src + off));
-                } else {
-                    p = load_bytes(a.src + off, nbytes);
-                }
-                uint32_t w[4] = {w0, w1, w2, bswap32(static_cast<uint32_t>(i) + 2u) ^ a.rk[3]};
-                aes_rounds_smem(w, a.rk, aes_tab, lb);
-                c = mask_bytes(make_uint4(p.x ^ w[0], p.y ^ w[1], p.z ^ w[2], p.w ^ w[3]), nbytes);
-            }
-
-            if (SQ == 4) {
-                if (valid) {
-                    if (nbytes == 16) {
-                        *reinterpret_cast<uint4*>(ct + off) = c;
-                    } else {
-                        store_bytes(ct + off, c, 0, nbytes);
-                    }
-                }
-            } else {
-                // next lane's block words 0..SQ
-                uint32_t nb[4];
+        const int64_t rows = a.iters;
+        constexpr int64_t T = kHornerThreads;
+        constexpr uint64_t kRowBytes = static_cast<uint64_t>(T) * 16u;
+        Chains<R> ch;
 #pragma unroll
-                for (int k = 0; k <= SQ; ++k) {
-                    nb[k] = __shfl_down_sync(0xffffffffu, word_of(c, k), 1);
-                }
-                const bool full = valid && lane < 31 && off + s + 16 <= P;
-                const bool prev_full = valid && lane > 0 && i >= 1 && off + s <= P;
-                if (full) {
-                    const uint32_t sw[8] = {c.x, c.y, c.z, c.w, nb[0], SQ >= 1 ? nb[1] : 0u,
-                                            SQ >= 2 ? nb[2] : 0u, SQ >= 3 ? nb[3] : 0u};
-                    uint4 o;
-                    o.x = funnel(sw[SQ + 0], sw[SQ + 1], fsel);
-                    o.y = funnel(sw[SQ + 1], sw[SQ + 2], fsel);
-                    o.z = funnel(sw[SQ + 2], sw[SQ + 3], fsel);
-                    o.w = funnel(sw[SQ + 3], sw[SQ + 4], fsel);
-                    *reinterpret_cast<uint4*>(ct + off + s) = o;
-                } else if (valid) {
-                    store_bytes(ct + off, c, static_cast<int>(s), nbytes);
-                }
-                if (valid && !prev_full) {
-                    store_bytes(ct + off, c, 0, nbytes < static_cast<int>(s) ? nbytes : static_cast<int>(s));
-                }
-            }
-
-            if (valid) {
-                q = xor4(gh_mul_rep(q, gh_tab, lb_lo, lb_hi), c);
-            }
+        for (int k = 0; k < R; ++k) {
+            ch.q[k] = make_uint4(0, 0, 0, 0);
         }
-        part[tid] = q;
+
+        // Rows [r_a, r_a + R*ngroups) hold only full blocks inside the object
+        // and start at a multiple of R: they run the check-free loop below.
+        // The others (CTA 0's leading padding, the row with the last partial
+        // block, leftovers) take generic_row. Rows are visited in order.
+        const int64_t n_full = static_cast<int64_t>(P / 16u);
+        const int64_t r_lo = base >= 0 ? 0 : (-base + T - 1) / T;
+        int64_t r_hi = (n_full - base) / T;
+        r_hi = r_hi > rows ? rows : r_hi;
+        int64_t r_a = (r_lo + R - 1) / R * R;
+        r_a = r_a > r_hi ? r_hi : r_a;
+        const int64_t ngroups = r_hi > r_a ? (r_hi - r_a) / R : 0;
+
+        auto generic_row = [&](int64_t r) __attribute__((always_inline)) {
+            const int64_t i = base + r * T + tid;
+            const int nb = block_bytes(i, P);
+            const uint4 p = load_pt_block<PT_ALIGNED>(a.src, i, P);
+            uint32_t x[4] = {s012[0], s012[1], s012[2], bswap32(static_cast<uint32_t>(i) + 2u) ^ a.rk[3]};
+            aes_rounds_smem<kSealAes>(x, a.rk, lb);
+            const uint4 c = mask_bytes(make_uint4(p.x ^ x[0], p.y ^ x[1], p.z ^ x[2], p.w ^ x[3]), nb);
+            store_ct_block<SQ>(ct, i, c, nb, P, s, fsel, lane);
+            chain_push_dyn<kSealGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
+        };
+
+        int64_t r = 0;
+#pragma unroll 1
+        for (; r < r_a; ++r) {
+            generic_row(r);
+        }
+        if (ngroups > 0) {
+            // Two rows per iteration: two AES chains (rounds 1-2 from the
+            // counter cache), two independent GHASH chains, next pair's
+            // plaintext prefetched.
+            const uint64_t i0 = static_cast<uint64_t>(base + r_a * T + tid);
+            const uint8_t* sp = a.src + i0 * 16u;
+            uint8_t* cp = ct + i0 * 16u;
+            uint32_t ctr = static_cast<uint32_t>(i0) + 2u;
+            CtrCache cc{0xffffffffu, 0u, {0u, 0u, 0u, 0u}};
+            uint4 pf0 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(sp)) : load_bytes(sp, 16);
+            uint4 pf1 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(sp + kRowBytes)) : load_bytes(sp + kRowBytes, 16);
+#pragma unroll 1
+            for (int64_t g = 0; g < ngroups; ++g) {
+                const uint4 p0 = pf0;
+                const uint4 p1 = pf1;
+                if (g + 1 < ngroups) {
+                    const uint8_t* nx = sp + 2 * kRowBytes;
+                    pf0 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(nx)) : load_bytes(nx, 16);
+                    pf1 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(nx + kRowBytes)) : load_bytes(nx + kRowBytes, 16);
+                }
+                const uint4 m0 = gh_mul_rep<kSealGh>(ch.q[0], lb_lo, lb_hi);
+                const uint4 m1 = gh_mul_rep<kSealGh>(ch.q[1], lb_lo, lb_hi);
+                uint32_t x[4], y[4];
+                aes_ctr2_cached<kSealAes>(x, y, ctr, ctr + static_cast<uint32_t>(T), cc, s012, rk3x, a.rk, lb);
+                const uint4 c0 = make_uint4(p0.x ^ x[0], p0.y ^ x[1], p0.z ^ x[2], p0.w ^ x[3]);
+                const uint4 c1 = make_uint4(p1.x ^ y[0], p1.y ^ y[1], p1.z ^ y[2], p1.w ^ y[3]);
+                store_ct_interior<SQ>(cp, c0, s, fsel, lane);
+                store_ct_interior<SQ>(cp + kRowBytes, c1, s, fsel, lane);
+                ch.q[0] = xor4(m0, c0);
+                ch.q[1] = xor4(m1, c1);
+                sp += 2 * kRowBytes;
+                cp += 2 * kRowBytes;
+                ctr += 2u * static_cast<uint32_t>(T);
+            }
+            r = r_a + R * ngroups;
+        }
+#pragma unroll 1
+        for (; r < rows; ++r) {
+            generic_row(r);
+        }
+        part[tid] = chains_combine<R>(ch, rows, a.kt.gh_pow2 + kHornerLog2 * 512);
     }
     __syncthreads();
 
-    // Stage the fold tables H^(2^l), l < kFoldLevels, over the GHASH region.
-    uint4* fold_tabs = reinterpret_cast<uint4*>(gh_tab);
+    // Stage the fold tables H^(2^l), l < kFoldLevels, over the AES region
+    // (E_K(J0) was computed by the power warp before the main loop).
+    uint4* fold_tabs = reinterpret_cast<uint4*>(smem + kSealAes);
     for (int i = tid; i < kFoldLevels * 512; i += blockDim.x) {
         fold_tabs[i] = __ldg(a.kt.gh_pow2 + i);
     }
@@ -156,45 +179,14 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
     fold_partials(part, fold_tabs);
 
     if (warp == kPowerWarp) {
-        unsigned long long rhi, rlo;
-        warp_generic_mul(part[0], uhi, ulo, lane, rhi, rlo);
-        unsigned int ticket = 0;
-        if (lane == 0) {
-            atomicXor(&a.slot->acc_hi, rhi);
-            atomicXor(&a.slot->acc_lo, rlo);
-            __threadfence();
-            ticket = atomicAdd(&a.slot->ticket, 1u);
-        }
-        ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        if (ticket == a.grid - 1) {
-            __threadfence();
-            unsigned long long shi = 0, slo = 0;
-            if (lane == 0) {
-                shi = atomicXor(&a.slot->acc_hi, 0ull);
-                slo = atomicXor(&a.slot->acc_lo, 0ull);
-            }
-            shi = __shfl_sync(0xffffffffu, shi, 0);
-            slo = __shfl_sync(0xffffffffu, slo, 0);
-            // length block [0^64 || 8P] times H
-            const uint4 lenblk = be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull);
-            const uint4 lh = warp_gh_mul_global(lenblk, a.kt.gh_pow2, lane);
-            uint32_t lb[4];
-            aes_lane_bases(lb, lane);
-            uint32_t w[4] = {a.ivw[0] ^ a.rk[0], a.ivw[1] ^ a.rk[1], a.ivw[2] ^ a.rk[2],
-                             bswap32(1u) ^ a.rk[3]};
-            aes_rounds_smem(w, a.rk, aes_tab, lb);
-            const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), make_uint4(w[0], w[1], w[2], w[3]));
+        unsigned long long shi, slo;
+        if (cta_accumulate(a.slot, part[0], uhi, ulo, lane, a.grid, shi, slo)) {
+            const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
             if (lane < 16) {
                 ct[P + lane] = static_cast<uint8_t>(byte_of(tag, lane));
             }
-            if (lane == 0) {
-                a.slot->acc_hi = 0;
-                a.slot->acc_lo = 0;
-                a.slot->ticket = 0;
-            }
         }
     }
-    (void)misc;
 }
 
 // Zero-length seal: header + tag = E_K(J0) (GHASH of nothing is 0).
@@ -215,46 +207,23 @@ __global__ void seal_empty_kernel(const SealArgs a)
 
 // ---------------------------------------------------- open: GHASH + verify
 //
-// Same CTA/thread partition and fold as seal_kernel, over the ciphertext at
-// frame + 13. LQ = word part of the load funnel (byte part a.load_r), 4 when
-// the ciphertext is 16-B aligned. Each lane reads the two aligned 16-B chunks
-// covering its block when both lie inside the frame buffer, else bytes.
-template <int LQ>
-__device__ __forceinline__ uint4 load_ct_block(const uint8_t* frame, uint64_t frame_len,
-                                               uint64_t off, int nbytes, uint32_t fsel)
-{
-    const uint8_t* ct = frame + 13;
-    if (nbytes == 16) {
-        if (LQ == 4) {
-            return *reinterpret_cast<const uint4*>(ct + off);
-        }
-        const uint64_t lag = 4u * LQ + 0u;  // word part; byte part folded into fsel
-        (void)lag;
-        const uint8_t* c0 = reinterpret_cast<const uint8_t*>(
-            reinterpret_cast<uintptr_t>(ct + off) & ~static_cast<uintptr_t>(15));
-        if (c0 >= frame && c0 + 32 <= frame + frame_len) {
-            const uint4 d = *reinterpret_cast<const uint4*>(c0);
-            const uint4 e = *reinterpret_cast<const uint4*>(c0 + 16);
-            const uint32_t sw[8] = {d.x, d.y, d.z, d.w, e.x, e.y, e.z, e.w};
-            return make_uint4(funnel(sw[LQ], sw[LQ + 1], fsel), funnel(sw[LQ + 1], sw[LQ + 2], fsel),
-                              funnel(sw[LQ + 2], sw[LQ + 3], fsel), funnel(sw[LQ + 3], sw[LQ + 4], fsel));
-        }
-    }
-    return load_bytes(ct + off, nbytes);
-}
-
+// Same CTA/row partition and fold as seal_kernel over the ciphertext at
+// frame + 13, with kOpenChains chains per thread and four rows per iteration
+// (next four prefetched). The power warp computes E_K(J0) and L*H up front;
+// the last CTA compares the expected tag with the frame's (16 bytes,
+// OR-accumulated) and checks the version byte, then writes *auth_ok.
 template <int LQ>
 __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem[];
-    uint8_t* gh_tab = smem + kOpenGh;
     uint4* part = reinterpret_cast<uint4*>(smem + kOpenPart);
+    constexpr int R = kOpenChains;
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
 
-    fill_gh_smem(gh_tab, a.kt.gh_main);
+    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
     __syncthreads();
 
     const uint64_t P = a.plen;
@@ -263,33 +232,96 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     const int64_t base = n - static_cast<int64_t>(a.grid - blockIdx.x) * span;
 
     unsigned long long uhi = 0, ulo = 0;
-    uint4 q = make_uint4(0, 0, 0, 0);
+    uint4 ej0 = make_uint4(0, 0, 0, 0);
+    uint4 lh = make_uint4(0, 0, 0, 0);
 
     if (warp == kPowerWarp) {
+        const uint4 iv = load_bytes(a.frame + 1, 12);
+        ej0 = aes_encrypt_gmem(a.kt.aes_t, a.rk, make_uint4(iv.x, iv.y, iv.z, bswap32(1u)));
+        lh = warp_gh_mul_global(be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull), a.kt.gh_pow2, lane);
         const unsigned long long d = static_cast<unsigned long long>(a.grid - 1 - blockIdx.x) *
                                          static_cast<unsigned long long>(span) + 2ull;
-        const uint4 m = warp_h_pow(a.kt.gh_pow2, d, lane);
-        warp_lane_basis(m, lane, uhi, ulo);
+        warp_lane_basis(warp_h_pow(a.kt.gh_pow2, d, lane), lane, uhi, ulo);
     } else {
         const uint32_t lb_lo = static_cast<uint32_t>(lane & 7) << 4;
         const uint32_t lb_hi = 0x80u | lb_lo;
         const uint32_t fsel = funnel_sel(a.load_r);
-#pragma unroll 1
-        for (uint32_t it = 0; it < a.iters; ++it) {
-            const int64_t i = base + static_cast<int64_t>(it) * kHornerThreads + tid;
-            if (i >= 0) {
-                const uint64_t off = static_cast<uint64_t>(i) * 16u;
-                const uint64_t rem = P - off;
-                const int nbytes = rem >= 16 ? 16 : static_cast<int>(rem);
-                const uint4 c = load_ct_block<LQ>(a.frame, a.frame_len, off, nbytes, fsel);
-                q = xor4(gh_mul_rep(q, gh_tab, lb_lo, lb_hi), c);
-            }
+        const int64_t rows = a.iters;
+        constexpr int64_t T = kHornerThreads;
+        constexpr uint64_t kRowBytes = static_cast<uint64_t>(T) * 16u;
+        Chains<R> ch;
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            ch.q[k] = make_uint4(0, 0, 0, 0);
         }
-        part[tid] = q;
+
+        // Interior rows: blocks 1 <= i < P/16, so both aligned chunks of every
+        // block lie inside the frame and no checks are needed.
+        const int64_t n_full = static_cast<int64_t>(P / 16u);
+        const int64_t r_lo = base >= 1 ? 0 : (1 - base + T - 1) / T;
+        int64_t r_hi = (n_full - base) / T;
+        r_hi = r_hi > rows ? rows : r_hi;
+        int64_t r_a = (r_lo + R - 1) / R * R;
+        r_a = r_a > r_hi ? r_hi : r_a;
+        const int64_t ngroups = r_hi > r_a ? (r_hi - r_a) / R : 0;
+
+        auto generic_row = [&](int64_t r) __attribute__((always_inline)) {
+            const int64_t i = base + r * T + tid;
+            const uint4 c = ct_finish<LQ>(ct_prefetch<LQ>(a.frame, a.frame_len, i, P), a.frame, i, P, fsel);
+            chain_push_dyn<kOpenGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
+        };
+
+        int64_t r = 0;
+#pragma unroll 1
+        for (; r < r_a; ++r) {
+            generic_row(r);
+        }
+        if (ngroups > 0) {
+            const uint64_t i0 = static_cast<uint64_t>(base + r_a * T + tid);
+            const uint8_t* cp = a.frame + 13 + i0 * 16u;
+            if (LQ != 4) {
+                cp = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(cp) & ~static_cast<uintptr_t>(15));
+            }
+            uint4 pd[R], pe[R];
+#pragma unroll
+            for (int k = 0; k < R; ++k) {
+                pd[k] = *reinterpret_cast<const uint4*>(cp + k * kRowBytes);
+                pe[k] = LQ != 4 ? *reinterpret_cast<const uint4*>(cp + k * kRowBytes + 16) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll 1
+            for (int64_t g = 0; g < ngroups; ++g) {
+                uint4 cd[R], ce[R];
+#pragma unroll
+                for (int k = 0; k < R; ++k) {
+                    cd[k] = pd[k];
+                    ce[k] = pe[k];
+                }
+                if (g + 1 < ngroups) {
+                    const uint8_t* nx = cp + R * kRowBytes;
+#pragma unroll
+                    for (int k = 0; k < R; ++k) {
+                        pd[k] = *reinterpret_cast<const uint4*>(nx + k * kRowBytes);
+                        pe[k] = LQ != 4 ? *reinterpret_cast<const uint4*>(nx + k * kRowBytes + 16) : make_uint4(0, 0, 0, 0);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < R; ++k) {
+                    const CtRaw raw{cd[k], ce[k], true};
+                    ch.q[k] = xor4(gh_mul_rep<kOpenGh>(ch.q[k], lb_lo, lb_hi), ct_finish<LQ>(raw, a.frame, 0, P, fsel));
+                }
+                cp += R * kRowBytes;
+            }
+            r = r_a + R * ngroups;
+        }
+#pragma unroll 1
+        for (; r < rows; ++r) {
+            generic_row(r);
+        }
+        part[tid] = chains_combine<R>(ch, rows, a.kt.gh_pow2 + kHornerLog2 * 512);
     }
     __syncthreads();
 
-    uint4* fold_tabs = reinterpret_cast<uint4*>(gh_tab);
+    uint4* fold_tabs = reinterpret_cast<uint4*>(smem + kOpenGh);
     for (int i = tid; i < kFoldLevels * 512; i += blockDim.x) {
         fold_tabs[i] = __ldg(a.kt.gh_pow2 + i);
     }
@@ -297,42 +329,15 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     fold_partials(part, fold_tabs);
 
     if (warp == kPowerWarp) {
-        unsigned long long rhi, rlo;
-        warp_generic_mul(part[0], uhi, ulo, lane, rhi, rlo);
-        unsigned int ticket = 0;
-        if (lane == 0) {
-            atomicXor(&a.slot->acc_hi, rhi);
-            atomicXor(&a.slot->acc_lo, rlo);
-            __threadfence();
-            ticket = atomicAdd(&a.slot->ticket, 1u);
-        }
-        ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        if (ticket == a.grid - 1) {
-            __threadfence();
-            unsigned long long shi = 0, slo = 0;
-            if (lane == 0) {
-                shi = atomicXor(&a.slot->acc_hi, 0ull);
-                slo = atomicXor(&a.slot->acc_lo, 0ull);
+        unsigned long long shi, slo;
+        if (cta_accumulate(a.slot, part[0], uhi, ulo, lane, a.grid, shi, slo) && lane == 0) {
+            const uint4 expect = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
+            const uint8_t* tag = a.frame + 13 + P;
+            uint32_t diff = 0;
+            for (int b = 0; b < 16; ++b) {
+                diff |= byte_of(expect, b) ^ static_cast<uint32_t>(tag[b]);
             }
-            shi = __shfl_sync(0xffffffffu, shi, 0);
-            slo = __shfl_sync(0xffffffffu, slo, 0);
-            const uint4 lenblk = be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull);
-            const uint4 lh = warp_gh_mul_global(lenblk, a.kt.gh_pow2, lane);
-            if (lane == 0) {
-                const uint4 iv = load_bytes(a.frame + 1, 12);
-                const uint4 e = aes_encrypt_gmem(a.kt.aes_t, a.rk, make_uint4(iv.x, iv.y, iv.z, bswap32(1u)));
-                const uint4 expect = xor4(xor4(be_to_raw(shi, slo), lh), e);
-                const uint8_t* tag = a.frame + 13 + P;
-                uint32_t diff = 0;
-                for (int b = 0; b < 16; ++b) {
-                    diff |= byte_of(expect, b) ^ static_cast<uint32_t>(tag[b]);
-                }
-                const int ok = (a.frame[0] == 1) & (diff == 0);
-                *a.auth_ok = ok;
-                a.slot->acc_hi = 0;
-                a.slot->acc_lo = 0;
-                a.slot->ticket = 0;
-            }
+            *a.auth_ok = (a.frame[0] == 1) & (diff == 0);
         }
     }
 }
@@ -362,53 +367,122 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_kernel(const CtrArgs 
 {
     extern __shared__ __align__(16) uint8_t smem[];
     const uint64_t P = a.plen;
-    const uint64_t n = a.nblocks;
-    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    const int64_t n = a.nblocks;
+    constexpr int64_t T = kCtrThreads;
+    constexpr uint64_t kRowBytes = static_cast<uint64_t>(T) * 16u;
+    const int tid = threadIdx.x;
+    // CTA c owns rows [c*R, (c+1)*R) of T blocks (block i = row*T + tid).
+    const int64_t row_begin = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta;
+    const int64_t rows_total = (n + T - 1) / T;
+    int64_t row_end = row_begin + a.rows_per_cta;
+    row_end = row_end > rows_total ? rows_total : row_end;
     const int ok = *reinterpret_cast<const volatile int*>(a.auth_ok);
 
     if (!ok) {
-        for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
-            const uint64_t off = i * 16u;
-            const uint64_t rem = P - off;
-            const int nbytes = rem >= 16 ? 16 : static_cast<int>(rem);
-            if (PT_ALIGNED && nbytes == 16) {
-                *reinterpret_cast<uint4*>(a.dst + off) = make_uint4(0, 0, 0, 0);
+        for (int64_t row = row_begin; row < row_end; ++row) {
+            const int64_t i = row * T + tid;
+            const int nb = block_bytes(i, P);
+            uint8_t* d = a.dst + static_cast<uint64_t>(i) * 16u;
+            if (PT_ALIGNED && nb == 16) {
+                *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
             } else {
-                for (int b = 0; b < nbytes; ++b) {
-                    a.dst[off + b] = 0;
+                for (int b = 0; b < nb; ++b) {
+                    d[b] = 0;
                 }
             }
         }
         return;
     }
 
-    uint8_t* aes_tab = smem;
-    fill_aes_smem(aes_tab, a.aes_t);
+    fill_aes_smem(smem, a.aes_t);
     __syncthreads();
 
-    const int lane = threadIdx.x & 31;
+    const int lane = tid & 31;
     uint32_t lb[4];
     aes_lane_bases(lb, lane);
     const uint4 iv = load_bytes(a.frame + 1, 12);
-    const uint32_t w0 = iv.x ^ a.rk[0];
-    const uint32_t w1 = iv.y ^ a.rk[1];
-    const uint32_t w2 = iv.z ^ a.rk[2];
+    const uint32_t s012[3] = {iv.x ^ a.rk[0], iv.y ^ a.rk[1], iv.z ^ a.rk[2]};
+    const uint32_t rk3x = bswap32(a.rk[3]);
     const uint32_t fsel = funnel_sel(a.load_r);
 
-#pragma unroll 1
-    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const uint64_t off = i * 16u;
-        const uint64_t rem = P - off;
-        const int nbytes = rem >= 16 ? 16 : static_cast<int>(rem);
-        const uint4 c = load_ct_block<LQ>(a.frame, a.frame_len, off, nbytes, fsel);
-        uint32_t w[4] = {w0, w1, w2, bswap32(static_cast<uint32_t>(i) + 2u) ^ a.rk[3]};
-        aes_rounds_smem(w, a.rk, aes_tab, lb);
-        const uint4 p = make_uint4(c.x ^ w[0], c.y ^ w[1], c.z ^ w[2], c.w ^ w[3]);
-        if (PT_ALIGNED && nbytes == 16) {
-            *reinterpret_cast<uint4*>(a.dst + off) = p;
-        } else {
-            store_bytes(a.dst + off, p, 0, nbytes);
+    auto store_pt = [&](int64_t i, uint4 p) __attribute__((always_inline)) {
+        const int nb = block_bytes(i, P);
+        uint8_t* d = a.dst + static_cast<uint64_t>(i) * 16u;
+        if (PT_ALIGNED && nb == 16) {
+            *reinterpret_cast<uint4*>(d) = p;
+        } else if (nb > 0) {
+            store_bytes(d, p, 0, nb);
         }
+    };
+    auto generic_row = [&](int64_t row) __attribute__((always_inline)) {
+        const int64_t i = row * T + tid;
+        const uint4 c = ct_finish<LQ>(ct_prefetch<LQ>(a.frame, a.frame_len, i, P), a.frame, i, P, fsel);
+        uint32_t x[4] = {s012[0], s012[1], s012[2], bswap32(static_cast<uint32_t>(i) + 2u) ^ a.rk[3]};
+        aes_rounds_smem<0>(x, a.rk, lb);
+        store_pt(i, make_uint4(c.x ^ x[0], c.y ^ x[1], c.z ^ x[2], c.w ^ x[3]));
+    };
+
+    // Interior rows: 1 <= row (block 0's chunk may start before the frame)
+    // and every block full.
+    const int64_t n_full = static_cast<int64_t>(P / 16u);
+    int64_t r_lo = row_begin < 1 ? 1 : row_begin;
+    int64_t r_hi = n_full / T;
+    r_hi = r_hi > row_end ? row_end : r_hi;
+    if (r_lo > r_hi) {
+        r_lo = r_hi = row_end;
+    }
+    int64_t row = row_begin;
+#pragma unroll 1
+    for (; row < r_lo; ++row) {
+        generic_row(row);
+    }
+    const int64_t npair = (r_hi - r_lo) / 2;
+    if (npair > 0) {
+        const uint64_t i0 = static_cast<uint64_t>(r_lo * T + tid);
+        const uint8_t* cp = a.frame + 13 + i0 * 16u;
+        if (LQ != 4) {
+            cp = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(cp) & ~static_cast<uintptr_t>(15));
+        }
+        uint8_t* dp = a.dst + i0 * 16u;
+        uint32_t ctr = static_cast<uint32_t>(i0) + 2u;
+        CtrCache cc{0xffffffffu, 0u, {0u, 0u, 0u, 0u}};
+        uint4 pd0 = *reinterpret_cast<const uint4*>(cp);
+        uint4 pe0 = LQ != 4 ? *reinterpret_cast<const uint4*>(cp + 16) : make_uint4(0, 0, 0, 0);
+        uint4 pd1 = *reinterpret_cast<const uint4*>(cp + kRowBytes);
+        uint4 pe1 = LQ != 4 ? *reinterpret_cast<const uint4*>(cp + kRowBytes + 16) : make_uint4(0, 0, 0, 0);
+#pragma unroll 1
+        for (int64_t k = 0; k < npair; ++k) {
+            const CtRaw r0{pd0, pe0, true};
+            const CtRaw r1{pd1, pe1, true};
+            if (k + 1 < npair) {
+                const uint8_t* nx = cp + 2 * kRowBytes;
+                pd0 = *reinterpret_cast<const uint4*>(nx);
+                pe0 = LQ != 4 ? *reinterpret_cast<const uint4*>(nx + 16) : make_uint4(0, 0, 0, 0);
+                pd1 = *reinterpret_cast<const uint4*>(nx + kRowBytes);
+                pe1 = LQ != 4 ? *reinterpret_cast<const uint4*>(nx + kRowBytes + 16) : make_uint4(0, 0, 0, 0);
+            }
+            uint32_t x[4], y[4];
+            aes_ctr2_cached<0>(x, y, ctr, ctr + static_cast<uint32_t>(T), cc, s012, rk3x, a.rk, lb);
+            const uint4 c0 = ct_finish<LQ>(r0, a.frame, 0, P, fsel);
+            const uint4 c1 = ct_finish<LQ>(r1, a.frame, 0, P, fsel);
+            const uint4 p0 = make_uint4(c0.x ^ x[0], c0.y ^ x[1], c0.z ^ x[2], c0.w ^ x[3]);
+            const uint4 p1 = make_uint4(c1.x ^ y[0], c1.y ^ y[1], c1.z ^ y[2], c1.w ^ y[3]);
+            if (PT_ALIGNED) {
+                *reinterpret_cast<uint4*>(dp) = p0;
+                *reinterpret_cast<uint4*>(dp + kRowBytes) = p1;
+            } else {
+                store_bytes(dp, p0, 0, 16);
+                store_bytes(dp + kRowBytes, p1, 0, 16);
+            }
+            cp += 2 * kRowBytes;
+            dp += 2 * kRowBytes;
+            ctr += 2u * static_cast<uint32_t>(T);
+        }
+        row = r_lo + 2 * npair;
+    }
+#pragma unroll 1
+    for (; row < row_end; ++row) {
+        generic_row(row);
     }
 }
 
@@ -524,6 +598,22 @@ cudaError_t configure_device(int device)
         chk(allow_smem(dev::open_ctr_kernel<2, false>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<3, false>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<4, false>, dev::kCtrSmem));
+        // The hot loops address shared memory as (offset + kDynSmemBase) with
+        // the base folded into the load instruction; check it on this device.
+        if (e == cudaSuccess) {
+            unsigned int* d = nullptr;
+            unsigned int base = 0;
+            chk(cudaMalloc(&d, sizeof(unsigned int)));
+            if (e == cudaSuccess) {
+                dev::smem_base_probe_kernel<<<1, 32, 1024>>>(d);
+                chk(cudaGetLastError());
+                chk(cudaMemcpy(&base, d, sizeof(base), cudaMemcpyDeviceToHost));
+                cudaFree(d);
+                if (e == cudaSuccess && base != dev::kDynSmemBase) {
+                    e = cudaErrorNotSupported;
+                }
+            }
+        }
         results[device] = e;
     });
     return results[device];
@@ -595,7 +685,11 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
     if (!guard.ok()) {
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
     }
-    if (configure_device(device) != cudaSuccess) {
+    const cudaError_t ce = configure_device(device);
+    if (ce == cudaErrorNotSupported) {
+        return LMCACHE_GPU_AESGCM_ERR_INTERNAL;  // unexpected shared-memory layout
+    }
+    if (ce != cudaSuccess) {
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
     }
 
@@ -619,8 +713,7 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
 
     constexpr size_t kAesT = 4 * 256 * sizeof(uint32_t);
     constexpr size_t kTab = confkv::kGhashTableBytes;
-    const size_t off_main = kAesT;
-    const size_t off_pow2 = off_main + kTab;
+    const size_t off_pow2 = kAesT;
     const size_t off_slots = off_pow2 + kTab * confkv::kPow2Tables;
     const size_t total = off_slots + sizeof(dev::Slot) * kSlots;
 
@@ -631,7 +724,6 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
     }
     std::memset(host, 0, total);
     confkv::aes_t_tables(reinterpret_cast<uint32_t(*)[256]>(host));
-    confkv::ghash_table(confkv::gf_pow(H, dev::kHornerThreads), host + off_main);
     Gf128 p = H;
     for (int k = 0; k < confkv::kPow2Tables; ++k) {
         confkv::ghash_table(p, host + off_pow2 + kTab * k);
@@ -651,7 +743,6 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
     }
     h->kt.aes_t = reinterpret_cast<const uint32_t*>(h->d_mem);
-    h->kt.gh_main = reinterpret_cast<const uint4*>(h->d_mem + off_main);
     h->kt.gh_pow2 = reinterpret_cast<const uint4*>(h->d_mem + off_pow2);
     h->slots = reinterpret_cast<dev::Slot*>(h->d_mem + off_slots);
     *out = reinterpret_cast<lmcache_gpu_aesgcm_key_t>(h);
@@ -820,8 +911,11 @@ extern "C" int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, co
     std::memcpy(ca.rk, h->rk, sizeof(ca.rk));
     ca.aes_t = h->kt.aes_t;
     ca.auth_ok = auth_ok;
-    const uint64_t want = (n + dev::kCtrThreads - 1) / dev::kCtrThreads;
-    const uint32_t grid = static_cast<uint32_t>(want < static_cast<uint64_t>(h->num_sms) ? want : h->num_sms);
+    const uint64_t rows_total = (n + dev::kCtrThreads - 1) / dev::kCtrThreads;
+    const uint64_t sms = static_cast<uint64_t>(h->num_sms);
+    const uint64_t rows_per_cta = (rows_total + sms - 1) / sms;
+    ca.rows_per_cta = static_cast<uint32_t>(rows_per_cta);
+    const uint32_t grid = static_cast<uint32_t>((rows_total + rows_per_cta - 1) / rows_per_cta);
     const bool pt_aligned = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
     if (pt_aligned) {
         switch (lq) {

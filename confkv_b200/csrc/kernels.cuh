@@ -13,8 +13,13 @@
 namespace confkv {
 namespace dev {
 
-constexpr int kHornerThreads = 256;                 // GHASH chains per CTA
-constexpr int kFoldLevels = 8;                      // log2(kHornerThreads)
+constexpr int kHornerThreads = 512;                 // threads running GHASH rows per CTA
+constexpr int kHornerLog2 = 9;                      // log2(kHornerThreads)
+constexpr int kFoldLevels = kHornerLog2;
+constexpr int kSealChains = 2;                      // GHASH chains per thread in seal
+constexpr int kSealChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * kHornerThreads)
+constexpr int kOpenChains = 2;                      // GHASH chains per thread in open
+constexpr int kOpenChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * kHornerThreads)
 constexpr int kPowerWarp = kHornerThreads / 32;     // warp index of the power warp
 constexpr int kSealThreads = kHornerThreads + 32;
 constexpr int kCtrThreads = 512;
@@ -30,6 +35,9 @@ constexpr uint32_t kAesBytes = 128u << 10;
 // phase hit 8 distinct bank groups.
 constexpr uint32_t kGhBytes = 64u << 10;
 constexpr uint32_t kPartBytes = kHornerThreads * 16;
+// After the main loop the fold tables H^(2^l), l < kFoldLevels (8 KiB each),
+// are staged over a table region that is no longer read.
+constexpr uint32_t kFoldBytes = kFoldLevels * 8192u;
 
 constexpr uint32_t kSealAes = 0;
 constexpr uint32_t kSealGh = kSealAes + kAesBytes;
@@ -38,11 +46,20 @@ constexpr uint32_t kSealMisc = kSealPart + kPartBytes;
 constexpr uint32_t kSealSmem = kSealMisc + 64;
 
 constexpr uint32_t kOpenGh = 0;
-constexpr uint32_t kOpenPart = kOpenGh + kGhBytes;
+constexpr uint32_t kOpenPart = kOpenGh + (kGhBytes > kFoldBytes ? kGhBytes : kFoldBytes);
 constexpr uint32_t kOpenMisc = kOpenPart + kPartBytes;
 constexpr uint32_t kOpenSmem = kOpenMisc + 64;
 
 constexpr uint32_t kCtrSmem = kAesBytes;
+static_assert(kFoldBytes <= kAesBytes, "seal stages the fold tables over the AES region");
+static_assert(kSealSmem <= 227u * 1024u, "seal shared memory exceeds the per-block limit");
+
+// Shared-window address at which dynamic shared memory starts for a kernel
+// without static shared memory on sm_100a (the first 1 KiB of each block's
+// window is reserved). Hot-loop table loads put this base in the LDS immediate
+// field so the PRMT-formed offset needs no add. configure_device() launches
+// smem_base_probe_kernel once per device and refuses to run if it differs.
+constexpr uint32_t kDynSmemBase = 0x400;
 
 // Per-call accumulation slot (32 bytes). The last CTA of a call resets it.
 struct Slot {
@@ -54,8 +71,7 @@ struct Slot {
 
 struct KeyTables {
     const uint32_t* aes_t;   // T0..T3, 4 x 256 words
-    const uint4* gh_main;    // compact 4-bit table for H^kHornerThreads (512 entries)
-    const uint4* gh_pow2;    // compact 4-bit tables for H^(2^k), k = 0..35
+    const uint4* gh_pow2;    // compact 4-bit tables (512 entries) for H^(2^k), k = 0..35
 };
 
 struct SealArgs {
@@ -93,6 +109,7 @@ struct CtrArgs {
     uint64_t plen;
     uint32_t nblocks;
     uint32_t load_r;
+    uint32_t rows_per_cta;  // rows of kCtrThreads blocks per CTA
     uint32_t rk[44];
     const uint32_t* aes_t;
     const int* auth_ok;
@@ -155,25 +172,55 @@ __device__ __forceinline__ void gf_mul_x(unsigned long long& hi, unsigned long l
 
 // ------------------------------------------------------------------ AES
 
-// One T-table lookup in the replicated shared-memory tables: index byte m of
-// w, table half/lane from lb (byte 0 and byte 2 of lb are passed through).
-__device__ __forceinline__ uint32_t tlook(const uint8_t* tab, uint32_t w, uint32_t lb, int m)
+// Shared loads at (dynamic-shared offset `off` + region offset BASE): the
+// constant part of the address rides in the instruction's immediate field.
+template <uint32_t BASE>
+__device__ __forceinline__ uint32_t lds32(uint32_t off)
 {
-    const uint32_t off = __byte_perm(w, lb, 0x7604u | (static_cast<uint32_t>(m) << 4));
-    return *reinterpret_cast<const uint32_t*>(tab + off);
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(off), "n"(kDynSmemBase + BASE));
+    return v;
 }
 
-// Encrypt state w (already xored with round key 0) with the shared tables.
-__device__ __forceinline__ void aes_rounds_smem(uint32_t w[4], const uint32_t* rk,
-                                                const uint8_t* tab, const uint32_t lb[4])
+template <uint32_t BASE>
+__device__ __forceinline__ uint4 lds128(uint32_t off)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+%5];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(off), "n"(kDynSmemBase + BASE));
+    return v;
+}
+
+__global__ void smem_base_probe_kernel(unsigned int* out)
+{
+    extern __shared__ __align__(16) uint8_t probe_smem[];
+    if (threadIdx.x == 0) {
+        out[0] = static_cast<unsigned int>(__cvta_generic_to_shared(probe_smem));
+    }
+}
+
+// One T-table lookup in the replicated shared-memory tables (region at
+// dynamic offset TAB): index byte m of w, table half/lane from lb (bytes 0
+// and 2 of lb pass through the PRMT).
+template <uint32_t TAB>
+__device__ __forceinline__ uint32_t tlook(uint32_t w, uint32_t lb, int m)
+{
+    return lds32<TAB>(__byte_perm(w, lb, 0x7604u | (static_cast<uint32_t>(m) << 4)));
+}
+
+// Rounds R0..10 of AES-128 on state w (the output of round R0-1) with the
+// shared tables at dynamic offset TAB.
+template <uint32_t TAB, int R0>
+__device__ __forceinline__ void aes_rounds_from(uint32_t w[4], const uint32_t* rk, const uint32_t lb[4])
 {
 #pragma unroll
-    for (int r = 1; r < 10; ++r) {
+    for (int r = R0; r < 10; ++r) {
         uint32_t n[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            n[c] = tlook(tab, w[c], lb[0], 0) ^ tlook(tab, w[(c + 1) & 3], lb[1], 1) ^
-                   tlook(tab, w[(c + 2) & 3], lb[2], 2) ^ tlook(tab, w[(c + 3) & 3], lb[3], 3) ^
+            n[c] = tlook<TAB>(w[c], lb[0], 0) ^ tlook<TAB>(w[(c + 1) & 3], lb[1], 1) ^
+                   tlook<TAB>(w[(c + 2) & 3], lb[2], 2) ^ tlook<TAB>(w[(c + 3) & 3], lb[3], 3) ^
                    rk[4 * r + c];
         }
 #pragma unroll
@@ -186,10 +233,10 @@ __device__ __forceinline__ void aes_rounds_smem(uint32_t w[4], const uint32_t* r
     for (int c = 0; c < 4; ++c) {
         // S-box bytes taken from the table whose entry holds S[x] at the
         // byte position of the output row: T2 row 0, T3 row 1, T0 row 2, T1 row 3.
-        const uint32_t e0 = tlook(tab, w[c], lb[2], 0);
-        const uint32_t e1 = tlook(tab, w[(c + 1) & 3], lb[3], 1);
-        const uint32_t e2 = tlook(tab, w[(c + 2) & 3], lb[0], 2);
-        const uint32_t e3 = tlook(tab, w[(c + 3) & 3], lb[1], 3);
+        const uint32_t e0 = tlook<TAB>(w[c], lb[2], 0);
+        const uint32_t e1 = tlook<TAB>(w[(c + 1) & 3], lb[3], 1);
+        const uint32_t e2 = tlook<TAB>(w[(c + 2) & 3], lb[0], 2);
+        const uint32_t e3 = tlook<TAB>(w[(c + 3) & 3], lb[1], 3);
         const uint32_t u = __byte_perm(e0, e1, 0x0050u);
         const uint32_t v = __byte_perm(e2, e3, 0x7200u);
         n[c] = __byte_perm(u, v, 0x7610u) ^ rk[40 + c];
@@ -197,6 +244,84 @@ __device__ __forceinline__ void aes_rounds_smem(uint32_t w[4], const uint32_t* r
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         w[c] = n[c];
+    }
+}
+
+// Full encryption of state w (already xored with round key 0).
+template <uint32_t TAB>
+__device__ __forceinline__ void aes_rounds_smem(uint32_t w[4], const uint32_t* rk, const uint32_t lb[4])
+{
+    aes_rounds_from<TAB, 1>(w, rk, lb);
+}
+
+// Counter-mode round caching. A thread's counters are c0 + 256*k (or + 512*k),
+// so counter byte 15 is fixed and bytes 12..13 change only on a carry out of
+// byte 14. Round 1 then has a single varying lookup (column 1, T2 of state
+// byte 14) and round 2 one varying lookup per column (all from column 1).
+// The cache holds the constant parts for the current value of ctr >> 16.
+struct CtrCache {
+    uint32_t epoch;  // ctr >> 16 the cache was built for
+    uint32_t k1;     // round-1 column 1 without T2[state byte 14]
+    uint32_t l[4];   // round-2 columns without their column-1 term
+};
+
+// s012 = IV words xor round key 0 (state columns 0..2 before round 1).
+template <uint32_t TAB>
+__device__ __forceinline__ void ctr_cache_build(CtrCache& cc, uint32_t ctr, const uint32_t s012[3],
+                                                const uint32_t* rk, const uint32_t lb[4])
+{
+    const uint32_t s0 = s012[0], s1 = s012[1], s2 = s012[2];
+    const uint32_t s3 = bswap32(ctr) ^ rk[3];
+    const uint32_t n0 = tlook<TAB>(s0, lb[0], 0) ^ tlook<TAB>(s1, lb[1], 1) ^ tlook<TAB>(s2, lb[2], 2) ^
+                        tlook<TAB>(s3, lb[3], 3) ^ rk[4];
+    const uint32_t n2 = tlook<TAB>(s2, lb[0], 0) ^ tlook<TAB>(s3, lb[1], 1) ^ tlook<TAB>(s0, lb[2], 2) ^
+                        tlook<TAB>(s1, lb[3], 3) ^ rk[6];
+    const uint32_t n3 = tlook<TAB>(s3, lb[0], 0) ^ tlook<TAB>(s0, lb[1], 1) ^ tlook<TAB>(s1, lb[2], 2) ^
+                        tlook<TAB>(s2, lb[3], 3) ^ rk[7];
+    cc.k1 = tlook<TAB>(s1, lb[0], 0) ^ tlook<TAB>(s2, lb[1], 1) ^ tlook<TAB>(s0, lb[3], 3) ^ rk[5];
+    cc.l[0] = tlook<TAB>(n0, lb[0], 0) ^ tlook<TAB>(n2, lb[2], 2) ^ tlook<TAB>(n3, lb[3], 3) ^ rk[8];
+    cc.l[1] = tlook<TAB>(n2, lb[1], 1) ^ tlook<TAB>(n3, lb[2], 2) ^ tlook<TAB>(n0, lb[3], 3) ^ rk[9];
+    cc.l[2] = tlook<TAB>(n2, lb[0], 0) ^ tlook<TAB>(n3, lb[1], 1) ^ tlook<TAB>(n0, lb[2], 2) ^ rk[10];
+    cc.l[3] = tlook<TAB>(n3, lb[0], 0) ^ tlook<TAB>(n0, lb[1], 1) ^ tlook<TAB>(n2, lb[3], 3) ^ rk[11];
+    cc.epoch = ctr >> 16;
+}
+
+// Rounds 1..2 of E_K(IV || BE32(ctr)) from the cache; rk3x = bswap32(rk[3]).
+template <uint32_t TAB>
+__device__ __forceinline__ void ctr_rounds12(uint32_t w[4], uint32_t ctr, const CtrCache& cc, uint32_t rk3x,
+                                             const uint32_t lb[4])
+{
+    // state byte 14 = counter byte 14 ^ key byte = byte 1 of (ctr ^ bswap(rk3))
+    const uint32_t n1 = cc.k1 ^ lds32<TAB>(__byte_perm(ctr ^ rk3x, lb[2], 0x7614u));
+    w[0] = cc.l[0] ^ tlook<TAB>(n1, lb[1], 1);
+    w[1] = cc.l[1] ^ tlook<TAB>(n1, lb[0], 0);
+    w[2] = cc.l[2] ^ tlook<TAB>(n1, lb[3], 3);
+    w[3] = cc.l[3] ^ tlook<TAB>(n1, lb[2], 2);
+}
+
+// Two keystream blocks for counters c0 < c1. Fast path (both in the cached
+// epoch): rounds 1-2 from the cache, rounds 3-10 of both blocks in one basic
+// block so their lookups interleave. Otherwise (first use, a carry into byte
+// 13, or counters of padding slots): full AES on both, cache rebuilt for c1.
+template <uint32_t TAB>
+__device__ __forceinline__ void aes_ctr2_cached(uint32_t x[4], uint32_t y[4], uint32_t c0, uint32_t c1,
+                                                CtrCache& cc, const uint32_t s012[3], uint32_t rk3x,
+                                                const uint32_t* rk, const uint32_t lb[4])
+{
+    if ((c0 >> 16) == cc.epoch && (c1 >> 16) == cc.epoch) {
+        ctr_rounds12<TAB>(x, c0, cc, rk3x, lb);
+        ctr_rounds12<TAB>(y, c1, cc, rk3x, lb);
+        aes_rounds_from<TAB, 3>(x, rk, lb);
+        aes_rounds_from<TAB, 3>(y, rk, lb);
+    } else {
+        x[0] = y[0] = s012[0];
+        x[1] = y[1] = s012[1];
+        x[2] = y[2] = s012[2];
+        x[3] = bswap32(c0) ^ rk[3];
+        y[3] = bswap32(c1) ^ rk[3];
+        aes_rounds_from<TAB, 1>(x, rk, lb);
+        aes_rounds_from<TAB, 1>(y, rk, lb);
+        ctr_cache_build<TAB>(cc, c1, s012, rk, lb);
     }
 }
 
@@ -264,8 +389,10 @@ __device__ __forceinline__ void fill_gh_smem(uint8_t* gh, const uint4* compact)
     }
 }
 
-// x * M using the replicated shared table of M (32 LDS.128, no bank conflicts).
-__device__ __forceinline__ uint4 gh_mul_rep(uint4 x, const uint8_t* gh, uint32_t lb_lo, uint32_t lb_hi)
+// x * M using the replicated shared table of M at dynamic offset GH
+// (32 LDS.128, no bank conflicts).
+template <uint32_t GH>
+__device__ __forceinline__ uint4 gh_mul_rep(uint4 x, uint32_t lb_lo, uint32_t lb_hi)
 {
     uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
 #pragma unroll
@@ -277,8 +404,8 @@ __device__ __forceinline__ uint4 gh_mul_rep(uint4 x, const uint8_t* gh, uint32_t
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const uint32_t sel = 0x7604u | (static_cast<uint32_t>(k) << 4);
-            const uint4 e = *reinterpret_cast<const uint4*>(gh + __byte_perm(lo, lb_lo, sel));
-            const uint4 f = *reinterpret_cast<const uint4*>(gh + __byte_perm(hi, lb_hi, sel));
+            const uint4 e = lds128<GH>(__byte_perm(lo, lb_lo, sel));
+            const uint4 f = lds128<GH>(__byte_perm(hi, lb_hi, sel));
             a0 ^= e.x ^ f.x;
             a1 ^= e.y ^ f.y;
             a2 ^= e.z ^ f.z;
@@ -297,6 +424,58 @@ __device__ __forceinline__ uint4 gh_mul_compact(uint4 x, const uint4* tab)
         const uint32_t b = byte_of(x, j);
         acc = xor4(acc, tab[(2 * j) * 16 + (b & 15u)]);
         acc = xor4(acc, tab[(2 * j + 1) * 16 + (b >> 4)]);
+    }
+    return acc;
+}
+
+// R independent GHASH Horner chains per thread: chain k takes the thread's
+// rows r = k (mod R) with multiplier M = H^(R*T), so the R multiplies of an
+// iteration do not wait on one another (only their final XOR waits for the
+// row's ciphertext).
+template <int R>
+struct Chains {
+    uint4 q[R];
+};
+
+// Push block c of row r into chain r mod R (k known only at run time).
+template <uint32_t GH, int R>
+__device__ __forceinline__ void chain_push_dyn(Chains<R>& ch, int k, uint4 c, uint32_t lb_lo, uint32_t lb_hi)
+{
+    uint4 v = ch.q[0];
+#pragma unroll
+    for (int j = 1; j < R; ++j) {
+        if (k == j) {
+            v = ch.q[j];
+        }
+    }
+    v = xor4(gh_mul_rep<GH>(v, lb_lo, lb_hi), c);
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+        if (k == j) {
+            ch.q[j] = v;
+        }
+    }
+}
+
+// The thread's share over its J rows, sum_r X_r H^(T (J-1-r)), from the R
+// chains: chain k's last row is J-1-((J-1-k) mod R), so
+//   Q = sum_k q_k H^(T ((J-1-k) mod R)),
+// evaluated by Horner with H^T (compact table ht, read through L1).
+template <int R>
+__device__ __forceinline__ uint4 chains_combine(const Chains<R>& ch, int64_t J, const uint4* ht)
+{
+    uint4 acc = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int d = R - 1; d >= 0; --d) {
+        const int k = static_cast<int>((((J - 1 - d) % R) + R) % R);
+        uint4 v = ch.q[0];
+#pragma unroll
+        for (int j = 1; j < R; ++j) {
+            if (k == j) {
+                v = ch.q[j];
+            }
+        }
+        acc = (d == R - 1) ? v : xor4(gh_mul_compact(acc, ht), v);
     }
     return acc;
 }
@@ -369,6 +548,41 @@ __device__ inline void warp_generic_mul(uint4 f_raw, unsigned long long uhi, uns
     rlo = alo;
 }
 
+// Power-warp epilogue of seal/open GHASH: scale the CTA's fold by H^(d_c)
+// (lane p holds U_p = H^(d_c) x^(4p)), XOR it into the call's slot and take
+// a ticket. Returns true in every lane of the last CTA to arrive, with the
+// full sum S (before the length block) in (shi, slo); that CTA also resets
+// the slot for the next call. No CTA waits on another.
+__device__ inline bool cta_accumulate(Slot* slot, uint4 fold, unsigned long long uhi, unsigned long long ulo,
+                                      int lane, uint32_t grid, unsigned long long& shi, unsigned long long& slo)
+{
+    unsigned long long rhi, rlo;
+    warp_generic_mul(fold, uhi, ulo, lane, rhi, rlo);
+    unsigned int ticket = 0;
+    if (lane == 0) {
+        atomicXor(&slot->acc_hi, rhi);
+        atomicXor(&slot->acc_lo, rlo);
+        __threadfence();
+        ticket = atomicAdd(&slot->ticket, 1u);
+    }
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket != grid - 1) {
+        return false;
+    }
+    __threadfence();
+    unsigned long long h = 0, l = 0;
+    if (lane == 0) {
+        h = atomicXor(&slot->acc_hi, 0ull);
+        l = atomicXor(&slot->acc_lo, 0ull);
+        slot->acc_hi = 0;
+        slot->acc_lo = 0;
+        slot->ticket = 0;
+    }
+    shi = __shfl_sync(0xffffffffu, h, 0);
+    slo = __shfl_sync(0xffffffffu, l, 0);
+    return true;
+}
+
 // Fold the kHornerThreads partials in shared memory: after level l the entry
 // at index p * 2^(l+1) holds left * H^(2^l) + right. fold_tabs are the compact
 // tables for H^(2^l), l = 0..kFoldLevels-1, staged in shared memory.
@@ -397,11 +611,20 @@ __device__ __forceinline__ void store_bytes(uint8_t* dst, uint4 v, int lo, int h
 
 __device__ __forceinline__ uint4 load_bytes(const uint8_t* src, int n)
 {
-    uint32_t w[4] = {0, 0, 0, 0};
+    uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
     for (int b = 0; b < n; ++b) {
-        w[b >> 2] |= static_cast<uint32_t>(src[b]) << (8 * (b & 3));
+        const uint32_t v = static_cast<uint32_t>(src[b]) << (8 * (b & 3));
+        if (b < 4) {
+            w0 |= v;
+        } else if (b < 8) {
+            w1 |= v;
+        } else if (b < 12) {
+            w2 |= v;
+        } else {
+            w3 |= v;
+        }
     }
-    return make_uint4(w[0], w[1], w[2], w[3]);
+    return make_uint4(w0, w1, w2, w3);
 }
 
 __device__ __forceinline__ uint4 mask_bytes(uint4 v, int n)
@@ -415,6 +638,192 @@ __device__ __forceinline__ uint4 mask_bytes(uint4 v, int n)
         w[k] &= m;
     }
     return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Bytes of block i of a P-byte object: 16 for i < P/16, the remainder for the
+// last partial block, 0 outside [0, n).
+__device__ __forceinline__ int block_bytes(int64_t i, uint64_t P)
+{
+    if (i < 0) {
+        return 0;
+    }
+    const uint64_t off = static_cast<uint64_t>(i) * 16u;
+    if (off >= P) {
+        return 0;
+    }
+    const uint64_t rem = P - off;
+    return rem >= 16 ? 16 : static_cast<int>(rem);
+}
+
+// Block i of a plaintext buffer (zero-padded; zero outside the object).
+template <bool ALIGNED>
+__device__ __forceinline__ uint4 load_pt_block(const uint8_t* src, int64_t i, uint64_t P)
+{
+    const int nb = block_bytes(i, P);
+    const uint8_t* p = src + static_cast<uint64_t>(i) * 16u;
+    if (ALIGNED && nb == 16) {
+        return __ldg(reinterpret_cast<const uint4*>(p));
+    }
+    if (nb == 0) {
+        return make_uint4(0, 0, 0, 0);
+    }
+    return load_bytes(p, nb);
+}
+
+// Block i of the ciphertext at frame + 13, in two steps. ct_prefetch issues the
+// loads: LQ = word part of (frame + 13) & 15 (4 = aligned); a lane reads the
+// two aligned 16-B chunks covering its block when both lie inside the frame
+// buffer. ct_finish applies the funnel (byte part in the PRMT selector fsel),
+// or falls back to byte loads for partial / edge blocks; zero outside the
+// object. Issuing the prefetch one iteration ahead hides the load latency.
+struct CtRaw {
+    uint4 d;
+    uint4 e;
+    bool fast;
+};
+
+template <int LQ>
+__device__ __forceinline__ CtRaw ct_prefetch(const uint8_t* frame, uint64_t frame_len, int64_t i, uint64_t P)
+{
+    CtRaw r{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), false};
+    if (block_bytes(i, P) == 16) {
+        const uint8_t* ct = frame + 13 + static_cast<uint64_t>(i) * 16u;
+        if (LQ == 4) {
+            r.d = *reinterpret_cast<const uint4*>(ct);
+            r.fast = true;
+        } else {
+            const uint8_t* c0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(ct) &
+                                                                 ~static_cast<uintptr_t>(15));
+            if (c0 >= frame && c0 + 32 <= frame + frame_len) {
+                r.d = *reinterpret_cast<const uint4*>(c0);
+                r.e = *reinterpret_cast<const uint4*>(c0 + 16);
+                r.fast = true;
+            }
+        }
+    }
+    return r;
+}
+
+template <int LQ>
+__device__ __forceinline__ uint4 ct_finish(const CtRaw& r, const uint8_t* frame, int64_t i, uint64_t P,
+                                           uint32_t fsel)
+{
+    if (r.fast) {
+        if (LQ == 4) {
+            return r.d;
+        }
+        const uint32_t sw[8] = {r.d.x, r.d.y, r.d.z, r.d.w, r.e.x, r.e.y, r.e.z, r.e.w};
+        constexpr int q = LQ & 3;
+        return make_uint4(funnel(sw[q], sw[q + 1], fsel), funnel(sw[q + 1], sw[q + 2], fsel),
+                          funnel(sw[q + 2], sw[q + 3], fsel), funnel(sw[q + 3], sw[q + 4], fsel));
+    }
+    const int nb = block_bytes(i, P);
+    if (nb == 0) {
+        return make_uint4(0, 0, 0, 0);
+    }
+    return load_bytes(frame + 13 + static_cast<uint64_t>(i) * 16u, nb);
+}
+
+// Store ciphertext block i (nb valid bytes, nb = 0 for no block) at
+// ct + 16 i. SQ = 4: ct is 16-B aligned. SQ = 0..3: ct is misaligned by
+// 16 - s (s = 4 SQ + r); lane l writes the aligned chunk at ct + 16 i + s,
+// built from its block and lane l+1's block (one shuffle per needed word),
+// when both are in this warp and the chunk lies inside [0, P); warp-edge and
+// object-edge bytes go out byte-wise. Every lane of the warp must call this.
+template <int SQ>
+__device__ __forceinline__ void store_ct_block(uint8_t* ct, int64_t i, uint4 c, int nb, uint64_t P,
+                                               uint32_t s, uint32_t fsel, int lane)
+{
+    const uint64_t off = static_cast<uint64_t>(i) * 16u;
+    if constexpr (SQ == 4) {
+        if (nb == 16) {
+            *reinterpret_cast<uint4*>(ct + off) = c;
+        } else if (nb > 0) {
+            store_bytes(ct + off, c, 0, nb);
+        }
+        return;
+    } else {
+    uint32_t nbw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        nbw[k] = k <= (SQ & 3) ? __shfl_down_sync(0xffffffffu, word_of(c, k), 1) : 0u;
+    }
+    const bool valid = nb > 0;
+    const bool full = valid && lane < 31 && off + s + 16 <= P;
+    const bool prev_full = valid && lane > 0 && i >= 1 && off + s <= P;
+    if (full) {
+        const uint32_t sw[8] = {c.x, c.y, c.z, c.w, nbw[0], nbw[1], nbw[2], nbw[3]};
+        uint4 o;
+        o.x = funnel(sw[(SQ & 3) + 0], sw[(SQ & 3) + 1], fsel);
+        o.y = funnel(sw[(SQ & 3) + 1], sw[(SQ & 3) + 2], fsel);
+        o.z = funnel(sw[(SQ & 3) + 2], sw[(SQ & 3) + 3], fsel);
+        o.w = funnel(sw[(SQ & 3) + 3], sw[(SQ & 3) + 4], fsel);
+        *reinterpret_cast<uint4*>(ct + off + s) = o;
+    } else if (valid) {
+        store_bytes(ct + off, c, static_cast<int>(s), nb);
+    }
+    if (valid && !prev_full) {
+        store_bytes(ct + off, c, 0, nb < static_cast<int>(s) ? nb : static_cast<int>(s));
+    }
+    }
+}
+
+// Bytes [0, n) of v to a 16-byte aligned destination, widest stores first.
+__device__ __forceinline__ void store_prefix_aligned(uint8_t* dst, uint4 v, uint32_t n)
+{
+    uint32_t k = 0;
+    if (n & 8u) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(v.x, v.y);
+        k = 8;
+    }
+    if (n & 4u) {
+        *reinterpret_cast<uint32_t*>(dst + k) = word_of(v, static_cast<int>(k >> 2));
+        k += 4;
+    }
+    if (n & 2u) {
+        const uint32_t w = word_of(v, static_cast<int>(k >> 2));
+        *reinterpret_cast<uint16_t*>(dst + k) = static_cast<uint16_t>(w >> (8 * (k & 3u)));
+        k += 2;
+    }
+    if (n & 1u) {
+        dst[k] = static_cast<uint8_t>(byte_of(v, static_cast<int>(k)));
+    }
+}
+
+// Store of ciphertext block i at ctp = ct + 16 i for a row whose 32 lanes all
+// hold full blocks inside the object. SQ = 4: ct aligned, one vector store.
+// Otherwise lanes 0..30 write the aligned chunk at ctp + s built from their
+// block and the next lane's; lane 31 writes the first 16 - s bytes of that
+// chunk (its block's tail; the next warp's lane 0 writes the rest) and lane 0
+// writes its block's first s bytes. No bounds checks: the caller guarantees
+// the row is interior. Every lane of the warp must call this.
+template <int SQ>
+__device__ __forceinline__ void store_ct_interior(uint8_t* ctp, uint4 c, uint32_t s, uint32_t fsel, int lane)
+{
+    if constexpr (SQ == 4) {
+        *reinterpret_cast<uint4*>(ctp) = c;
+    } else {
+        uint32_t nbw[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            nbw[k] = k <= (SQ & 3) ? __shfl_down_sync(0xffffffffu, word_of(c, k), 1) : 0u;
+        }
+        const uint32_t sw[8] = {c.x, c.y, c.z, c.w, nbw[0], nbw[1], nbw[2], nbw[3]};
+        constexpr int q = SQ & 3;
+        uint4 o;
+        o.x = funnel(sw[q + 0], sw[q + 1], fsel);
+        o.y = funnel(sw[q + 1], sw[q + 2], fsel);
+        o.z = funnel(sw[q + 2], sw[q + 3], fsel);
+        o.w = funnel(sw[q + 3], sw[q + 4], fsel);
+        if (lane < 31) {
+            *reinterpret_cast<uint4*>(ctp + s) = o;
+        } else {
+            store_prefix_aligned(ctp + s, o, 16u - s);
+        }
+        if (lane == 0) {
+            store_bytes(ctp, c, 0, static_cast<int>(s));
+        }
+    }
 }
 
 }  // namespace dev

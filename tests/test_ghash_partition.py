@@ -1,19 +1,22 @@
 """CPU model of the seal / open-GHASH kernels' partition of GHASH, checked
 against the oracle's serial GHASH (oracle_ghash_ct).
 
-The kernels split the n ciphertext blocks over G CTAs of J iterations x T
-threads (CTA c covers [n - (G-c)JT, n - (G-1-c)JT), leading slots below block 0
-skipped), run one Horner chain per thread with multiplier H^T, fold the T
-chains with H^(2^l), and scale each CTA's fold by H^(d_c), d_c = (G-1-c)JT + 2;
-the length block contributes L*H. This model mirrors horner_grid() in
-confkv_b200/csrc/gpu_aesgcm.cu and the algebra of seal_kernel/open_ghash_kernel.
+The kernels split the n ciphertext blocks over G CTAs of J rows x T threads
+(CTA c covers [n - (G-c)JT, n - (G-1-c)JT), leading slots below block 0
+skipped). Each thread runs R Horner chains (chain k takes its rows r = k mod R,
+multiplier H^(R*T)), combines them with H^T into sum_r X_r H^(T(J-1-r)), the T
+thread shares are folded with H^(2^l), and each CTA's fold is scaled by
+H^(d_c), d_c = (G-1-c)JT + 2; the length block contributes L*H. R = 2 in
+seal_kernel, 4 in open_ghash_kernel. This model mirrors horner_grid() in
+confkv_b200/csrc/gpu_aesgcm.cu and the algebra of chain_push_dyn /
+chains_combine / fold_partials / cta_accumulate in kernels.cuh.
 """
 
 import numpy as np
 import pytest
 
-T = 256
-FOLD_LEVELS = 8
+T = 512
+FOLD_LEVELS = 9
 ONE = b"\x80" + bytes(15)
 
 
@@ -28,7 +31,7 @@ def horner_grid(n: int, num_sms: int) -> tuple[int, int]:
     return j, -(-n // span)
 
 
-def model_ghash(oracle, h: bytes, ct: bytes, num_sms: int) -> bytes:
+def model_ghash(oracle, h: bytes, ct: bytes, num_sms: int, chains: int) -> bytes:
     mul = oracle.gf_mul
 
     def power(e: int) -> bytes:
@@ -47,17 +50,24 @@ def model_ghash(oracle, h: bytes, ct: bytes, num_sms: int) -> bytes:
     iters, grid = horner_grid(n, num_sms)
     span = iters * T
     ht = power(T)
+    hrt = power(chains * T)
     fold_pows = [power(1 << l) for l in range(FOLD_LEVELS)]
     acc = bytes(16)
     for c in range(grid):
         base = n - (grid - c) * span
-        q = [bytes(16)] * T
-        for it in range(iters):
+        q = [[bytes(16)] * chains for _ in range(T)]
+        for r in range(iters):
             for t in range(T):
-                i = base + it * T + t
-                if i >= 0:
-                    q[t] = xor(mul(q[t], ht), blocks[i])
-        part = list(q)
+                i = base + r * T + t
+                x = blocks[i] if i >= 0 else bytes(16)
+                q[t][r % chains] = xor(mul(q[t][r % chains], hrt), x)
+        part = []
+        for t in range(T):
+            share = bytes(16)
+            for d in range(chains - 1, -1, -1):
+                k = (iters - 1 - d) % chains
+                share = q[t][k] if d == chains - 1 else xor(mul(share, ht), q[t][k])
+            part.append(share)
         for l in range(FOLD_LEVELS):
             for p in range(T >> (l + 1)):
                 left = p << (l + 1)
@@ -68,13 +78,14 @@ def model_ghash(oracle, h: bytes, ct: bytes, num_sms: int) -> bytes:
     return xor(acc, mul(lenblk, h))
 
 
+@pytest.mark.parametrize("chains", [2])
 @pytest.mark.parametrize("size,num_sms", [(1, 148), (16, 148), (17, 4), (4096, 148), (16 * 700 + 5, 2),
-                                          (16 * 1024, 4), (16 * 1537 + 9, 3), (16 * 3000, 5)])
-def test_partitioned_ghash_matches_serial(oracle, size, num_sms):
+                                          (16 * 1024, 4), (16 * 1537 + 9, 3), (16 * 3000, 2)])
+def test_partitioned_ghash_matches_serial(oracle, size, num_sms, chains):
     rng = np.random.default_rng(size * 7 + num_sms)
     h = rng.bytes(16)
     ct = rng.bytes(size)
-    assert model_ghash(oracle, h, ct, num_sms) == oracle.ghash_ct(h, ct)
+    assert model_ghash(oracle, h, ct, num_sms, chains) == oracle.ghash_ct(h, ct)
 
 
 def test_grid_covers_blocks_once():
