@@ -937,6 +937,196 @@ extern "C" int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, co
     return cuda_rc(e);
 }
 
+// ===================================================== seal without allocation
+//
+// lmcache_gpu_aes128gcm_seal_noalloc serves callers that cannot call
+// cudaMalloc at the point where they seal: a KV-cache server that has handed
+// (nearly) all device memory to its own pool at start-up, or a pipeline
+// thread that must not hit cudaMalloc's implicit device synchronisation. It
+// takes the raw key instead of a handle and keeps everything the seal kernel
+// needs beyond its input and output -- the key's GHASH tables, the AES
+// T-tables and the call's accumulation slot -- in one file-scope __device__
+// array that every GPU loading this library holds until process exit.
+namespace {
+
+constexpr int kNoAllocPow2Tables = 28;  // H^(2^k), k < 28: exponents of objects up to 1 GiB
+constexpr size_t kNoAllocAesBytes = 4 * 256 * sizeof(uint32_t);
+constexpr size_t kNoAllocTableBytes =
+    kNoAllocAesBytes + static_cast<size_t>(kNoAllocPow2Tables) * confkv::kGhashTableBytes;
+constexpr size_t kNoAllocSlotOffset = (kNoAllocTableBytes + 255) / 256 * 256;
+constexpr size_t kNoAllocScratchBytes = kNoAllocSlotOffset + 256;
+constexpr uint64_t kNoAllocMaxPlaintext = 1ull << 30;
+
+static_assert(dev::kSealChainLog2 < kNoAllocPow2Tables, "chain multiplier table must be in the scratch");
+
+// The shared scratch array (228 KiB + 256 B per device).
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocDevice {
+    std::once_flag once;
+    int status = LMCACHE_GPU_AESGCM_OK;
+    uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    int num_sms = 0;
+    bool have_key = false;
+    uint8_t key[16] = {0};
+};
+
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+std::mutex g_noalloc_mu;                       // guards the staging buffer and key caches
+uint8_t g_noalloc_staging[kNoAllocTableBytes];  // host image of the scratch tables
+
+// Once per device, with that device current: resolve the array's device
+// address, opt the seal kernels into their shared memory and check the
+// shared-memory layout with the probe kernel writing into the array.
+int noalloc_setup(int device, NoAllocDevice& st)
+{
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&st.scratch), g_noalloc_scratch) != cudaSuccess ||
+        st.scratch == nullptr) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    if (cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+        st.num_sms <= 0) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    cudaError_t e = cudaSuccess;
+    auto chk = [&e](cudaError_t r) {
+        if (e == cudaSuccess) {
+            e = r;
+        }
+    };
+    chk(allow_smem(dev::seal_kernel<0, true>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<1, true>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<2, true>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<3, true>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<4, true>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<0, false>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<1, false>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<2, false>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<3, false>, dev::kSealSmem));
+    chk(allow_smem(dev::seal_kernel<4, false>, dev::kSealSmem));
+    if (e != cudaSuccess) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    unsigned int* probe = reinterpret_cast<unsigned int*>(st.scratch + kNoAllocSlotOffset + 128);
+    dev::smem_base_probe_kernel<<<1, 32, 1024>>>(probe);
+    unsigned int base = 0;
+    if (cudaGetLastError() != cudaSuccess ||
+        cudaMemcpy(&base, probe, sizeof(base), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    return base == dev::kDynSmemBase ? LMCACHE_GPU_AESGCM_OK : LMCACHE_GPU_AESGCM_ERR_INTERNAL;
+}
+
+}  // namespace
+
+extern "C" int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key_len, const void* src,
+                                                  size_t plaintext_len, void* dst, size_t dst_capacity,
+                                                  const uint8_t* iv, int device, void* stream_ptr)
+{
+    if (key == nullptr || key_len != 16 || src == nullptr || dst == nullptr || iv == nullptr) {
+        return LMCACHE_GPU_AESGCM_ERR_ARGUMENT;
+    }
+    if (plaintext_len > kNoAllocMaxPlaintext ||
+        dst_capacity < lmcache_gpu_aesgcm_frame_size(plaintext_len)) {
+        return LMCACHE_GPU_AESGCM_ERR_ARGUMENT;
+    }
+    if (device < 0 || device >= kMaxDevices) {
+        return LMCACHE_GPU_AESGCM_ERR_ARGUMENT;
+    }
+    DeviceGuard guard(device);
+    if (!guard.ok()) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    NoAllocDevice& st = g_noalloc_dev[device];
+    std::call_once(st.once, [&]() { st.status = noalloc_setup(device, st); });
+    if (st.status != LMCACHE_GPU_AESGCM_OK) {
+        return st.status;
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_ptr);
+
+    dev::SealArgs args{};
+    args.src = static_cast<const uint8_t*>(src);
+    args.frame = static_cast<uint8_t*>(dst);
+    args.plen = plaintext_len;
+    const uint64_t n = (static_cast<uint64_t>(plaintext_len) + 15u) / 16u;
+    args.nblocks = static_cast<uint32_t>(n);
+    for (int k = 0; k < 3; ++k) {
+        args.ivw[k] = le_word(iv + 4 * k);
+    }
+    confkv::aes128_expand_le(key, args.rk);
+    args.kt.aes_t = reinterpret_cast<const uint32_t*>(st.scratch);
+    args.kt.gh_pow2 = reinterpret_cast<const uint4*>(st.scratch + kNoAllocAesBytes);
+    args.slot = reinterpret_cast<dev::Slot*>(st.scratch + kNoAllocSlotOffset);
+
+    {
+        // Upload the key's tables unless this device already holds them. The
+        // copy is ordered on `stream`; from pageable memory it returns once
+        // the source has been consumed, so the staging buffer is free again.
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!st.have_key || std::memcmp(st.key, key, 16) != 0) {
+            uint8_t zero[16] = {0};
+            uint8_t hbytes[16];
+            confkv::aes128_encrypt_block(args.rk, zero, hbytes);
+            confkv::aes_t_tables(reinterpret_cast<uint32_t(*)[256]>(g_noalloc_staging));
+            confkv::Gf128 p = confkv::gf_load(hbytes);
+            for (int k = 0; k < kNoAllocPow2Tables; ++k) {
+                confkv::ghash_table(p, g_noalloc_staging + kNoAllocAesBytes +
+                                           static_cast<size_t>(k) * confkv::kGhashTableBytes);
+                p = confkv::gf_mul(p, p);
+            }
+            if (cudaMemcpyAsync(st.scratch, g_noalloc_staging, kNoAllocTableBytes, cudaMemcpyHostToDevice, s) !=
+                cudaSuccess) {
+                st.have_key = false;
+                return LMCACHE_GPU_AESGCM_ERR_CUDA;
+            }
+            std::memcpy(st.key, key, 16);
+            st.have_key = true;
+        }
+    }
+
+    cudaError_t e;
+    if (n == 0) {
+        args.grid = 1;
+        dev::seal_empty_kernel<<<1, 32, 0, s>>>(args);
+        e = cudaGetLastError();
+        std::memset(args.rk, 0, sizeof(args.rk));
+        return cuda_rc(e);
+    }
+    // The slot must start at zero; it keeps whatever the previous call left.
+    if (cudaMemsetAsync(args.slot, 0, sizeof(dev::Slot), s) != cudaSuccess) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    horner_grid(n, st.num_sms, args.iters, args.grid);
+    const uintptr_t ct = reinterpret_cast<uintptr_t>(dst) + 13u;
+    const uint32_t off = static_cast<uint32_t>(ct & 15u);
+    const bool pt_aligned = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+    int sq = 4;
+    if (off != 0) {
+        const uint32_t sh = 16u - off;
+        sq = static_cast<int>(sh >> 2);
+        args.store_r = sh & 3u;
+    }
+    if (pt_aligned) {
+        switch (sq) {
+        case 0: e = launch_seal_t<0, true>(args, s); break;
+        case 1: e = launch_seal_t<1, true>(args, s); break;
+        case 2: e = launch_seal_t<2, true>(args, s); break;
+        case 3: e = launch_seal_t<3, true>(args, s); break;
+        default: e = launch_seal_t<4, true>(args, s); break;
+        }
+    } else {
+        switch (sq) {
+        case 0: e = launch_seal_t<0, false>(args, s); break;
+        case 1: e = launch_seal_t<1, false>(args, s); break;
+        case 2: e = launch_seal_t<2, false>(args, s); break;
+        case 3: e = launch_seal_t<3, false>(args, s); break;
+        default: e = launch_seal_t<4, false>(args, s); break;
+        }
+    }
+    std::memset(args.rk, 0, sizeof(args.rk));
+    return cuda_rc(e);
+}
+
 extern "C" const char* lmcache_gpu_aesgcm_strerror(int rc)
 {
     switch (rc) {

@@ -82,6 +82,31 @@ int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, const void* s
                                      size_t frame_len, void* dst, size_t plaintext_len,
                                      int* auth_ok, void* stream);
 
+/*
+ * Seal that allocates nothing. No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc when they seal (a server whose
+ * memory pool already owns the device's memory, or a thread that must not
+ * take cudaMalloc's implicit device synchronisation). It takes the raw
+ * 16-byte key instead of a handle, runs on `device`, and writes the same
+ * frame as lmcache_gpu_aes128gcm_seal_async. Its only working memory is one
+ * file-scope __device__ array of 233,728 bytes that every GPU loading this
+ * library holds until the process exits; it calls no cudaMalloc or cudaFree.
+ *
+ * - plaintext_len above 1 GiB (2^30 bytes) -> ERR_ARGUMENT (the array holds
+ *   GHASH tables for objects up to that size); other argument rules as seal.
+ * - The first call on a device sets up that device (resolves the array's
+ *   address, opts the kernels into their shared memory, checks the layout);
+ *   make that first call before any stream capture.
+ * - All calls share the array: it keeps the last call's key tables (a new
+ *   key uploads new ones, in stream order) and the accumulation slot, which
+ *   each call clears. Calls whose work overlaps on the GPU race on it;
+ *   issue them on one stream or wait for the previous call.
+ */
+int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key_len, const void* src,
+                                       size_t plaintext_len, void* dst, size_t dst_capacity,
+                                       const uint8_t* iv, int device, void* stream);
+
 /* rc -> static string (reference gpu_aesgcm_api.h:90-92). */
 const char* lmcache_gpu_aesgcm_strerror(int rc);
 

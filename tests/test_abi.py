@@ -24,8 +24,12 @@ def header_functions():
     return set(re.findall(r"^\s*(?:size_t|int|const char\*)\s+(lmcache_\w+)\s*\(", text, re.M))
 
 
+NOALLOC_SYMBOL = "lmcache_gpu_aes128gcm_seal_noalloc"
+
+
 def test_header_declares_the_reference_abi():
-    assert header_functions() == set(EXPORTED_SYMBOLS)
+    # the reference's seven entry points plus the seal that allocates nothing
+    assert header_functions() == set(EXPORTED_SYMBOLS) | {NOALLOC_SYMBOL}
 
 
 def test_library_exports_every_header_symbol(cpu_lib):
@@ -102,6 +106,24 @@ def test_open_argument_errors(cpu_lib):
     assert op(FAKE_HANDLE, p, 44, p, 16, p, None) == ERR_ARG
     big = 16 * 0xFFFFFFFF
     assert op(FAKE_HANDLE, p, big + 29, p, big, p, None) == ERR_ARG
+
+
+def test_seal_noalloc_argument_errors(cpu_lib):
+    f = getattr(cpu_lib.lib, NOALLOC_SYMBOL)
+    vp, sz = ctypes.c_void_p, ctypes.c_size_t
+    f.argtypes = [vp, sz, vp, sz, vp, sz, vp, ctypes.c_int, vp]
+    f.restype = ctypes.c_int
+    key = bytes(16)
+    iv = (ctypes.c_uint8 * 12)()
+    p = ctypes.c_void_p(0x2000)
+    assert f(None, 16, p, 16, p, 45, iv, 0, None) == ERR_ARG
+    assert f(key, 15, p, 16, p, 45, iv, 0, None) == ERR_ARG
+    assert f(key, 16, None, 16, p, 45, iv, 0, None) == ERR_ARG
+    assert f(key, 16, p, 16, None, 45, iv, 0, None) == ERR_ARG
+    assert f(key, 16, p, 16, p, 45, None, 0, None) == ERR_ARG
+    assert f(key, 16, p, 16, p, 44, iv, 0, None) == ERR_ARG
+    assert f(key, 16, p, (1 << 30) + 1, p, (1 << 30) + 30, iv, 0, None) == ERR_ARG
+    assert f(key, 16, p, 16, p, 45, iv, -1, None) == ERR_ARG
 
 
 def test_binding_rejects_bad_lengths(cpu_lib):
