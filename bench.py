@@ -56,10 +56,9 @@ def parse():
 
 
 def dist_env():
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return rank, world, local
+    from confkv_b200.multigpu import rank_env
+
+    return rank_env()
 
 
 def load_peaks() -> tuple[float, str]:
@@ -218,18 +217,11 @@ def run_ours(args, rank, world, local):
     e2e = {"ms": float("nan"), "gbs": float("nan"), "h2d": 0, "d2h": 0} if args.no_e2e else \
         run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args)
 
-    t = torch.tensor([total_ms, sum(seal_ms), sum(open_ms), e2e["ms"], float(ok)], dtype=torch.float64, device=dev)
-    if world > 1:
-        import torch.distributed as dist
+    from confkv_b200 import multigpu
 
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        mn = t.clone()
-        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
-        total_ms, seal_sum, open_sum, e2e_ms = mx[0].item(), mx[1].item(), mx[2].item(), mx[3].item()
-        ok = mn[4].item() == 1.0
-    else:
-        seal_sum, open_sum, e2e_ms = sum(seal_ms), sum(open_ms), e2e["ms"]
+    total_ms, seal_sum, open_sum, e2e_ms = multigpu.reduce_max(
+        [total_ms, sum(seal_ms), sum(open_ms), e2e["ms"]], device=dev)
+    ok = multigpu.all_ok(ok, device=dev)
 
     if rank == 0:
         bytes_per_step = 2 * nobj * P * world  # sealed + opened plaintext, all ranks
@@ -242,7 +234,7 @@ def run_ours(args, rank, world, local):
         # bytes = read P + write P + 29.
         seal_launch_ms = seal_sum / args.steps / nobj
         achieved = (2 * P + 29) / (seal_launch_ms * 1e-3) / 1e9
-        traffic = profile_traffic("seal_kernel_kv_llama8b.txt")
+        traffic = profile_traffic("seal_kernel_kv_llama8b.txt")  # DRAM bytes per launch (ncu)
         line = {
             "metric": METRIC,
             "value": round(value, 2),
