@@ -17,7 +17,8 @@ def to_host(t: torch.Tensor) -> np.ndarray:
 def dev_bytes(data, offset: int = 0, extra: int = 0, fill: int = 0xCC) -> tuple[torch.Tensor, int]:
     """Copy `data` to the device at byte `offset` of a fresh buffer; returns
     (buffer, address of the first byte)."""
-    arr = np.frombuffer(bytes(data), dtype=np.uint8) if not isinstance(data, np.ndarray) else data.view(np.uint8).reshape(-1)
+    arr = np.array(np.frombuffer(bytes(data), dtype=np.uint8)) if not isinstance(data, np.ndarray) \
+        else np.ascontiguousarray(data).view(np.uint8).reshape(-1)
     buf = torch.full((offset + arr.size + extra + 16,), fill, dtype=torch.uint8, device="cuda")
     if arr.size:
         buf[offset:offset + arr.size].copy_(torch.from_numpy(np.ascontiguousarray(arr)))
