@@ -51,6 +51,9 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
 
     fill_aes_smem(smem + kSealAes, a.kt.aes_t);
     fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
+    for (int i = threadIdx.x; i < kSealFoldSmemLevels * 512; i += blockDim.x) {
+        reinterpret_cast<uint4*>(smem + kSealFold)[i] = __ldg(a.kt.gh_pow2 + i);
+    }
     if (blockIdx.x == 0 && tid == 0) {
         a.frame[0] = 1;
         for (int b = 0; b < 12; ++b) {
@@ -97,17 +100,21 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
             ch.q[k] = make_uint4(0, 0, 0, 0);
         }
 
-        // Rows [r_a, r_a + R*ngroups) hold only full blocks inside the object
+        // Rows [r_a, r_a + kPair*ngroups) hold only full blocks inside the object
         // and start at a multiple of R: they run the check-free loop below.
         // The others (CTA 0's leading padding, the row with the last partial
         // block, leftovers) take generic_row. Rows are visited in order.
+        // The interior loop takes kPair = 2 rows per iteration; it starts on
+        // an even row so row r lands in chain r mod R (R divides kPair).
+        constexpr int64_t kPair = 2;
+        static_assert(kPair % R == 0, "chains must divide the rows per iteration");
         const int64_t n_full = static_cast<int64_t>(P / 16u);
         const int64_t r_lo = base >= 0 ? 0 : (-base + T - 1) / T;
         int64_t r_hi = (n_full - base) / T;
         r_hi = r_hi > rows ? rows : r_hi;
-        int64_t r_a = (r_lo + R - 1) / R * R;
+        int64_t r_a = (r_lo + kPair - 1) / kPair * kPair;
         r_a = r_a > r_hi ? r_hi : r_a;
-        const int64_t ngroups = r_hi > r_a ? (r_hi - r_a) / R : 0;
+        const int64_t ngroups = r_hi > r_a ? (r_hi - r_a) / kPair : 0;
 
         auto generic_row = [&](int64_t r) __attribute__((always_inline)) {
             const int64_t i = base + r * T + tid;
@@ -146,37 +153,58 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
                     pf1 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(nx + kRowBytes)) : load_bytes(nx + kRowBytes, 16);
                 }
                 const uint4 m0 = gh_mul_rep<kSealGh>(ch.q[0], lb_lo, lb_hi);
-                const uint4 m1 = gh_mul_rep<kSealGh>(ch.q[1], lb_lo, lb_hi);
                 uint32_t x[4], y[4];
                 aes_ctr2_cached<kSealAes>(x, y, ctr, ctr + static_cast<uint32_t>(T), cc, s012, rk3x, a.rk, lb);
                 const uint4 c0 = make_uint4(p0.x ^ x[0], p0.y ^ x[1], p0.z ^ x[2], p0.w ^ x[3]);
                 const uint4 c1 = make_uint4(p1.x ^ y[0], p1.y ^ y[1], p1.z ^ y[2], p1.w ^ y[3]);
                 store_ct_interior<SQ>(cp, c0, s, fsel, lane);
                 store_ct_interior<SQ>(cp + kRowBytes, c1, s, fsel, lane);
-                ch.q[0] = xor4(m0, c0);
-                ch.q[1] = xor4(m1, c1);
+                if constexpr (R == 1) {
+                    ch.q[0] = xor4(gh_mul_rep<kSealGh>(xor4(m0, c0), lb_lo, lb_hi), c1);
+                } else {
+                    const uint4 m1 = gh_mul_rep<kSealGh>(ch.q[1], lb_lo, lb_hi);
+                    ch.q[0] = xor4(m0, c0);
+                    ch.q[1] = xor4(m1, c1);
+                }
                 sp += 2 * kRowBytes;
                 cp += 2 * kRowBytes;
                 ctr += 2u * static_cast<uint32_t>(T);
             }
-            r = r_a + R * ngroups;
+            r = r_a + kPair * ngroups;
         }
 #pragma unroll 1
         for (; r < rows; ++r) {
             generic_row(r);
         }
-        part[tid] = chains_combine<R>(ch, rows, a.kt.gh_pow2 + kHornerLog2 * 512);
+        part[tid] = R == 1 ? ch.q[0] : chains_combine<R>(ch, rows, a.kt.gh_pow2 + kHornerLog2 * 512);
     }
     __syncthreads();
 
-    // Stage the fold tables H^(2^l), l < kFoldLevels, over the AES region
-    // (E_K(J0) was computed by the power warp before the main loop).
-    uint4* fold_tabs = reinterpret_cast<uint4*>(smem + kSealAes);
-    for (int i = tid; i < kFoldLevels * 512; i += blockDim.x) {
-        fold_tabs[i] = __ldg(a.kt.gh_pow2 + i);
+    // Fold: levels 0..2 use the tables staged in the prologue; the tables of
+    // levels 3.. are loaded now (the AES region is free) and stored after
+    // levels 0..2, so their L2 latency overlaps that work.
+    {
+        constexpr int kLate = (kFoldLevels - kSealFoldSmemLevels) * 512;
+        constexpr int kPer = (kLate + kSealThreads - 1) / kSealThreads;
+        uint4 late[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = tid + k * kSealThreads;
+            late[k] = i < kLate ? __ldg(a.kt.gh_pow2 + kSealFoldSmemLevels * 512 + i) : make_uint4(0, 0, 0, 0);
+        }
+        fold_partials<kSealFoldSmemLevels>(part, reinterpret_cast<const uint4*>(smem + kSealFold), a.kt.gh_pow2,
+                                           0, kSealFoldSmemLevels);
+        uint4* late_tabs = reinterpret_cast<uint4*>(smem + kSealAes);
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = tid + k * kSealThreads;
+            if (i < kLate) {
+                late_tabs[i] = late[k];
+            }
+        }
+        __syncthreads();
+        fold_partials<kFoldLevels>(part, late_tabs, a.kt.gh_pow2, kSealFoldSmemLevels, kFoldLevels);
     }
-    __syncthreads();
-    fold_partials(part, fold_tabs);
 
     if (warp == kPowerWarp) {
         unsigned long long shi, slo;
@@ -224,6 +252,9 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     const int warp = tid >> 5;
 
     fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
+    for (int i = threadIdx.x; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
+        reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);  // H^(2^l), l <= kHornerLog2
+    }
     __syncthreads();
 
     const uint64_t P = a.plen;
@@ -317,16 +348,11 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
         for (; r < rows; ++r) {
             generic_row(r);
         }
-        part[tid] = chains_combine<R>(ch, rows, a.kt.gh_pow2 + kHornerLog2 * 512);
+        part[tid] = chains_combine<R>(ch, rows, reinterpret_cast<const uint4*>(smem + kOpenHt));
     }
     __syncthreads();
 
-    uint4* fold_tabs = reinterpret_cast<uint4*>(smem + kOpenGh);
-    for (int i = tid; i < kFoldLevels * 512; i += blockDim.x) {
-        fold_tabs[i] = __ldg(a.kt.gh_pow2 + i);
-    }
-    __syncthreads();
-    fold_partials(part, fold_tabs);
+    fold_partials<kFoldLevels>(part, reinterpret_cast<const uint4*>(smem + kOpenFold), a.kt.gh_pow2);
 
     if (warp == kPowerWarp) {
         unsigned long long shi, slo;

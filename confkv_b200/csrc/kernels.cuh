@@ -16,8 +16,8 @@ namespace dev {
 constexpr int kHornerThreads = 512;                 // threads running GHASH rows per CTA
 constexpr int kHornerLog2 = 9;                      // log2(kHornerThreads)
 constexpr int kFoldLevels = kHornerLog2;
-constexpr int kSealChains = 2;                      // GHASH chains per thread in seal
-constexpr int kSealChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * kHornerThreads)
+constexpr int kSealChains = 1;                      // GHASH chains per thread in seal
+constexpr int kSealChainLog2 = kHornerLog2;         // chain multiplier H^kHornerThreads
 constexpr int kOpenChains = 2;                      // GHASH chains per thread in open
 constexpr int kOpenChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * kHornerThreads)
 constexpr int kPowerWarp = kHornerThreads / 32;     // warp index of the power warp
@@ -39,19 +39,22 @@ constexpr uint32_t kPartBytes = kHornerThreads * 16;
 // are staged over a table region that is no longer read.
 constexpr uint32_t kFoldBytes = kFoldLevels * 8192u;
 
+constexpr int kSealFoldSmemLevels = 3;             // fold levels whose tables seal keeps in smem
 constexpr uint32_t kSealAes = 0;
 constexpr uint32_t kSealGh = kSealAes + kAesBytes;
 constexpr uint32_t kSealPart = kSealGh + kGhBytes;
-constexpr uint32_t kSealMisc = kSealPart + kPartBytes;
+constexpr uint32_t kSealFold = kSealPart + kPartBytes;
+constexpr uint32_t kSealMisc = kSealFold + kSealFoldSmemLevels * 8192u;
 constexpr uint32_t kSealSmem = kSealMisc + 64;
 
 constexpr uint32_t kOpenGh = 0;
-constexpr uint32_t kOpenPart = kOpenGh + (kGhBytes > kFoldBytes ? kGhBytes : kFoldBytes);
+constexpr uint32_t kOpenFold = kOpenGh + kGhBytes;   // all fold tables, staged in the prologue
+constexpr uint32_t kOpenHt = kOpenFold + kFoldBytes;  // compact table of H^kHornerThreads (chain combine)
+constexpr uint32_t kOpenPart = kOpenHt + 8192u;
 constexpr uint32_t kOpenMisc = kOpenPart + kPartBytes;
 constexpr uint32_t kOpenSmem = kOpenMisc + 64;
 
 constexpr uint32_t kCtrSmem = kAesBytes;
-static_assert(kFoldBytes <= kAesBytes, "seal stages the fold tables over the AES region");
 static_assert(kSealSmem <= 227u * 1024u, "seal shared memory exceeds the per-block limit");
 
 // Shared-window address at which dynamic shared memory starts for a kernel
@@ -513,14 +516,79 @@ __device__ inline uint4 warp_h_pow(const uint4* pow2, unsigned long long d, int 
     return m;
 }
 
+// 128-bit shifts of (hi, lo) (hi = coefficients x^0..x^63, MSB first) by
+// 0 <= s < 128 bits; "right" moves toward higher powers of x.
+__device__ __forceinline__ void shr128(unsigned long long& hi, unsigned long long& lo, int s)
+{
+    if (s >= 64) {
+        lo = hi >> (s - 64);
+        hi = 0;
+    } else if (s > 0) {
+        lo = (lo >> s) | (hi << (64 - s));
+        hi >>= s;
+    }
+}
+
+__device__ __forceinline__ void shl128(unsigned long long& hi, unsigned long long& lo, int s)
+{
+    if (s >= 64) {
+        hi = lo << (s - 64);
+        lo = 0;
+    } else if (s > 0) {
+        hi = (hi << s) | (lo >> (64 - s));
+        lo <<= s;
+    }
+}
+
+// (hi, lo) <- (hi, lo) * x^0 + x^1 + x^2 + x^7 applied to an element of degree
+// < 121 (no overflow): the reduction polynomial of x^128 in GF(2^128).
+__device__ __forceinline__ void mul_r(unsigned long long& hi, unsigned long long& lo)
+{
+    unsigned long long h1 = hi, l1 = lo, h2 = hi, l2 = lo, h7 = hi, l7 = lo;
+    shr128(h1, l1, 1);
+    shr128(h2, l2, 2);
+    shr128(h7, l7, 7);
+    hi ^= h1 ^ h2 ^ h7;
+    lo ^= l1 ^ l2 ^ l7;
+}
+
+// V * x^k for 0 <= k < 128 without a loop: shift, then fold the k overflow
+// bits back with x^128 = 1 + x + x^2 + x^7 (twice: the second overflow,
+// from the x^2 and x^7 terms when k > 121, has degree < 7).
+__device__ inline void gf_mul_xk(unsigned long long& hi, unsigned long long& lo, int k)
+{
+    if (k == 0) {
+        return;
+    }
+    unsigned long long oh = hi, ol = lo;  // overflow: the low k bits moved to the top
+    shl128(oh, ol, 128 - k);
+    shr128(hi, lo, k);
+    // second-level overflow of O*(x^2 + x^7): the low 2 and 7 bits of O
+    unsigned long long ph = oh, pl = ol, qh = oh, ql = ol;
+    shl128(ph, pl, 126);
+    shl128(qh, ql, 121);
+    unsigned long long o2h = ph ^ qh, o2l = pl ^ ql;
+    // O * (1 + x + x^2 + x^7), keeping only the part that stays below x^128
+    unsigned long long rh = oh, rl = ol;
+    {
+        unsigned long long h1 = oh, l1 = ol, h2 = oh, l2 = ol, h7 = oh, l7 = ol;
+        shr128(h1, l1, 1);
+        shr128(h2, l2, 2);
+        shr128(h7, l7, 7);
+        rh ^= h1 ^ h2 ^ h7;
+        rl ^= l1 ^ l2 ^ l7;
+    }
+    mul_r(o2h, o2l);
+    hi ^= rh ^ o2h;
+    lo ^= rl ^ o2l;
+}
+
 // Power warp, part 2: lane p keeps U_p = M * x^(4p) for the final multiply.
 __device__ inline void warp_lane_basis(uint4 m_raw, int lane, unsigned long long& uhi,
                                        unsigned long long& ulo)
 {
     raw_to_be(m_raw, uhi, ulo);
-    for (int s = 0; s < 4 * lane; ++s) {
-        gf_mul_x(uhi, ulo);
-    }
+    gf_mul_xk(uhi, ulo, 4 * lane);
 }
 
 // Power warp, part 3: F * M where lane p holds U_p = M * x^(4p); result
@@ -583,18 +651,28 @@ __device__ inline bool cta_accumulate(Slot* slot, uint4 fold, unsigned long long
     return true;
 }
 
-// Fold the kHornerThreads partials in shared memory: after level l the entry
-// at index p * 2^(l+1) holds left * H^(2^l) + right. fold_tabs are the compact
-// tables for H^(2^l), l = 0..kFoldLevels-1, staged in shared memory.
-__device__ __forceinline__ void fold_partials(uint4* part, const uint4* fold_tabs)
+// Fold the kHornerThreads partials in shared memory, levels [first, last):
+// after level l the entry at index p * 2^(l+1) holds left * H^(2^l) + right.
+// Levels l < NSMEM read the compact table of H^(2^l) staged in shared memory
+// at smem_tabs + 512 (l - first); the rest read it from global memory
+// (pow2 + 512 l) through L1. A zero left operand (rows the object does not
+// reach) skips its multiply.
+template <int NSMEM>
+__device__ __forceinline__ void fold_partials(uint4* part, const uint4* smem_tabs, const uint4* pow2,
+                                              int first = 0, int last = kFoldLevels)
 {
 #pragma unroll 1
-    for (int l = 0; l < kFoldLevels; ++l) {
+    for (int l = first; l < last; ++l) {
         const int pairs = kHornerThreads >> (l + 1);
         const int t = threadIdx.x;
         if (t < pairs) {
             const int left = t << (l + 1);
-            part[left] = xor4(gh_mul_compact(part[left], fold_tabs + l * 512), part[left + (1 << l)]);
+            const uint4 x = part[left];
+            uint4 m = make_uint4(0, 0, 0, 0);
+            if ((x.x | x.y | x.z | x.w) != 0u) {
+                m = gh_mul_compact(x, l < NSMEM ? smem_tabs + (l - first) * 512 : pow2 + l * 512);
+            }
+            part[left] = xor4(m, part[left + (1 << l)]);
         }
         __syncthreads();
     }

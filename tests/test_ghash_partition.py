@@ -6,8 +6,8 @@ The kernels split the n ciphertext blocks over G CTAs of J rows x T threads
 skipped). Each thread runs R Horner chains (chain k takes its rows r = k mod R,
 multiplier H^(R*T)), combines them with H^T into sum_r X_r H^(T(J-1-r)), the T
 thread shares are folded with H^(2^l), and each CTA's fold is scaled by
-H^(d_c), d_c = (G-1-c)JT + 2; the length block contributes L*H. R = 2 in
-seal_kernel, 4 in open_ghash_kernel. This model mirrors horner_grid() in
+H^(d_c), d_c = (G-1-c)JT + 2; the length block contributes L*H. R = 1 in
+seal_kernel, 2 in open_ghash_kernel. This model mirrors horner_grid() in
 confkv_b200/csrc/gpu_aesgcm.cu and the algebra of chain_push_dyn /
 chains_combine / fold_partials / cta_accumulate in kernels.cuh.
 """
@@ -78,7 +78,7 @@ def model_ghash(oracle, h: bytes, ct: bytes, num_sms: int, chains: int) -> bytes
     return xor(acc, mul(lenblk, h))
 
 
-@pytest.mark.parametrize("chains", [2])
+@pytest.mark.parametrize("chains", [1, 2])
 @pytest.mark.parametrize("size,num_sms", [(1, 148), (16, 148), (17, 4), (4096, 148), (16 * 700 + 5, 2),
                                           (16 * 1024, 4), (16 * 1537 + 9, 3), (16 * 3000, 2)])
 def test_partitioned_ghash_matches_serial(oracle, size, num_sms, chains):
