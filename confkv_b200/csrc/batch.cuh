@@ -1,0 +1,550 @@
+// Batched seal / open: one plan launch and one (seal) or two (open)
+// persistent launches for any number of objects of any sizes and alignments.
+//
+//   batch_plan_kernel    one CTA: validates every descriptor (status), sums
+//                        the rows, picks the tile height J* so the batch has
+//                        about kBatchWaves tiles per SM, gives object i
+//                        J_i = min(J*, rows_i) and G_i = ceil(n_i / (J_i T))
+//                        tiles, and writes the tile records (object, tile)
+//                        with taller tiles first, so the queue's tail holds
+//                        the short ones.
+//   seal_batch_kernel    one CTA per SM; each takes tiles from the queue
+//   open_ghash_batch_    (atomic head) and runs the same tile bodies as the
+//   kernel               single-object kernels (tiles.cuh). A one-tile
+//   open_ctr_batch_      object needs no atomics; others accumulate through
+//   kernel               their slot and the last tile writes the tag / the
+//                        verdict. No CTA waits for another.
+//
+// Device-written workspace (caller-owned, any contents on entry):
+//   [0, 256)            BatchHeader
+//   [256, ...)          one Slot per object: acc, ticket, aux = {J, G, verdict}
+//   [tiles_offset, ...) TileRec per tile, at most count + kBatchExtraTiles
+#pragma once
+
+#include "tiles.cuh"
+
+namespace confkv {
+namespace dev {
+
+// Device view of lmcache_gpu_aesgcm_batch_item (include/gpu_aesgcm_api.h).
+struct BatchItem {
+    const uint8_t* src;   // seal: plaintext; open: frame
+    uint8_t* dst;         // seal: frame; open: plaintext
+    uint64_t plen;
+    uint64_t capacity;    // seal: dst capacity; open: frame length
+    int* auth_ok;         // open only
+    uint32_t iv[3];       // seal only: IV bytes as little-endian words
+    int32_t status;       // written by the plan: 0 or ERR_ARGUMENT
+    uint64_t reserved;
+};
+static_assert(sizeof(BatchItem) == 64, "batch descriptor is 64 bytes");
+
+constexpr int kBatchWaves = 8;        // target tiles per SM
+constexpr int kBatchMaxSms = 256;     // SMs counted for the tile bound
+constexpr uint32_t kBatchExtraTiles = static_cast<uint32_t>(kBatchWaves * kBatchMaxSms);
+constexpr uint32_t kBatchMaxItems = 1u << 20;
+constexpr int kPlanThreads = 1024;
+constexpr int kBuckets = 32;
+constexpr uint64_t kBatchMaxBlocks = 0xfffffffeull;
+constexpr uint32_t kCtrBatchMisc = kAesBytes;
+constexpr uint32_t kCtrBatchSmem = kCtrBatchMisc + 64;
+
+struct BatchHeader {
+    uint32_t total_tiles;
+    uint32_t next_tile[2];   // queue heads: [0] seal / open GHASH, [1] open CTR
+    uint32_t iters_max;      // J*
+    uint32_t pad[12];
+};
+
+struct TileRec {
+    uint32_t item;
+    uint32_t cta;            // tile index c within the object
+};
+
+__host__ __device__ constexpr size_t batch_slots_offset() { return 256; }
+__host__ __device__ constexpr size_t batch_tiles_offset(size_t count)
+{
+    return 256 + (count * sizeof(Slot) + 255) / 256 * 256;
+}
+__host__ __device__ constexpr size_t batch_workspace_bytes(size_t count)
+{
+    return batch_tiles_offset(count) + (count + kBatchExtraTiles) * sizeof(TileRec);
+}
+
+struct BatchArgs {
+    BatchItem* items;
+    uint8_t* ws;
+    uint32_t count;
+    uint32_t rk[44];
+    KeyTables kt;
+};
+
+// ------------------------------------------------------------------ plan
+
+// `open` selects the descriptor rules: seal needs capacity >= P + 29; open
+// needs frame length >= P + 29 and an auth_ok pointer. sms_waves = tiles the
+// batch should have when it is large (SMs x kBatchWaves).
+__global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* items, uint32_t count,
+                                                                  uint8_t* ws, int open, uint32_t sms_waves)
+{
+    __shared__ unsigned long long red[kPlanThreads / 32];
+    __shared__ unsigned int hist[kBuckets];
+    __shared__ unsigned int cursor[kBuckets];
+    __shared__ unsigned long long total_rows;
+    BatchHeader* hdr = reinterpret_cast<BatchHeader*>(ws);
+    Slot* st = reinterpret_cast<Slot*>(ws + batch_slots_offset());
+    TileRec* rec = reinterpret_cast<TileRec*>(ws + batch_tiles_offset(count));
+    const int tid = threadIdx.x;
+    constexpr uint64_t T = kHornerThreads;
+    if (tid < kBuckets) {
+        hist[tid] = 0;
+    }
+
+    // Pass 1: validate, rows per object (a zero-length object is one row:
+    // its tile writes the header and tag), reset the slot.
+    unsigned long long rows_sum = 0;
+    for (uint32_t i = tid; i < count; i += kPlanThreads) {
+        BatchItem& it = items[i];
+        const uint64_t P = it.plen;
+        const uint64_t n = P / 16u + ((P & 15u) != 0);
+        bool ok = it.src != nullptr && it.dst != nullptr && n <= kBatchMaxBlocks && it.capacity >= P + 29u;
+        if (open) {
+            ok = ok && it.auth_ok != nullptr;
+        }
+        const uint32_t rows = ok ? static_cast<uint32_t>(n == 0 ? 1 : (n + T - 1) / T) : 0u;
+        it.status = ok ? 0 : -1;
+        Slot& s = st[i];
+        s.acc_hi = 0;
+        s.acc_lo = 0;
+        s.ticket = 0;
+        s.aux[0] = rows;
+        s.aux[1] = 0;
+        s.aux[2] = 0;
+        rows_sum += rows;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        rows_sum += __shfl_xor_sync(0xffffffffu, rows_sum, o);
+    }
+    if ((tid & 31) == 0) {
+        red[tid >> 5] = rows_sum;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        unsigned long long v = red[tid];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            v += __shfl_xor_sync(0xffffffffu, v, o);
+        }
+        if (tid == 0) {
+            total_rows = v;
+        }
+    }
+    __syncthreads();
+    unsigned long long js = (total_rows + sms_waves - 1) / sms_waves;
+    js = js < 1 ? 1 : js;
+    const uint32_t jstar = static_cast<uint32_t>(js > 0x7fffffffull ? 0x7fffffffull : js);
+
+    // Pass 2: tile height and count per object; histogram of tiles by
+    // floor(log2 J).
+    for (uint32_t i = tid; i < count; i += kPlanThreads) {
+        Slot& s = st[i];
+        const uint32_t rows = s.aux[0];
+        if (rows == 0) {
+            continue;
+        }
+        const uint32_t J = rows < jstar ? rows : jstar;
+        const uint64_t P = items[i].plen;
+        const uint64_t n = P / 16u + ((P & 15u) != 0);
+        const uint64_t span = static_cast<uint64_t>(J) * T;
+        uint64_t G = (n + span - 1) / span;
+        G = G < 1 ? 1 : G;
+        s.aux[0] = J;
+        s.aux[1] = static_cast<uint32_t>(G);
+        atomicAdd(&hist[31 - __clz(static_cast<int>(J))], static_cast<unsigned int>(G));
+    }
+    __syncthreads();
+    if (tid == 0) {
+        unsigned int pos = 0;
+        for (int b = kBuckets - 1; b >= 0; --b) {
+            cursor[b] = pos;
+            pos += hist[b];
+        }
+        hdr->total_tiles = pos;
+        hdr->next_tile[0] = 0;
+        hdr->next_tile[1] = 0;
+        hdr->iters_max = jstar;
+    }
+    __syncthreads();
+
+    // Pass 3: tile records, tallest bucket first.
+    for (uint32_t i = tid; i < count; i += kPlanThreads) {
+        const Slot& s = st[i];
+        const uint32_t G = s.aux[1];
+        if (G == 0) {
+            continue;
+        }
+        const unsigned int p = atomicAdd(&cursor[31 - __clz(static_cast<int>(s.aux[0]))], G);
+        for (uint32_t c = 0; c < G; ++c) {
+            rec[p + c] = TileRec{i, c};
+        }
+    }
+}
+
+// ------------------------------------------------------------ dispatch
+
+template <int SQ>
+__device__ __forceinline__ uint4 seal_rows_pt(bool pt_aligned, const SealTile& t, const uint32_t* rk,
+                                              const uint4* pow2, int tid, int lane)
+{
+    return pt_aligned ? seal_rows<SQ, true>(t, rk, pow2, tid, lane) : seal_rows<SQ, false>(t, rk, pow2, tid, lane);
+}
+
+__device__ __forceinline__ uint4 seal_rows_any(int sq, bool pt_aligned, const SealTile& t, const uint32_t* rk,
+                                               const uint4* pow2, int tid, int lane)
+{
+    switch (sq) {
+    case 0: return seal_rows_pt<0>(pt_aligned, t, rk, pow2, tid, lane);
+    case 1: return seal_rows_pt<1>(pt_aligned, t, rk, pow2, tid, lane);
+    case 2: return seal_rows_pt<2>(pt_aligned, t, rk, pow2, tid, lane);
+    case 3: return seal_rows_pt<3>(pt_aligned, t, rk, pow2, tid, lane);
+    default: return seal_rows_pt<4>(pt_aligned, t, rk, pow2, tid, lane);
+    }
+}
+
+__device__ __forceinline__ uint4 open_ghash_rows_any(int lq, const OpenTile& t, const uint4* ht, int tid, int lane)
+{
+    switch (lq) {
+    case 0: return open_ghash_rows<0>(t, ht, tid, lane);
+    case 1: return open_ghash_rows<1>(t, ht, tid, lane);
+    case 2: return open_ghash_rows<2>(t, ht, tid, lane);
+    case 3: return open_ghash_rows<3>(t, ht, tid, lane);
+    default: return open_ghash_rows<4>(t, ht, tid, lane);
+    }
+}
+
+template <int LQ>
+__device__ __forceinline__ void ctr_rows_pt(bool pt_aligned, const CtrTile& t, const uint32_t* rk, int tid, int lane)
+{
+    if (pt_aligned) {
+        ctr_rows<LQ, true>(t, rk, tid, lane);
+    } else {
+        ctr_rows<LQ, false>(t, rk, tid, lane);
+    }
+}
+
+__device__ __forceinline__ void ctr_rows_any(int lq, bool pt_aligned, const CtrTile& t, const uint32_t* rk, int tid,
+                                             int lane)
+{
+    switch (lq) {
+    case 0: ctr_rows_pt<0>(pt_aligned, t, rk, tid, lane); break;
+    case 1: ctr_rows_pt<1>(pt_aligned, t, rk, tid, lane); break;
+    case 2: ctr_rows_pt<2>(pt_aligned, t, rk, tid, lane); break;
+    case 3: ctr_rows_pt<3>(pt_aligned, t, rk, tid, lane); break;
+    default: ctr_rows_pt<4>(pt_aligned, t, rk, tid, lane); break;
+    }
+}
+
+// Final GHASH sum of a tile's object: a one-tile object multiplies its fold
+// by H^2 directly; otherwise the fold goes through the object's slot and only
+// the last tile gets the sum. Power warp only; returns true where (shi, slo)
+// holds the sum.
+__device__ __forceinline__ bool batch_object_sum(Slot* slot, uint32_t G, uint4 fold, unsigned long long uhi,
+                                                 unsigned long long ulo, int lane, unsigned long long& shi,
+                                                 unsigned long long& slo)
+{
+    if (G == 1) {
+        warp_generic_mul(fold, uhi, ulo, lane, shi, slo);
+        return true;
+    }
+    return cta_accumulate(slot, fold, uhi, ulo, lane, G, shi, slo);
+}
+
+// Ciphertext store class of a frame: sq = word part of 16 - (ct & 15)
+// (4 when aligned), r = its byte part.
+__device__ __forceinline__ void store_class(const uint8_t* ct, int& sq, uint32_t& r)
+{
+    const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(ct) & 15u);
+    sq = 4;
+    r = 0;
+    if (off != 0) {
+        const uint32_t sh = 16u - off;
+        sq = static_cast<int>(sh >> 2);
+        r = sh & 3u;
+    }
+}
+
+// Ciphertext load class of a frame: lq = word part of (ct & 15) (4 when
+// aligned), r = its byte part.
+__device__ __forceinline__ void load_class(const uint8_t* ct, int& lq, uint32_t& r)
+{
+    const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(ct) & 15u);
+    lq = off == 0 ? 4 : static_cast<int>(off >> 2);
+    r = off & 3u;
+}
+
+// ------------------------------------------------------------------ seal
+
+__global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const BatchArgs a)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* part = reinterpret_cast<uint4*>(smem + kSealPart);
+    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kSealMisc);
+    BatchHeader* hdr = reinterpret_cast<BatchHeader*>(a.ws);
+    Slot* st = reinterpret_cast<Slot*>(a.ws + batch_slots_offset());
+    const TileRec* rec = reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count));
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const uint32_t total = hdr->total_tiles;
+    constexpr int64_t T = kHornerThreads;
+
+    if (tid == 0) {
+        *next_s = atomicAdd(&hdr->next_tile[0], 1u);
+    }
+    __syncthreads();
+    uint32_t tile = *next_s;
+    if (tile >= total) {
+        return;
+    }
+    fill_aes_smem(smem + kSealAes, a.kt.aes_t);
+    fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
+    for (int i = tid; i < kSealFoldSmemLevels * 512; i += blockDim.x) {
+        reinterpret_cast<uint4*>(smem + kSealFold)[i] = __ldg(a.kt.gh_pow2 + i);
+    }
+    __syncthreads();
+
+    // Per-tile values are loaded where they are used (the power warp reloads
+    // them after the fold) so that only `tile` stays live across the rows.
+    for (;;) {
+        unsigned long long uhi = 0, ulo = 0;
+        uint4 ej0 = make_uint4(0, 0, 0, 0);
+        uint4 lh = make_uint4(0, 0, 0, 0);
+        {
+            const TileRec tr = rec[tile];
+            const BatchItem* it = a.items + tr.item;
+            const uint32_t J = st[tr.item].aux[0];
+            const uint32_t G = st[tr.item].aux[1];
+            const uint64_t P = it->plen;
+            const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
+            const int64_t span = static_cast<int64_t>(J) * T;
+            uint8_t* frame = it->dst;
+            const uint32_t ivw[3] = {it->iv[0], it->iv[1], it->iv[2]};
+            if (tr.cta == 0 && tid == 0) {
+                frame[0] = 1;
+                for (int b = 0; b < 12; ++b) {
+                    frame[1 + b] = static_cast<uint8_t>(ivw[b >> 2] >> (8 * (b & 3)));
+                }
+            }
+            if (warp == kPowerWarp) {
+                const unsigned long long d = static_cast<unsigned long long>(G - 1 - tr.cta) *
+                                                 static_cast<unsigned long long>(span) + 2ull;
+                seal_power(ivw, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
+            } else {
+                int sq;
+                uint32_t store_r;
+                store_class(frame + 13, sq, store_r);
+                const SealTile t{it->src, frame + 13, P, n - static_cast<int64_t>(G - tr.cta) * span,
+                                 static_cast<int64_t>(J), {ivw[0] ^ a.rk[0], ivw[1] ^ a.rk[1], ivw[2] ^ a.rk[2]},
+                                 store_r};
+                const bool pt_aligned = (reinterpret_cast<uintptr_t>(it->src) & 15u) == 0;
+                part[tid] = seal_rows_any(sq, pt_aligned, t, a.rk, a.kt.gh_pow2, tid, lane);
+                if (tid == 0) {
+                    *next_s = atomicAdd(&hdr->next_tile[0], 1u);
+                }
+            }
+        }
+        __syncthreads();
+        seal_fold(smem, part, a.kt.gh_pow2, tid);
+        const uint32_t next = *next_s;
+        const uint32_t total_now = hdr->total_tiles;
+
+        if (warp == kPowerWarp) {
+            const uint32_t item = rec[tile].item;
+            Slot* slot = st + item;
+            unsigned long long shi, slo;
+            if (batch_object_sum(slot, slot->aux[1], part[0], uhi, ulo, lane, shi, slo)) {
+                const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
+                if (lane < 16) {
+                    const BatchItem* it = a.items + item;
+                    it->dst[13 + it->plen + lane] = static_cast<uint8_t>(byte_of(tag, lane));
+                }
+            }
+        } else if (next < total_now) {
+            // seal_fold stored the late fold tables over the first
+            // kSealLateBytes of the AES region: T0/T1 entries x < 192.
+            for (int i = tid; i < 4096; i += kHornerThreads) {
+                const int x = (i >> 3) & 255;
+                if (x < static_cast<int>(kSealLateBytes >> 8)) {
+                    const int k = i >> 11;
+                    const uint32_t tv = __ldg(a.kt.aes_t + k * 256 + x);
+                    const uint32_t off = (static_cast<uint32_t>(x) << 8) | (static_cast<uint32_t>(k & 1) << 7) |
+                                         (static_cast<uint32_t>(i & 7) << 4);
+                    *reinterpret_cast<uint4*>(smem + kSealAes + off) = make_uint4(tv, tv, tv, tv);
+                }
+            }
+        }
+        __syncthreads();
+        if (next >= total_now) {
+            break;
+        }
+        tile = next;
+    }
+}
+
+// ------------------------------------------------------------------ open
+
+__global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const BatchArgs a)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* part = reinterpret_cast<uint4*>(smem + kOpenPart);
+    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kOpenMisc);
+    BatchHeader* hdr = reinterpret_cast<BatchHeader*>(a.ws);
+    Slot* st = reinterpret_cast<Slot*>(a.ws + batch_slots_offset());
+    const TileRec* rec = reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count));
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const uint32_t total = hdr->total_tiles;
+    constexpr int64_t T = kHornerThreads;
+
+    if (tid == 0) {
+        *next_s = atomicAdd(&hdr->next_tile[0], 1u);
+    }
+    __syncthreads();
+    uint32_t tile = *next_s;
+    if (tile >= total) {
+        return;
+    }
+    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
+    for (int i = tid; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
+        reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);
+    }
+    __syncthreads();
+
+    for (;;) {
+        unsigned long long uhi = 0, ulo = 0;
+        uint4 ej0 = make_uint4(0, 0, 0, 0);
+        uint4 lh = make_uint4(0, 0, 0, 0);
+        {
+            const TileRec tr = rec[tile];
+            const BatchItem* it = a.items + tr.item;
+            const uint32_t J = st[tr.item].aux[0];
+            const uint32_t G = st[tr.item].aux[1];
+            const uint64_t P = it->plen;
+            const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
+            const int64_t span = static_cast<int64_t>(J) * T;
+            const uint8_t* frame = it->src;
+            if (warp == kPowerWarp) {
+                const unsigned long long d = static_cast<unsigned long long>(G - 1 - tr.cta) *
+                                                 static_cast<unsigned long long>(span) + 2ull;
+                open_power(frame, a.kt.aes_t, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
+            } else {
+                int lq;
+                uint32_t load_r;
+                load_class(frame + 13, lq, load_r);
+                const OpenTile t{frame, it->capacity, P, n - static_cast<int64_t>(G - tr.cta) * span,
+                                 static_cast<int64_t>(J), load_r};
+                part[tid] = open_ghash_rows_any(lq, t, reinterpret_cast<const uint4*>(smem + kOpenHt), tid, lane);
+                if (tid == 0) {
+                    *next_s = atomicAdd(&hdr->next_tile[0], 1u);
+                }
+            }
+        }
+        __syncthreads();
+        fold_partials<kFoldLevels>(part, reinterpret_cast<const uint4*>(smem + kOpenFold), a.kt.gh_pow2);
+        const uint32_t next = *next_s;
+        const uint32_t total_now = hdr->total_tiles;
+
+        if (warp == kPowerWarp) {
+            const uint32_t item = rec[tile].item;
+            Slot* slot = st + item;
+            unsigned long long shi, slo;
+            if (batch_object_sum(slot, slot->aux[1], part[0], uhi, ulo, lane, shi, slo) && lane == 0) {
+                const BatchItem* it = a.items + item;
+                const int v = open_verdict(it->src, it->plen, shi, slo, lh, ej0);
+                *it->auth_ok = v;
+                slot->aux[2] = static_cast<unsigned int>(v);
+            }
+        }
+        __syncthreads();
+        if (next >= total_now) {
+            break;
+        }
+        tile = next;
+    }
+}
+
+// Gated CTR over the same tiles (rows of kCtrThreads = kHornerThreads
+// blocks). Each tile reads its object's verdict, written by
+// open_ghash_batch_kernel earlier on the stream: authentic -> decrypt,
+// otherwise zero the tile's plaintext bytes. The queue head is read from a
+// two-entry shared buffer so one barrier per tile suffices.
+__global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const BatchArgs a)
+{
+    static_assert(kCtrThreads == kHornerThreads, "CTR tiles reuse the GHASH tile rows");
+    extern __shared__ __align__(16) uint8_t smem[];
+    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kCtrBatchMisc);
+    BatchHeader* hdr = reinterpret_cast<BatchHeader*>(a.ws);
+    const Slot* st = reinterpret_cast<const Slot*>(a.ws + batch_slots_offset());
+    const TileRec* rec = reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count));
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const uint32_t total = hdr->total_tiles;
+    constexpr int64_t T = kCtrThreads;
+
+    if (tid == 0) {
+        next_s[0] = atomicAdd(&hdr->next_tile[1], 1u);
+    }
+    __syncthreads();
+    uint32_t tile = next_s[0];
+    if (tile >= total) {
+        return;
+    }
+    fill_aes_smem(smem, a.kt.aes_t);
+    __syncthreads();
+
+    for (uint32_t k = 1;; ++k) {
+        if (tid == 0) {
+            next_s[k & 1] = atomicAdd(&hdr->next_tile[1], 1u);
+        }
+        const TileRec tr = rec[tile];
+        const BatchItem& it = a.items[tr.item];
+        const Slot& slot = st[tr.item];
+        const uint32_t J = slot.aux[0];
+        const uint32_t G = slot.aux[1];
+        const int ok = static_cast<int>(slot.aux[2]);
+        const uint64_t P = it.plen;
+        const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
+        const int64_t span = static_cast<int64_t>(J) * T;
+        const uint8_t* frame = it.src;
+        int lq;
+        uint32_t load_r;
+        load_class(frame + 13, lq, load_r);
+        CtrTile t{frame, it.capacity, it.dst, P, n - static_cast<int64_t>(G - tr.cta) * span,
+                  static_cast<int64_t>(J), {0u, 0u, 0u}, load_r};
+        const bool pt_aligned = (reinterpret_cast<uintptr_t>(it.dst) & 15u) == 0;
+        if (!ok) {
+            if (pt_aligned) {
+                ctr_zero_rows<true>(t, tid);
+            } else {
+                ctr_zero_rows<false>(t, tid);
+            }
+        } else {
+            const uint4 iv = load_bytes(frame + 1, 12);
+            t.s012[0] = iv.x ^ a.rk[0];
+            t.s012[1] = iv.y ^ a.rk[1];
+            t.s012[2] = iv.z ^ a.rk[2];
+            ctr_rows_any(lq, pt_aligned, t, a.rk, tid, lane);
+        }
+        __syncthreads();
+        const uint32_t next = next_s[k & 1];
+        if (next >= total) {
+            break;
+        }
+        tile = next;
+    }
+}
+
+}  // namespace dev
+}  // namespace confkv

@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstddef>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -20,30 +21,25 @@
 
 #include "host_crypto.h"
 #include "kernels.cuh"
+#include "tiles.cuh"
+#include "batch.cuh"
 
 namespace confkv {
 namespace dev {
 
 // ------------------------------------------------------------ seal kernel
 //
-// CTA c owns blocks [n - (G-c)*J*T, n - (G-1-c)*J*T) (only CTA 0 may start
-// below block 0; those leading slots are skipped). Row r of a CTA is blocks
-// base + r*T + t, t = thread, so a warp touches 512 contiguous bytes per row.
-// Each thread keeps kSealChains GHASH chains (rows r = k mod R, multiplier
-// H^(R*T)) and combines them into Q_t = sum_r C_r H^(T*(J-1-r)); the CTA's
-// share of GHASH is (sum_t Q_t H^(T-1-t)) * H^(d_c), d_c = n + 2 - e_c. The
-// power warp computes H^(d_c), E_K(J0) and L*H while the other warps run the
-// main loop; the last CTA to finish writes the tag.
-//
-// SQ selects the ciphertext store: 4 = ciphertext pointer 16-B aligned;
-// 0..3 = word part of the funnel that builds an aligned 16-B chunk from this
-// lane's block and the next lane's (byte part in a.store_r).
+// One object, grid = its G tiles (CTA c = tile c, see tiles.cuh). Each thread
+// keeps kSealChains GHASH chains (rows r = k mod R, multiplier H^(R*T)) and
+// ends with Q_t = sum_r C_r H^(T*(J-1-r)); the CTA's share of GHASH is
+// (sum_t Q_t H^(T-1-t)) * H^(d_c), d_c = (G-1-c) J T + 2. The power warp
+// computes H^(d_c), E_K(J0) and L*H while the other warps run the rows; the
+// last CTA to finish writes the tag.
 template <int SQ, bool PT_ALIGNED>
 __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* part = reinterpret_cast<uint4*>(smem + kSealPart);
-    constexpr int R = kSealChains;
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -63,9 +59,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
     __syncthreads();
 
     const uint64_t P = a.plen;
-    const int64_t n = a.nblocks;
     const int64_t span = static_cast<int64_t>(a.iters) * kHornerThreads;
-    const int64_t base = n - static_cast<int64_t>(a.grid - blockIdx.x) * span;
     uint8_t* ct = a.frame + 13;
 
     unsigned long long uhi = 0, ulo = 0;  // power warp: U_p = H^(d_c) * x^(4p)
@@ -73,138 +67,19 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
     uint4 lh = make_uint4(0, 0, 0, 0);    // power warp: length block * H
 
     if (warp == kPowerWarp) {
-        uint32_t lb[4];
-        aes_lane_bases(lb, lane);
-        uint32_t w[4] = {a.ivw[0] ^ a.rk[0], a.ivw[1] ^ a.rk[1], a.ivw[2] ^ a.rk[2], bswap32(1u) ^ a.rk[3]};
-        aes_rounds_smem<kSealAes>(w, a.rk, lb);
-        ej0 = make_uint4(w[0], w[1], w[2], w[3]);
-        lh = warp_gh_mul_global(be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull), a.kt.gh_pow2, lane);
         const unsigned long long d = static_cast<unsigned long long>(a.grid - 1 - blockIdx.x) *
                                          static_cast<unsigned long long>(span) + 2ull;
-        warp_lane_basis(warp_h_pow(a.kt.gh_pow2, d, lane), lane, uhi, ulo);
+        seal_power(a.ivw, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
     } else {
-        uint32_t lb[4];
-        aes_lane_bases(lb, lane);
-        const uint32_t lb_lo = static_cast<uint32_t>(lane & 7) << 4;
-        const uint32_t lb_hi = 0x80u | lb_lo;
-        const uint32_t s012[3] = {a.ivw[0] ^ a.rk[0], a.ivw[1] ^ a.rk[1], a.ivw[2] ^ a.rk[2]};
-        const uint32_t rk3x = bswap32(a.rk[3]);
-        const uint32_t fsel = funnel_sel(a.store_r);
-        const uint32_t s = (SQ < 4) ? 4u * SQ + a.store_r : 16u;  // 16 - (ct & 15)
-        const int64_t rows = a.iters;
-        constexpr int64_t T = kHornerThreads;
-        constexpr uint64_t kRowBytes = static_cast<uint64_t>(T) * 16u;
-        Chains<R> ch;
-#pragma unroll
-        for (int k = 0; k < R; ++k) {
-            ch.q[k] = make_uint4(0, 0, 0, 0);
-        }
-
-        // Rows [r_a, r_a + kPair*ngroups) hold only full blocks inside the object
-        // and start at a multiple of R: they run the check-free loop below.
-        // The others (CTA 0's leading padding, the row with the last partial
-        // block, leftovers) take generic_row. Rows are visited in order.
-        // The interior loop takes kPair = 2 rows per iteration; it starts on
-        // an even row so row r lands in chain r mod R (R divides kPair).
-        constexpr int64_t kPair = 2;
-        static_assert(kPair % R == 0, "chains must divide the rows per iteration");
-        const int64_t n_full = static_cast<int64_t>(P / 16u);
-        const int64_t r_lo = base >= 0 ? 0 : (-base + T - 1) / T;
-        int64_t r_hi = (n_full - base) / T;
-        r_hi = r_hi > rows ? rows : r_hi;
-        int64_t r_a = (r_lo + kPair - 1) / kPair * kPair;
-        r_a = r_a > r_hi ? r_hi : r_a;
-        const int64_t ngroups = r_hi > r_a ? (r_hi - r_a) / kPair : 0;
-
-        auto generic_row = [&](int64_t r) __attribute__((always_inline)) {
-            const int64_t i = base + r * T + tid;
-            const int nb = block_bytes(i, P);
-            const uint4 p = load_pt_block<PT_ALIGNED>(a.src, i, P);
-            uint32_t x[4] = {s012[0], s012[1], s012[2], bswap32(static_cast<uint32_t>(i) + 2u) ^ a.rk[3]};
-            aes_rounds_smem<kSealAes>(x, a.rk, lb);
-            const uint4 c = mask_bytes(make_uint4(p.x ^ x[0], p.y ^ x[1], p.z ^ x[2], p.w ^ x[3]), nb);
-            store_ct_block<SQ>(ct, i, c, nb, P, s, fsel, lane);
-            chain_push_dyn<kSealGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
-        };
-
-        int64_t r = 0;
-#pragma unroll 1
-        for (; r < r_a; ++r) {
-            generic_row(r);
-        }
-        if (ngroups > 0) {
-            // Two rows per iteration: two AES chains (rounds 1-2 from the
-            // counter cache), two independent GHASH chains, next pair's
-            // plaintext prefetched.
-            const uint64_t i0 = static_cast<uint64_t>(base + r_a * T + tid);
-            const uint8_t* sp = a.src + i0 * 16u;
-            uint8_t* cp = ct + i0 * 16u;
-            uint32_t ctr = static_cast<uint32_t>(i0) + 2u;
-            CtrCache cc{0xffffffffu, 0u, {0u, 0u, 0u, 0u}};
-            uint4 pf0 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(sp)) : load_bytes(sp, 16);
-            uint4 pf1 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(sp + kRowBytes)) : load_bytes(sp + kRowBytes, 16);
-#pragma unroll 1
-            for (int64_t g = 0; g < ngroups; ++g) {
-                const uint4 p0 = pf0;
-                const uint4 p1 = pf1;
-                if (g + 1 < ngroups) {
-                    const uint8_t* nx = sp + 2 * kRowBytes;
-                    pf0 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(nx)) : load_bytes(nx, 16);
-                    pf1 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(nx + kRowBytes)) : load_bytes(nx + kRowBytes, 16);
-                }
-                const uint4 m0 = gh_mul_rep<kSealGh>(ch.q[0], lb_lo, lb_hi);
-                uint32_t x[4], y[4];
-                aes_ctr2_cached<kSealAes>(x, y, ctr, ctr + static_cast<uint32_t>(T), cc, s012, rk3x, a.rk, lb);
-                const uint4 c0 = make_uint4(p0.x ^ x[0], p0.y ^ x[1], p0.z ^ x[2], p0.w ^ x[3]);
-                const uint4 c1 = make_uint4(p1.x ^ y[0], p1.y ^ y[1], p1.z ^ y[2], p1.w ^ y[3]);
-                store_ct_interior<SQ>(cp, c0, s, fsel, lane);
-                store_ct_interior<SQ>(cp + kRowBytes, c1, s, fsel, lane);
-                if constexpr (R == 1) {
-                    ch.q[0] = xor4(gh_mul_rep<kSealGh>(xor4(m0, c0), lb_lo, lb_hi), c1);
-                } else {
-                    const uint4 m1 = gh_mul_rep<kSealGh>(ch.q[1], lb_lo, lb_hi);
-                    ch.q[0] = xor4(m0, c0);
-                    ch.q[1] = xor4(m1, c1);
-                }
-                sp += 2 * kRowBytes;
-                cp += 2 * kRowBytes;
-                ctr += 2u * static_cast<uint32_t>(T);
-            }
-            r = r_a + kPair * ngroups;
-        }
-#pragma unroll 1
-        for (; r < rows; ++r) {
-            generic_row(r);
-        }
-        part[tid] = R == 1 ? ch.q[0] : chains_combine<R>(ch, rows, a.kt.gh_pow2 + kHornerLog2 * 512);
+        const SealTile t{a.src, ct, P,
+                         static_cast<int64_t>(a.nblocks) - static_cast<int64_t>(a.grid - blockIdx.x) * span,
+                         static_cast<int64_t>(a.iters),
+                         {a.ivw[0] ^ a.rk[0], a.ivw[1] ^ a.rk[1], a.ivw[2] ^ a.rk[2]},
+                         a.store_r};
+        part[tid] = seal_rows<SQ, PT_ALIGNED>(t, a.rk, a.kt.gh_pow2, tid, lane);
     }
     __syncthreads();
-
-    // Fold: levels 0..2 use the tables staged in the prologue; the tables of
-    // levels 3.. are loaded now (the AES region is free) and stored after
-    // levels 0..2, so their L2 latency overlaps that work.
-    {
-        constexpr int kLate = (kFoldLevels - kSealFoldSmemLevels) * 512;
-        constexpr int kPer = (kLate + kSealThreads - 1) / kSealThreads;
-        uint4 late[kPer];
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            const int i = tid + k * kSealThreads;
-            late[k] = i < kLate ? __ldg(a.kt.gh_pow2 + kSealFoldSmemLevels * 512 + i) : make_uint4(0, 0, 0, 0);
-        }
-        fold_partials<kSealFoldSmemLevels>(part, reinterpret_cast<const uint4*>(smem + kSealFold), a.kt.gh_pow2,
-                                           0, kSealFoldSmemLevels);
-        uint4* late_tabs = reinterpret_cast<uint4*>(smem + kSealAes);
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            const int i = tid + k * kSealThreads;
-            if (i < kLate) {
-                late_tabs[i] = late[k];
-            }
-        }
-        __syncthreads();
-        fold_partials<kFoldLevels>(part, late_tabs, a.kt.gh_pow2, kSealFoldSmemLevels, kFoldLevels);
-    }
+    seal_fold(smem, part, a.kt.gh_pow2, tid);
 
     if (warp == kPowerWarp) {
         unsigned long long shi, slo;
@@ -235,17 +110,15 @@ __global__ void seal_empty_kernel(const SealArgs a)
 
 // ---------------------------------------------------- open: GHASH + verify
 //
-// Same CTA/row partition and fold as seal_kernel over the ciphertext at
-// frame + 13, with kOpenChains chains per thread and four rows per iteration
-// (next four prefetched). The power warp computes E_K(J0) and L*H up front;
-// the last CTA compares the expected tag with the frame's (16 bytes,
+// Same tiles and fold as seal_kernel over the ciphertext at frame + 13, with
+// kOpenChains chains per thread. The power warp computes E_K(J0) and L*H up
+// front; the last CTA compares the expected tag with the frame's (16 bytes,
 // OR-accumulated) and checks the version byte, then writes *auth_ok.
 template <int LQ>
 __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* part = reinterpret_cast<uint4*>(smem + kOpenPart);
-    constexpr int R = kOpenChains;
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -258,97 +131,21 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     __syncthreads();
 
     const uint64_t P = a.plen;
-    const int64_t n = a.nblocks;
     const int64_t span = static_cast<int64_t>(a.iters) * kHornerThreads;
-    const int64_t base = n - static_cast<int64_t>(a.grid - blockIdx.x) * span;
 
     unsigned long long uhi = 0, ulo = 0;
     uint4 ej0 = make_uint4(0, 0, 0, 0);
     uint4 lh = make_uint4(0, 0, 0, 0);
 
     if (warp == kPowerWarp) {
-        const uint4 iv = load_bytes(a.frame + 1, 12);
-        ej0 = aes_encrypt_gmem(a.kt.aes_t, a.rk, make_uint4(iv.x, iv.y, iv.z, bswap32(1u)));
-        lh = warp_gh_mul_global(be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull), a.kt.gh_pow2, lane);
         const unsigned long long d = static_cast<unsigned long long>(a.grid - 1 - blockIdx.x) *
                                          static_cast<unsigned long long>(span) + 2ull;
-        warp_lane_basis(warp_h_pow(a.kt.gh_pow2, d, lane), lane, uhi, ulo);
+        open_power(a.frame, a.kt.aes_t, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
     } else {
-        const uint32_t lb_lo = static_cast<uint32_t>(lane & 7) << 4;
-        const uint32_t lb_hi = 0x80u | lb_lo;
-        const uint32_t fsel = funnel_sel(a.load_r);
-        const int64_t rows = a.iters;
-        constexpr int64_t T = kHornerThreads;
-        constexpr uint64_t kRowBytes = static_cast<uint64_t>(T) * 16u;
-        Chains<R> ch;
-#pragma unroll
-        for (int k = 0; k < R; ++k) {
-            ch.q[k] = make_uint4(0, 0, 0, 0);
-        }
-
-        // Interior rows: blocks 1 <= i < P/16, so both aligned chunks of every
-        // block lie inside the frame and no checks are needed.
-        const int64_t n_full = static_cast<int64_t>(P / 16u);
-        const int64_t r_lo = base >= 1 ? 0 : (1 - base + T - 1) / T;
-        int64_t r_hi = (n_full - base) / T;
-        r_hi = r_hi > rows ? rows : r_hi;
-        int64_t r_a = (r_lo + R - 1) / R * R;
-        r_a = r_a > r_hi ? r_hi : r_a;
-        const int64_t ngroups = r_hi > r_a ? (r_hi - r_a) / R : 0;
-
-        auto generic_row = [&](int64_t r) __attribute__((always_inline)) {
-            const int64_t i = base + r * T + tid;
-            const uint4 c = ct_finish<LQ>(ct_prefetch<LQ>(a.frame, a.frame_len, i, P), a.frame, i, P, fsel);
-            chain_push_dyn<kOpenGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
-        };
-
-        int64_t r = 0;
-#pragma unroll 1
-        for (; r < r_a; ++r) {
-            generic_row(r);
-        }
-        if (ngroups > 0) {
-            const uint64_t i0 = static_cast<uint64_t>(base + r_a * T + tid);
-            const uint8_t* cp = a.frame + 13 + i0 * 16u;
-            if (LQ != 4) {
-                cp = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(cp) & ~static_cast<uintptr_t>(15));
-            }
-            uint4 pd[R], pe[R];
-#pragma unroll
-            for (int k = 0; k < R; ++k) {
-                pd[k] = *reinterpret_cast<const uint4*>(cp + k * kRowBytes);
-                pe[k] = LQ != 4 ? *reinterpret_cast<const uint4*>(cp + k * kRowBytes + 16) : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll 1
-            for (int64_t g = 0; g < ngroups; ++g) {
-                uint4 cd[R], ce[R];
-#pragma unroll
-                for (int k = 0; k < R; ++k) {
-                    cd[k] = pd[k];
-                    ce[k] = pe[k];
-                }
-                if (g + 1 < ngroups) {
-                    const uint8_t* nx = cp + R * kRowBytes;
-#pragma unroll
-                    for (int k = 0; k < R; ++k) {
-                        pd[k] = *reinterpret_cast<const uint4*>(nx + k * kRowBytes);
-                        pe[k] = LQ != 4 ? *reinterpret_cast<const uint4*>(nx + k * kRowBytes + 16) : make_uint4(0, 0, 0, 0);
-                    }
-                }
-#pragma unroll
-                for (int k = 0; k < R; ++k) {
-                    const CtRaw raw{cd[k], ce[k], true};
-                    ch.q[k] = xor4(gh_mul_rep<kOpenGh>(ch.q[k], lb_lo, lb_hi), ct_finish<LQ>(raw, a.frame, 0, P, fsel));
-                }
-                cp += R * kRowBytes;
-            }
-            r = r_a + R * ngroups;
-        }
-#pragma unroll 1
-        for (; r < rows; ++r) {
-            generic_row(r);
-        }
-        part[tid] = chains_combine<R>(ch, rows, reinterpret_cast<const uint4*>(smem + kOpenHt));
+        const OpenTile t{a.frame, a.frame_len, P,
+                         static_cast<int64_t>(a.nblocks) - static_cast<int64_t>(a.grid - blockIdx.x) * span,
+                         static_cast<int64_t>(a.iters), a.load_r};
+        part[tid] = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), tid, lane);
     }
     __syncthreads();
 
@@ -357,13 +154,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     if (warp == kPowerWarp) {
         unsigned long long shi, slo;
         if (cta_accumulate(a.slot, part[0], uhi, ulo, lane, a.grid, shi, slo) && lane == 0) {
-            const uint4 expect = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
-            const uint8_t* tag = a.frame + 13 + P;
-            uint32_t diff = 0;
-            for (int b = 0; b < 16; ++b) {
-                diff |= byte_of(expect, b) ^ static_cast<uint32_t>(tag[b]);
-            }
-            *a.auth_ok = (a.frame[0] == 1) & (diff == 0);
+            *a.auth_ok = open_verdict(a.frame, P, shi, slo, lh, ej0);
         }
     }
 }
@@ -387,129 +178,34 @@ __global__ void open_empty_kernel(const OpenArgs a)
 //
 // Reads *auth_ok (written by open_ghash_kernel earlier on the same stream).
 // Authentic: plaintext = ciphertext ^ keystream. Otherwise dst[0, P) is
-// zero-filled and no keystream is produced.
+// zero-filled and no keystream is produced. CTA c owns rows
+// [c R, (c+1) R) of kCtrThreads blocks (block i = row*T + thread).
 template <int LQ, bool PT_ALIGNED>
 __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_kernel(const CtrArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem[];
-    const uint64_t P = a.plen;
-    const int64_t n = a.nblocks;
     constexpr int64_t T = kCtrThreads;
-    constexpr uint64_t kRowBytes = static_cast<uint64_t>(T) * 16u;
     const int tid = threadIdx.x;
-    // CTA c owns rows [c*R, (c+1)*R) of T blocks (block i = row*T + tid).
     const int64_t row_begin = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta;
-    const int64_t rows_total = (n + T - 1) / T;
+    const int64_t rows_total = (static_cast<int64_t>(a.nblocks) + T - 1) / T;
     int64_t row_end = row_begin + a.rows_per_cta;
     row_end = row_end > rows_total ? rows_total : row_end;
     const int ok = *reinterpret_cast<const volatile int*>(a.auth_ok);
 
+    CtrTile t{a.frame, a.frame_len, a.dst, a.plen, row_begin * T, row_end - row_begin, {0u, 0u, 0u}, a.load_r};
     if (!ok) {
-        for (int64_t row = row_begin; row < row_end; ++row) {
-            const int64_t i = row * T + tid;
-            const int nb = block_bytes(i, P);
-            uint8_t* d = a.dst + static_cast<uint64_t>(i) * 16u;
-            if (PT_ALIGNED && nb == 16) {
-                *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
-            } else {
-                for (int b = 0; b < nb; ++b) {
-                    d[b] = 0;
-                }
-            }
-        }
+        ctr_zero_rows<PT_ALIGNED>(t, tid);
         return;
     }
 
     fill_aes_smem(smem, a.aes_t);
     __syncthreads();
 
-    const int lane = tid & 31;
-    uint32_t lb[4];
-    aes_lane_bases(lb, lane);
     const uint4 iv = load_bytes(a.frame + 1, 12);
-    const uint32_t s012[3] = {iv.x ^ a.rk[0], iv.y ^ a.rk[1], iv.z ^ a.rk[2]};
-    const uint32_t rk3x = bswap32(a.rk[3]);
-    const uint32_t fsel = funnel_sel(a.load_r);
-
-    auto store_pt = [&](int64_t i, uint4 p) __attribute__((always_inline)) {
-        const int nb = block_bytes(i, P);
-        uint8_t* d = a.dst + static_cast<uint64_t>(i) * 16u;
-        if (PT_ALIGNED && nb == 16) {
-            *reinterpret_cast<uint4*>(d) = p;
-        } else if (nb > 0) {
-            store_bytes(d, p, 0, nb);
-        }
-    };
-    auto generic_row = [&](int64_t row) __attribute__((always_inline)) {
-        const int64_t i = row * T + tid;
-        const uint4 c = ct_finish<LQ>(ct_prefetch<LQ>(a.frame, a.frame_len, i, P), a.frame, i, P, fsel);
-        uint32_t x[4] = {s012[0], s012[1], s012[2], bswap32(static_cast<uint32_t>(i) + 2u) ^ a.rk[3]};
-        aes_rounds_smem<0>(x, a.rk, lb);
-        store_pt(i, make_uint4(c.x ^ x[0], c.y ^ x[1], c.z ^ x[2], c.w ^ x[3]));
-    };
-
-    // Interior rows: 1 <= row (block 0's chunk may start before the frame)
-    // and every block full.
-    const int64_t n_full = static_cast<int64_t>(P / 16u);
-    int64_t r_lo = row_begin < 1 ? 1 : row_begin;
-    int64_t r_hi = n_full / T;
-    r_hi = r_hi > row_end ? row_end : r_hi;
-    if (r_lo > r_hi) {
-        r_lo = r_hi = row_end;
-    }
-    int64_t row = row_begin;
-#pragma unroll 1
-    for (; row < r_lo; ++row) {
-        generic_row(row);
-    }
-    const int64_t npair = (r_hi - r_lo) / 2;
-    if (npair > 0) {
-        const uint64_t i0 = static_cast<uint64_t>(r_lo * T + tid);
-        const uint8_t* cp = a.frame + 13 + i0 * 16u;
-        if (LQ != 4) {
-            cp = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(cp) & ~static_cast<uintptr_t>(15));
-        }
-        uint8_t* dp = a.dst + i0 * 16u;
-        uint32_t ctr = static_cast<uint32_t>(i0) + 2u;
-        CtrCache cc{0xffffffffu, 0u, {0u, 0u, 0u, 0u}};
-        uint4 pd0 = *reinterpret_cast<const uint4*>(cp);
-        uint4 pe0 = LQ != 4 ? *reinterpret_cast<const uint4*>(cp + 16) : make_uint4(0, 0, 0, 0);
-        uint4 pd1 = *reinterpret_cast<const uint4*>(cp + kRowBytes);
-        uint4 pe1 = LQ != 4 ? *reinterpret_cast<const uint4*>(cp + kRowBytes + 16) : make_uint4(0, 0, 0, 0);
-#pragma unroll 1
-        for (int64_t k = 0; k < npair; ++k) {
-            const CtRaw r0{pd0, pe0, true};
-            const CtRaw r1{pd1, pe1, true};
-            if (k + 1 < npair) {
-                const uint8_t* nx = cp + 2 * kRowBytes;
-                pd0 = *reinterpret_cast<const uint4*>(nx);
-                pe0 = LQ != 4 ? *reinterpret_cast<const uint4*>(nx + 16) : make_uint4(0, 0, 0, 0);
-                pd1 = *reinterpret_cast<const uint4*>(nx + kRowBytes);
-                pe1 = LQ != 4 ? *reinterpret_cast<const uint4*>(nx + kRowBytes + 16) : make_uint4(0, 0, 0, 0);
-            }
-            uint32_t x[4], y[4];
-            aes_ctr2_cached<0>(x, y, ctr, ctr + static_cast<uint32_t>(T), cc, s012, rk3x, a.rk, lb);
-            const uint4 c0 = ct_finish<LQ>(r0, a.frame, 0, P, fsel);
-            const uint4 c1 = ct_finish<LQ>(r1, a.frame, 0, P, fsel);
-            const uint4 p0 = make_uint4(c0.x ^ x[0], c0.y ^ x[1], c0.z ^ x[2], c0.w ^ x[3]);
-            const uint4 p1 = make_uint4(c1.x ^ y[0], c1.y ^ y[1], c1.z ^ y[2], c1.w ^ y[3]);
-            if (PT_ALIGNED) {
-                *reinterpret_cast<uint4*>(dp) = p0;
-                *reinterpret_cast<uint4*>(dp + kRowBytes) = p1;
-            } else {
-                store_bytes(dp, p0, 0, 16);
-                store_bytes(dp + kRowBytes, p1, 0, 16);
-            }
-            cp += 2 * kRowBytes;
-            dp += 2 * kRowBytes;
-            ctr += 2u * static_cast<uint32_t>(T);
-        }
-        row = r_lo + 2 * npair;
-    }
-#pragma unroll 1
-    for (; row < row_end; ++row) {
-        generic_row(row);
-    }
+    t.s012[0] = iv.x ^ a.rk[0];
+    t.s012[1] = iv.y ^ a.rk[1];
+    t.s012[2] = iv.z ^ a.rk[2];
+    ctr_rows<LQ, PT_ALIGNED>(t, a.rk, tid, tid & 31);
 }
 
 }  // namespace dev
@@ -624,6 +320,9 @@ cudaError_t configure_device(int device)
         chk(allow_smem(dev::open_ctr_kernel<2, false>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<3, false>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<4, false>, dev::kCtrSmem));
+        chk(allow_smem(dev::seal_batch_kernel, dev::kSealSmem));
+        chk(allow_smem(dev::open_ghash_batch_kernel, dev::kOpenSmem));
+        chk(allow_smem(dev::open_ctr_batch_kernel, dev::kCtrBatchSmem));
         // The hot loops address shared memory as (offset + kDynSmemBase) with
         // the base folded into the load instruction; check it on this device.
         if (e == cudaSuccess) {
@@ -961,6 +660,84 @@ extern "C" int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, co
         }
     }
     return cuda_rc(e);
+}
+
+// ========================================================= batched seal/open
+
+namespace {
+
+static_assert(sizeof(lmcache_gpu_aesgcm_batch_item) == sizeof(dev::BatchItem), "descriptor size");
+static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, auth_ok) == offsetof(dev::BatchItem, auth_ok),
+              "descriptor layout");
+static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, iv) == offsetof(dev::BatchItem, iv), "descriptor layout");
+static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, status) == offsetof(dev::BatchItem, status),
+              "descriptor layout");
+
+int batch_launch(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* items, size_t count,
+                 void* workspace, size_t workspace_bytes, void* stream_ptr, bool open)
+{
+    if (key == nullptr) {
+        return LMCACHE_GPU_AESGCM_ERR_ARGUMENT;
+    }
+    if (count == 0) {
+        return LMCACHE_GPU_AESGCM_OK;
+    }
+    if (items == nullptr || workspace == nullptr || count > dev::kBatchMaxItems ||
+        (reinterpret_cast<uintptr_t>(items) & 15u) != 0 || (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0 ||
+        workspace_bytes < dev::batch_workspace_bytes(count)) {
+        return LMCACHE_GPU_AESGCM_ERR_ARGUMENT;
+    }
+    auto* h = reinterpret_cast<KeyHandle*>(key);
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_ptr);
+    auto* d_items = reinterpret_cast<dev::BatchItem*>(items);
+    auto* ws = static_cast<uint8_t*>(workspace);
+    const int sms = h->num_sms < dev::kBatchMaxSms ? h->num_sms : dev::kBatchMaxSms;
+    dev::batch_plan_kernel<<<1, dev::kPlanThreads, 0, s>>>(d_items, static_cast<uint32_t>(count), ws, open ? 1 : 0,
+                                                           static_cast<uint32_t>(sms * dev::kBatchWaves));
+    if (cudaGetLastError() != cudaSuccess) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    dev::BatchArgs ba{};
+    ba.items = d_items;
+    ba.ws = ws;
+    ba.count = static_cast<uint32_t>(count);
+    std::memcpy(ba.rk, h->rk, sizeof(ba.rk));
+    ba.kt = h->kt;
+    if (!open) {
+        dev::seal_batch_kernel<<<h->num_sms, dev::kSealThreads, dev::kSealSmem, s>>>(ba);
+        return cuda_rc(cudaGetLastError());
+    }
+    dev::open_ghash_batch_kernel<<<h->num_sms, dev::kSealThreads, dev::kOpenSmem, s>>>(ba);
+    if (cudaGetLastError() != cudaSuccess) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    dev::open_ctr_batch_kernel<<<h->num_sms, dev::kCtrThreads, dev::kCtrBatchSmem, s>>>(ba);
+    return cuda_rc(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" size_t lmcache_gpu_aes128gcm_batch_workspace_size(size_t count)
+{
+    return count > dev::kBatchMaxItems ? 0 : dev::batch_workspace_bytes(count);
+}
+
+extern "C" int lmcache_gpu_aes128gcm_seal_batch_async(lmcache_gpu_aesgcm_key_t key,
+                                                      lmcache_gpu_aesgcm_batch_item* items, size_t count,
+                                                      void* workspace, size_t workspace_bytes, void* stream)
+{
+    return batch_launch(key, items, count, workspace, workspace_bytes, stream, false);
+}
+
+extern "C" int lmcache_gpu_aes128gcm_open_batch_async(lmcache_gpu_aesgcm_key_t key,
+                                                      lmcache_gpu_aesgcm_batch_item* items, size_t count,
+                                                      void* workspace, size_t workspace_bytes, void* stream)
+{
+    return batch_launch(key, items, count, workspace, workspace_bytes, stream, true);
 }
 
 // ===================================================== seal without allocation

@@ -64,12 +64,14 @@ static_assert(kSealSmem <= 227u * 1024u, "seal shared memory exceeds the per-blo
 // smem_base_probe_kernel once per device and refuses to run if it differs.
 constexpr uint32_t kDynSmemBase = 0x400;
 
-// Per-call accumulation slot (32 bytes). The last CTA of a call resets it.
+// Per-call accumulation slot (32 bytes). The last CTA of a call resets
+// acc_hi, acc_lo and ticket. Batched calls keep one slot per object and its
+// tile plan in aux: {J, G, authentication verdict}.
 struct Slot {
     unsigned long long acc_hi;
     unsigned long long acc_lo;
     unsigned int ticket;
-    unsigned int pad[3];
+    unsigned int aux[3];
 };
 
 struct KeyTables {

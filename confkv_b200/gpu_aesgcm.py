@@ -33,8 +33,55 @@ EXPORTED_SYMBOLS = (
 )
 
 
+# Entry points beyond the reference ABI (include/gpu_aesgcm_api.h marks each
+# as an extension): the seal that allocates nothing and batched seal/open.
+EXTENSION_SYMBOLS = (
+    "lmcache_gpu_aes128gcm_seal_noalloc",
+    "lmcache_gpu_aes128gcm_batch_workspace_size",
+    "lmcache_gpu_aes128gcm_seal_batch_async",
+    "lmcache_gpu_aes128gcm_open_batch_async",
+)
+
+
 class GpuAesGcmError(RuntimeError):
     pass
+
+
+class BatchItem(ctypes.Structure):
+    """lmcache_gpu_aesgcm_batch_item: one object of a batched seal/open.
+    Pointers are device addresses; `status` is written by the device."""
+
+    _fields_ = [
+        ("src", ctypes.c_uint64),
+        ("dst", ctypes.c_uint64),
+        ("plaintext_len", ctypes.c_uint64),
+        ("capacity", ctypes.c_uint64),
+        ("auth_ok", ctypes.c_uint64),
+        ("iv", ctypes.c_uint8 * IV_LEN),
+        ("status", ctypes.c_int32),
+        ("reserved", ctypes.c_uint64),
+    ]
+
+
+assert ctypes.sizeof(BatchItem) == 64
+
+
+def pack_batch_items(items) -> bytes:
+    """Descriptor bytes for a batch. `items` yields tuples
+    (src_ptr, dst_ptr, plaintext_len, capacity, auth_ok_ptr, iv) with iv 12
+    bytes (seal) or None (open) and auth_ok_ptr 0 for seal."""
+    items = list(items)
+    arr = (BatchItem * len(items))()
+    for k, (src, dst, plen, cap, auth, iv) in enumerate(items):
+        e = arr[k]
+        e.src, e.dst, e.plaintext_len, e.capacity, e.auth_ok = src, dst, plen, cap, auth
+        if iv is not None:
+            if len(iv) != IV_LEN:
+                raise ValueError("AES-GCM IV must be exactly 12 bytes")
+            ctypes.memmove(e.iv, bytes(iv), IV_LEN)
+        e.status = 0
+        e.reserved = 0
+    return bytes(arr)
 
 
 class GpuAesGcmLibrary:
@@ -73,6 +120,13 @@ class GpuAesGcmLibrary:
         lib.lmcache_gpu_aesgcm_strerror.argtypes = [c_int]
         lib.lmcache_gpu_aesgcm_strerror.restype = ctypes.c_char_p
 
+        lib.lmcache_gpu_aes128gcm_batch_workspace_size.argtypes = [c_size]
+        lib.lmcache_gpu_aes128gcm_batch_workspace_size.restype = c_size
+        for name in ("lmcache_gpu_aes128gcm_seal_batch_async", "lmcache_gpu_aes128gcm_open_batch_async"):
+            fn = getattr(lib, name)
+            fn.argtypes = [c_vp, c_vp, c_size, c_vp, c_size, c_vp]
+            fn.restype = c_int
+
     def frame_size(self, plaintext_len: int) -> int:
         if plaintext_len < 0:
             raise ValueError("plaintext_len must be non-negative")
@@ -83,6 +137,10 @@ class GpuAesGcmLibrary:
         if not p:
             return f"error {rc}"
         return p.decode("utf-8", errors="replace")
+
+    def batch_workspace_size(self, count: int) -> int:
+        """Device workspace bytes for a batch of `count` objects (0 = too many)."""
+        return int(self.lib.lmcache_gpu_aes128gcm_batch_workspace_size(count))
 
     def check(self, rc: int, operation: str) -> None:
         if rc == 0:
@@ -165,6 +223,24 @@ class GpuAes128GcmKey:
             ctypes.c_void_p(stream_ptr),
         )
         self.library.check(rc, "open_async")
+
+    def seal_batch_async(self, *, items_ptr: int, count: int, workspace_ptr: int, workspace_bytes: int,
+                         stream_ptr: int) -> None:
+        """Enqueue seal of `count` objects described by the device array at
+        items_ptr (pack_batch_items layout); per-object status on the device."""
+        rc = self.library.lib.lmcache_gpu_aes128gcm_seal_batch_async(
+            self._handle, ctypes.c_void_p(items_ptr), count, ctypes.c_void_p(workspace_ptr), workspace_bytes,
+            ctypes.c_void_p(stream_ptr))
+        self.library.check(rc, "seal_batch_async")
+
+    def open_batch_async(self, *, items_ptr: int, count: int, workspace_ptr: int, workspace_bytes: int,
+                         stream_ptr: int) -> None:
+        """Enqueue authentication-gated open of `count` frames; each object's
+        verdict goes to its auth_ok pointer."""
+        rc = self.library.lib.lmcache_gpu_aes128gcm_open_batch_async(
+            self._handle, ctypes.c_void_p(items_ptr), count, ctypes.c_void_p(workspace_ptr), workspace_bytes,
+            ctypes.c_void_p(stream_ptr))
+        self.library.check(rc, "open_batch_async")
 
     def close(self) -> None:
         if not self._handle.value:

@@ -11,6 +11,10 @@ Prints one JSON line per measurement:
   side stream overlapped with the next seal (the persistent-store path).
 * workloads: 64 x 2 MiB kv_small objects and 64 x 10 MiB Llama-3-70B TP-8
   KV-head shards (seal then open).
+* batches (--batch): the ragged workload (4096 objects, log-uniform 4 KiB ..
+  1 MiB, odd lengths, packed back to back), 8192 x 4 KiB and 32 x 32 MiB,
+  each sealed and opened once per object (seal_async / open_async) and once
+  per call (seal_batch / open_batch).
 
 All numbers are CUDA-event device times; GB/s counts plaintext bytes.
 """
@@ -89,17 +93,109 @@ def measure_batch(key: GpuAes128GcmKey, plain: torch.Tensor, reps: int, warmup: 
             "open_us_per_object": round(open_ms * 1e3 / count, 2)}
 
 
+def measure_batch_api(lib: GpuAesGcmLibrary, key: GpuAes128GcmKey, lens, seed: int, reps: int,
+                      warmup: int = 2) -> dict:
+    """Per-object calls vs one batched call over objects packed back to back
+    (plaintexts and frames at arbitrary byte offsets)."""
+    from .batch import DeviceBatch
+
+    dev = torch.device("cuda", key.device)
+    lens = [int(x) for x in lens]
+    pt_off, fr_off, p, f = [], [], 0, 0
+    for n in lens:
+        pt_off.append(p)
+        fr_off.append(f)
+        p += n
+        f += n + 29
+    g = torch.Generator(device=dev).manual_seed(seed)
+    plain = torch.randint(0, 256, (p + 16,), dtype=torch.uint8, device=dev, generator=g)
+    frames = torch.empty(f + 16, dtype=torch.uint8, device=dev)
+    out = torch.empty(p + 16, dtype=torch.uint8, device=dev)
+    auth = torch.zeros(len(lens), dtype=torch.int32, device=dev)
+    ivs = workloads.make_ivs(seed, len(lens))
+    s = torch.cuda.Stream(device=dev)
+    pb, fb, ob, ab = plain.data_ptr(), frames.data_ptr(), out.data_ptr(), auth.data_ptr()
+    seal_entries = [(pb + pt_off[i], fb + fr_off[i], n, n + 29, ivs[i]) for i, n in enumerate(lens)]
+    open_entries = [(fb + fr_off[i], ob + pt_off[i], n, n + 29, ab + 4 * i) for i, n in enumerate(lens)]
+    # one DeviceBatch per direction: descriptors are uploaded by the first
+    # (warm-up) call; the timed region is the batched launches alone
+    bseal = DeviceBatch(lib, len(lens), dev)
+    bopen = DeviceBatch(lib, len(lens), dev)
+
+    def per_object_seal():
+        for i, n in enumerate(lens):
+            key.seal_async(src_ptr=pb + pt_off[i], plaintext_len=n, dst_ptr=fb + fr_off[i], dst_capacity=n + 29,
+                           iv=ivs[i], stream_ptr=s.cuda_stream)
+
+    def per_object_open():
+        for i, n in enumerate(lens):
+            key.open_async(src_ptr=fb + fr_off[i], frame_len=n + 29, dst_ptr=ob + pt_off[i], plaintext_len=n,
+                           auth_ok_ptr=ab + 4 * i, stream_ptr=s.cuda_stream)
+
+    def batched(fn, b):
+        def run():
+            fn(items_ptr=b.items.data_ptr(), count=len(lens), workspace_ptr=b.workspace.data_ptr(),
+               workspace_bytes=b.workspace_bytes, stream_ptr=s.cuda_stream)
+        return run
+
+    def timed(body):
+        for _ in range(warmup):
+            body()
+        torch.cuda.synchronize(dev)
+        a, b = _events()
+        a.record(s)
+        for _ in range(reps):
+            body()
+        b.record(s)
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / reps
+
+    def check_open():
+        assert bool((auth == 1).all()) and torch.equal(out[:p], plain[:p]), "round trip failed"
+
+    r = {}
+
+    def record(name, ms):
+        r[name + "_gbs"] = round(sum(lens) / (ms * 1e-3) / 1e9, 2)
+        r[name + "_ms"] = round(ms, 4)
+
+    record("per_object_seal", timed(per_object_seal))
+    ref_frames = frames[:f].clone()
+    frames.zero_()
+    torch.cuda.synchronize(dev)   # default-stream work above, stream `s` below
+    bseal.seal(key, seal_entries, s)
+    record("batch_seal", timed(batched(key.seal_batch_async, bseal)))
+    assert torch.equal(frames[:f], ref_frames), "batched seal frames differ from per-object frames"
+    record("per_object_open", timed(per_object_open))
+    check_open()
+    out.zero_()
+    auth.zero_()
+    torch.cuda.synchronize(dev)
+    bopen.open(key, open_entries, s)
+    record("batch_open", timed(batched(key.open_batch_async, bopen)))
+    check_open()
+    return {"objects": len(lens), "bytes": sum(lens), **r}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--min-log2", type=int, default=12)
     ap.add_argument("--max-log2", type=int, default=30)
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--batch", action="store_true", help="only the batched-call comparison")
     args = ap.parse_args()
     torch.cuda.set_device(args.device)
     dev = torch.device("cuda", args.device)
     lib = GpuAesGcmLibrary()
     with GpuAes128GcmKey(lib, workloads.make_key(5), device=args.device) as key:
+        if args.batch:
+            ragged = workloads.ragged_case(4096, seed=3).lengths
+            for name, lens in (("ragged_4096", ragged), ("small_8192x4KiB", [4096] * 8192),
+                               ("kv_llama8b_32x32MiB", [32 << 20] * 32)):
+                r = measure_batch_api(lib, key, lens, seed=13, reps=args.reps)
+                print(json.dumps({"sweep": "batch", "workload": name, **r}), flush=True)
+            return
         for k in range(args.min_log2, args.max_log2 + 1):
             P = 1 << k
             count = max(4, min(4096, (64 << 20) // P))

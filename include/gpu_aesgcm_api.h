@@ -107,6 +107,48 @@ int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key_len, const
                                        size_t plaintext_len, void* dst, size_t dst_capacity,
                                        const uint8_t* iv, int device, void* stream);
 
+/*
+ * Batched seal / open. Extensions: no counterpart in the reference, whose
+ * callers enqueue one seal_async / open_async per object.
+ *
+ * One call covers `count` objects of any sizes (0 included) and alignments
+ * with a fixed number of launches (seal 2, open 3), so thousands of small
+ * objects cost one pass over the GPU instead of one launch sequence each.
+ * Frames, tags and open's gating are exactly those of seal_async/open_async.
+ *
+ * items: DEVICE array of `count` descriptors, 16-byte aligned. The device
+ *   checks each descriptor by the rules of seal_async / open_async and writes
+ *   its `status`: 0, or ERR_ARGUMENT, in which case that object is skipped
+ *   (nothing of it is written, its auth_ok included).
+ * workspace: DEVICE buffer, 16-byte aligned, at least
+ *   lmcache_gpu_aes128gcm_batch_workspace_size(count) bytes, any contents; the
+ *   call owns it until its work on `stream` completes (one call at a time).
+ * Host-side errors (null key/items/workspace, misalignment, a short
+ * workspace, count above 2^20) return ERR_ARGUMENT before any launch;
+ * count == 0 is a no-op.
+ */
+typedef struct lmcache_gpu_aesgcm_batch_item {
+    const void* src;          /* seal: plaintext; open: frame (DEVICE) */
+    void* dst;                /* seal: frame; open: plaintext (DEVICE) */
+    uint64_t plaintext_len;   /* P */
+    uint64_t capacity;        /* seal: dst capacity; open: frame length */
+    int* auth_ok;             /* open: DEVICE int, 1 = authentic, else 0; seal: unused */
+    uint8_t iv[12];           /* seal: the object's IV; open: unused (read from the frame) */
+    int32_t status;           /* written by the device */
+    uint64_t reserved;        /* set to 0 */
+} lmcache_gpu_aesgcm_batch_item;
+
+/* Workspace bytes for a batch of `count` objects; 0 when count > 2^20. */
+size_t lmcache_gpu_aes128gcm_batch_workspace_size(size_t count);
+
+int lmcache_gpu_aes128gcm_seal_batch_async(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* items,
+                                           size_t count, void* workspace, size_t workspace_bytes,
+                                           void* stream);
+
+int lmcache_gpu_aes128gcm_open_batch_async(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* items,
+                                           size_t count, void* workspace, size_t workspace_bytes,
+                                           void* stream);
+
 /* rc -> static string (reference gpu_aesgcm_api.h:90-92). */
 const char* lmcache_gpu_aesgcm_strerror(int rc);
 

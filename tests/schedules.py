@@ -1,0 +1,113 @@
+"""CPU replays of the kernels' index arithmetic (test infrastructure).
+
+Each function restates, line for line, one piece of confkv_b200/csrc:
+  tile rows    seal_rows / open_ghash_rows / ctr_rows (tiles.cuh): how a
+               tile's J rows split into generic edge rows and the check-free
+               interior loop;
+  grids        horner_grid and the open-CTR rows_per_cta split
+               (gpu_aesgcm.cu), which cut one object into tiles;
+  batch plan   batch_plan_kernel (batch.cuh): tile height J*, per-object
+               (J, G) and the tile queue order.
+The interior loops index memory without bounds checks, so these replays are
+their bounds proofs.
+"""
+
+from __future__ import annotations
+
+T = 512              # kHornerThreads == kCtrThreads
+SEAL_PAIR = 2        # rows per interior iteration of seal_rows
+OPEN_R = 2           # kOpenChains: rows per interior iteration of open_ghash_rows
+CTR_PAIR = 2
+BATCH_WAVES = 8      # kBatchWaves
+BATCH_MAX_SMS = 256  # kBatchMaxSms
+BATCH_EXTRA = BATCH_WAVES * BATCH_MAX_SMS
+
+
+def cdiv(a, b):
+    return -(-a // b)
+
+
+def _trunc_div(a, b):
+    """C++ integer division (truncates toward zero)."""
+    q = abs(a) // abs(b)
+    return q if (a >= 0) == (b > 0) else -q
+
+
+def seal_tile_rows(base, rows, P):
+    """(generic rows, interior rows) of seal_rows for a tile."""
+    n_full = P // 16
+    r_lo = 0 if base >= 0 else _trunc_div(-base + T - 1, T)
+    r_hi = min(_trunc_div(n_full - base, T), rows)
+    r_a = min(_trunc_div(r_lo + SEAL_PAIR - 1, SEAL_PAIR) * SEAL_PAIR, r_hi)
+    ngroups = _trunc_div(r_hi - r_a, SEAL_PAIR) if r_hi > r_a else 0
+    interior = list(range(r_a, r_a + SEAL_PAIR * ngroups))
+    generic = list(range(0, r_a)) + list(range(r_a + SEAL_PAIR * ngroups, rows))
+    return generic, interior
+
+
+def open_tile_rows(base, rows, P):
+    """(generic rows, interior rows) of open_ghash_rows for a tile."""
+    n_full = P // 16
+    r_lo = 0 if base >= 1 else _trunc_div(1 - base + T - 1, T)
+    r_hi = min(_trunc_div(n_full - base, T), rows)
+    r_a = min(_trunc_div(r_lo + OPEN_R - 1, OPEN_R) * OPEN_R, r_hi)
+    ngroups = _trunc_div(r_hi - r_a, OPEN_R) if r_hi > r_a else 0
+    interior = list(range(r_a, r_a + OPEN_R * ngroups))
+    generic = list(range(0, r_a)) + list(range(r_a + OPEN_R * ngroups, rows))
+    return generic, interior
+
+
+def ctr_tile_rows(base, rows, P):
+    """(generic rows, interior rows) of ctr_rows for a tile."""
+    n_full = P // 16
+    r_lo = 0 if base >= 1 else _trunc_div(1 - base + T - 1, T)
+    r_hi = min(_trunc_div(n_full - base, T), rows)
+    if r_lo > r_hi:
+        r_lo = r_hi = rows
+    npair = _trunc_div(r_hi - r_lo, CTR_PAIR)
+    interior = list(range(r_lo, r_lo + CTR_PAIR * npair))
+    generic = list(range(0, r_lo)) + list(range(r_lo + CTR_PAIR * npair, rows))
+    return generic, interior
+
+
+def horner_grid(n, sms):
+    j = max(1, cdiv(n, sms * T))
+    return j, cdiv(n, j * T)
+
+
+def ctr_grid(n, sms):
+    rows_total = cdiv(n, T)
+    per = cdiv(rows_total, sms)
+    return per, cdiv(rows_total, per)
+
+
+def tile_base(n, J, G, c):
+    """First block of tile c of G (J rows each), tiles aligned to the end."""
+    return n - (G - c) * J * T
+
+
+def batch_plan(lens, sms, valid=None):
+    """batch_plan_kernel: returns (jstar, [(J, G) or None per object], queue)
+    where the queue lists (object, tile) in device order up to the order
+    inside one bucket (the device fills a bucket with atomics)."""
+    count = len(lens)
+    valid = valid if valid is not None else [True] * count
+    rows = []
+    for P, ok in zip(lens, valid):
+        n = cdiv(P, 16)
+        rows.append((1 if n == 0 else cdiv(n, T)) if ok else 0)
+    sms_waves = min(sms, BATCH_MAX_SMS) * BATCH_WAVES
+    jstar = max(1, cdiv(sum(rows), sms_waves))
+    plan = []
+    buckets = {}
+    for i, (P, r) in enumerate(zip(lens, rows)):
+        if r == 0:
+            plan.append(None)
+            continue
+        J = min(r, jstar)
+        n = cdiv(P, 16)
+        G = max(1, cdiv(n, J * T))
+        plan.append((J, G))
+        buckets.setdefault(J.bit_length() - 1, []).extend((i, c) for c in range(G))
+    queue = [t for b in sorted(buckets, reverse=True) for t in buckets[b]]
+    return jstar, plan, queue

@@ -11,7 +11,7 @@ from pathlib import Path
 
 import pytest
 
-from confkv_b200.gpu_aesgcm import EXPORTED_SYMBOLS, FRAME_OVERHEAD
+from confkv_b200.gpu_aesgcm import EXPORTED_SYMBOLS, EXTENSION_SYMBOLS, FRAME_OVERHEAD
 
 HEADER = Path(__file__).resolve().parents[1] / "include" / "gpu_aesgcm_api.h"
 
@@ -28,8 +28,10 @@ NOALLOC_SYMBOL = "lmcache_gpu_aes128gcm_seal_noalloc"
 
 
 def test_header_declares_the_reference_abi():
-    # the reference's seven entry points plus the seal that allocates nothing
-    assert header_functions() == set(EXPORTED_SYMBOLS) | {NOALLOC_SYMBOL}
+    # the reference's seven entry points plus the extensions (the seal that
+    # allocates nothing, batched seal/open)
+    assert NOALLOC_SYMBOL in EXTENSION_SYMBOLS
+    assert header_functions() == set(EXPORTED_SYMBOLS) | set(EXTENSION_SYMBOLS)
 
 
 def test_library_exports_every_header_symbol(cpu_lib):
@@ -124,6 +126,44 @@ def test_seal_noalloc_argument_errors(cpu_lib):
     assert f(key, 16, p, 16, p, 44, iv, 0, None) == ERR_ARG
     assert f(key, 16, p, (1 << 30) + 1, p, (1 << 30) + 30, iv, 0, None) == ERR_ARG
     assert f(key, 16, p, 16, p, 45, iv, -1, None) == ERR_ARG
+
+
+def test_batch_workspace_size(cpu_lib):
+    ws = cpu_lib.batch_workspace_size
+    # header 256 B, one 32-B slot per object (rounded to 256 B), 8-B tile
+    # records for count + 2048 tiles
+    for count in (1, 7, 8, 9, 4096, 1 << 20):
+        assert ws(count) == 256 + (count * 32 + 255) // 256 * 256 + (count + 2048) * 8
+    assert ws((1 << 20) + 1) == 0
+
+
+def test_batch_argument_errors(cpu_lib):
+    lib = cpu_lib.lib
+    p = ctypes.c_void_p(0x2000)
+    for f in (lib.lmcache_gpu_aes128gcm_seal_batch_async, lib.lmcache_gpu_aes128gcm_open_batch_async):
+        need = cpu_lib.batch_workspace_size(4)
+        assert f(None, p, 4, p, need, None) == ERR_ARG
+        assert f(FAKE_HANDLE, p, 0, None, 0, None) == OK           # empty batch: no-op
+        assert f(FAKE_HANDLE, None, 4, p, need, None) == ERR_ARG
+        assert f(FAKE_HANDLE, p, 4, None, need, None) == ERR_ARG
+        assert f(FAKE_HANDLE, p, 4, p, need - 1, None) == ERR_ARG  # short workspace
+        assert f(FAKE_HANDLE, ctypes.c_void_p(0x2008), 4, p, need, None) == ERR_ARG  # items not 16-B aligned
+        assert f(FAKE_HANDLE, p, 4, ctypes.c_void_p(0x2004), need, None) == ERR_ARG  # workspace not 16-B aligned
+        assert f(FAKE_HANDLE, p, (1 << 20) + 1, p, 1 << 40, None) == ERR_ARG
+
+
+def test_batch_item_layout():
+    from confkv_b200.gpu_aesgcm import BatchItem, pack_batch_items
+
+    assert ctypes.sizeof(BatchItem) == 64
+    offs = {name: getattr(BatchItem, name).offset for name, _ in BatchItem._fields_}
+    assert offs == {"src": 0, "dst": 8, "plaintext_len": 16, "capacity": 24, "auth_ok": 32, "iv": 40,
+                    "status": 52, "reserved": 56}
+    raw = pack_batch_items([(1, 2, 3, 32, 0, bytes(range(12))), (5, 6, 7, 36, 0x99, None)])
+    assert len(raw) == 128
+    assert raw[40:52] == bytes(range(12)) and raw[64 + 32] == 0x99 and raw[64 + 40:64 + 52] == bytes(12)
+    with pytest.raises(ValueError):
+        pack_batch_items([(1, 2, 3, 32, 0, b"short")])
 
 
 def test_binding_rejects_bad_lengths(cpu_lib):
