@@ -45,11 +45,13 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
     const int lane = tid & 31;
     const int warp = tid >> 5;
 
+    pdl_release();
     fill_aes_smem(smem + kSealAes, a.kt.aes_t);
     fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
     for (int i = threadIdx.x; i < kSealFoldSmemLevels * 512; i += blockDim.x) {
         reinterpret_cast<uint4*>(smem + kSealFold)[i] = __ldg(a.kt.gh_pow2 + i);
     }
+    pdl_wait();
     if (blockIdx.x == 0 && tid == 0) {
         a.frame[0] = 1;
         for (int b = 0; b < 12; ++b) {
@@ -95,6 +97,8 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
 // Zero-length seal: header + tag = E_K(J0) (GHASH of nothing is 0).
 __global__ void seal_empty_kernel(const SealArgs a)
 {
+    pdl_release();
+    pdl_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) {
         return;
     }
@@ -124,10 +128,12 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     const int lane = tid & 31;
     const int warp = tid >> 5;
 
+    pdl_release();
     fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
     for (int i = threadIdx.x; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
         reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);  // H^(2^l), l <= kHornerLog2
     }
+    pdl_wait();
     __syncthreads();
 
     const uint64_t P = a.plen;
@@ -162,6 +168,8 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
 // Zero-length open: only the version byte and tag = E_K(J0) to check.
 __global__ void open_empty_kernel(const OpenArgs a)
 {
+    pdl_release();
+    pdl_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) {
         return;
     }
@@ -190,15 +198,16 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_kernel(const CtrArgs 
     const int64_t rows_total = (static_cast<int64_t>(a.nblocks) + T - 1) / T;
     int64_t row_end = row_begin + a.rows_per_cta;
     row_end = row_end > rows_total ? rows_total : row_end;
-    const int ok = *reinterpret_cast<const volatile int*>(a.auth_ok);
 
+    pdl_release();
+    fill_aes_smem(smem, a.aes_t);
+    pdl_wait();
+    const int ok = *reinterpret_cast<const volatile int*>(a.auth_ok);
     CtrTile t{a.frame, a.frame_len, a.dst, a.plen, row_begin * T, row_end - row_begin, {0u, 0u, 0u}, a.load_r};
     if (!ok) {
         ctr_zero_rows<PT_ALIGNED>(t, tid);
         return;
     }
-
-    fill_aes_smem(smem, a.aes_t);
     __syncthreads();
 
     const uint4 iv = load_bytes(a.frame + 1, 12);
@@ -369,25 +378,41 @@ dev::Slot* take_slot(KeyHandle* h)
     return h->slots + (h->next_slot.fetch_add(1, std::memory_order_relaxed) % kSlots);
 }
 
+// Launch with programmatic stream serialization (see pdl_release/pdl_wait):
+// the kernel may start while the previous kernel on the stream drains.
+template <class Arg>
+cudaError_t launch_pdl(void (*kernel)(Arg), uint32_t grid, uint32_t block, uint32_t smem, cudaStream_t s,
+                       const Arg& arg)
+{
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, arg);
+}
+
 template <int SQ, bool A>
 cudaError_t launch_seal_t(const dev::SealArgs& args, cudaStream_t s)
 {
-    dev::seal_kernel<SQ, A><<<args.grid, dev::kSealThreads, dev::kSealSmem, s>>>(args);
-    return cudaGetLastError();
+    return launch_pdl(dev::seal_kernel<SQ, A>, args.grid, dev::kSealThreads, dev::kSealSmem, s, args);
 }
 
 template <int LQ>
 cudaError_t launch_open_ghash_t(const dev::OpenArgs& args, cudaStream_t s)
 {
-    dev::open_ghash_kernel<LQ><<<args.grid, dev::kSealThreads, dev::kOpenSmem, s>>>(args);
-    return cudaGetLastError();
+    return launch_pdl(dev::open_ghash_kernel<LQ>, args.grid, dev::kSealThreads, dev::kOpenSmem, s, args);
 }
 
 template <int LQ, bool A>
 cudaError_t launch_open_ctr_t(const dev::CtrArgs& args, uint32_t grid, cudaStream_t s)
 {
-    dev::open_ctr_kernel<LQ, A><<<grid, dev::kCtrThreads, dev::kCtrSmem, s>>>(args);
-    return cudaGetLastError();
+    return launch_pdl(dev::open_ctr_kernel<LQ, A>, grid, dev::kCtrThreads, dev::kCtrSmem, s, args);
 }
 
 }  // namespace
@@ -535,8 +560,7 @@ extern "C" int lmcache_gpu_aes128gcm_seal_async(lmcache_gpu_aesgcm_key_t key, co
 
     if (n == 0) {
         args.grid = 1;
-        dev::seal_empty_kernel<<<1, 32, 0, s>>>(args);
-        return cuda_rc(cudaGetLastError());
+        return cuda_rc(launch_pdl(dev::seal_empty_kernel, 1, 32, 0, s, args));
     }
     horner_grid(n, h->num_sms, args.iters, args.grid);
     args.slot = take_slot(h);
@@ -603,8 +627,7 @@ extern "C" int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, co
     oa.auth_ok = auth_ok;
 
     if (n == 0) {
-        dev::open_empty_kernel<<<1, 32, 0, s>>>(oa);
-        return cuda_rc(cudaGetLastError());
+        return cuda_rc(launch_pdl(dev::open_empty_kernel, 1, 32, 0, s, oa));
     }
     horner_grid(n, h->num_sms, oa.iters, oa.grid);
     oa.slot = take_slot(h);

@@ -120,6 +120,27 @@ struct CtrArgs {
     const int* auth_ok;
 };
 
+// ------------------------------------------------ programmatic dependent launch
+//
+// The single-object kernels are launched with programmatic stream
+// serialization: pdl_release() at the top of every CTA lets the next kernel
+// on the stream launch once all of this grid's CTAs run, so its CTAs take
+// SMs as this grid's CTAs exit and fill their shared tables (key tables
+// only, written once by key_create) while this grid drains. Every access to
+// memory another kernel of the stream may read or write -- objects, frames,
+// slots, auth_ok -- comes after pdl_wait(), which returns once the previous
+// grid has completed and its writes are visible (at once when there is no
+// programmatic predecessor).
+__device__ __forceinline__ void pdl_wait()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_release()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- helpers
 
 __device__ __forceinline__ uint32_t bswap32(uint32_t x)
