@@ -6,9 +6,13 @@ One step = seal a batch of 32 KV objects [2, 32 layers, 256 tokens, 8 KV heads,
 [1 | IV | ct | tag], then open all 32 frames with tag verification. Each GPU
 (one process per GPU under torchrun) seals its own 32 objects: no collective
 on the data path, weak scaling. value = plaintext bytes sealed + opened by all
-ranks / max-over-ranks device time.
+ranks / max-over-ranks device time, through one batched seal call and one
+batched open call per step; the same step through one seal_async / open_async
+call per object (the reference's C-ABI) is reported beside it ("per_object"),
+and e2e (host buffers, copies timed) goes through the per-object calls.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--api both|batched|per_object]
 
 --impl reference times the reference's own OpenSSL CPU backend
 (lmcache_aes128gcm_seal/open from oracle/_ref/libcpu_seal.so) on the host
@@ -48,6 +52,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--api", choices=["both", "batched", "per_object"], default="both",
+                    help="both: value from the batched calls, per-object calls reported beside it")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling runs)")
     ap.add_argument("--objects", type=int, default=OBJECTS, help="objects per GPU per step (profiling runs)")
     ap.add_argument("--cpu-sample-objects", type=int, default=0,
@@ -71,18 +77,21 @@ def load_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-def profile_traffic(name: str):
-    """Per-launch DRAM bytes from a committed ncu summary, if present."""
+def profile_summary(name: str) -> dict:
+    """`key: number` lines of a committed ncu summary under profiles/
+    (dram_bytes_per_launch, wavefronts_per_block), if present."""
     p = ROOT / "profiles" / name
+    out = {}
     if not p.exists():
-        return None
+        return out
     for line in p.read_text().splitlines():
-        if line.startswith("dram_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
+        for k in ("dram_bytes_per_launch", "wavefronts_per_block"):
+            if line.startswith(k + ":"):
+                try:
+                    out[k] = float(line.split(":", 1)[1].strip().split()[0])
+                except ValueError:
+                    pass
+    return out
 
 
 class ClockSampler:
@@ -139,6 +148,7 @@ def run_ours(args, rank, world, local):
     import torch
 
     from confkv_b200 import build, workloads
+    from confkv_b200.batch import DeviceBatch
     from confkv_b200.gpu_aesgcm import GpuAes128GcmKey, GpuAesGcmLibrary
 
     torch.cuda.set_device(local)
@@ -172,84 +182,122 @@ def run_ours(args, rank, world, local):
     stream = torch.cuda.Stream(device=dev)
     sp = stream.cuda_stream
 
-    def seal_all():
+    # per-object calls: the reference's C-ABI, one seal_async / open_async each
+    def seal_each():
         for k in range(nobj):
             key.seal_async(src_ptr=plain_u8[k].data_ptr(), plaintext_len=P, dst_ptr=frames[k].data_ptr(),
                            dst_capacity=stride, iv=ivs[k], stream_ptr=sp)
 
-    def open_all():
+    def open_each():
         for k in range(nobj):
             key.open_async(src_ptr=frames[k].data_ptr(), frame_len=frame_len, dst_ptr=opened[k].data_ptr(),
                            plaintext_len=P, auth_ok_ptr=auth[k:k + 1].data_ptr(), stream_ptr=sp)
+
+    # batched calls: one seal_batch_async / open_batch_async per step over the
+    # same objects; the descriptor arrays are device-resident like the inputs
+    bseal = DeviceBatch(lib, nobj, dev)
+    bopen = DeviceBatch(lib, nobj, dev)
+    bseal.seal(key, [(plain_u8[k].data_ptr(), frames[k].data_ptr(), P, stride, ivs[k]) for k in range(nobj)], stream)
+    bopen.open(key, [(frames[k].data_ptr(), opened[k].data_ptr(), P, frame_len, auth.data_ptr() + 4 * k)
+                     for k in range(nobj)], stream)
+
+    def seal_batched():
+        key.seal_batch_async(items_ptr=bseal.items.data_ptr(), count=nobj, workspace_ptr=bseal.workspace.data_ptr(),
+                             workspace_bytes=bseal.workspace_bytes, stream_ptr=sp)
+
+    def open_batched():
+        key.open_batch_async(items_ptr=bopen.items.data_ptr(), count=nobj, workspace_ptr=bopen.workspace.data_ptr(),
+                             workspace_bytes=bopen.workspace_bytes, stream_ptr=sp)
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
-        seal_all()
-        open_all()
-    barrier()
-    assert bool((auth == 1).all()), "warm-up open failed authentication"
-    assert torch.equal(opened, plain_u8), "warm-up round trip mismatch"
+    def measure(seal_fn, open_fn):
+        """W warm-up steps, then K steps timed with events on the launching
+        stream; checks every object's round trip afterwards."""
+        opened.zero_()
+        auth.zero_()
+        barrier()
+        for _ in range(args.warmup):
+            seal_fn()
+            open_fn()
+        barrier()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        barrier()
+        with torch.cuda.stream(stream):
+            for s in range(args.steps):
+                ev[s][0].record(stream)
+                seal_fn()
+                ev[s][1].record(stream)
+                open_fn()
+                ev[s][2].record(stream)
+        barrier()
+        seal_ms = [e[0].elapsed_time(e[1]) for e in ev]
+        open_ms = [e[1].elapsed_time(e[2]) for e in ev]
+        ok = bool((auth == 1).all()) and torch.equal(opened, plain_u8)
+        return seal_ms, open_ms, ok
 
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    from confkv_b200 import multigpu
+
+    apis = ["batched", "per_object"] if args.api == "both" else [args.api]
     clocks = ClockSampler(local)
     clocks.start()
-    barrier()
-    with torch.cuda.stream(stream):
-        for s in range(args.steps):
-            ev[s][0].record(stream)
-            seal_all()
-            ev[s][1].record(stream)
-            open_all()
-            ev[s][2].record(stream)
-    barrier()
+    results = {}
+    for api in apis:
+        seal_ms, open_ms, ok = measure(seal_batched, open_batched) if api == "batched" else \
+            measure(seal_each, open_each)
+        tot, ssum, osum = multigpu.reduce_max([sum(a + b for a, b in zip(seal_ms, open_ms)), sum(seal_ms),
+                                               sum(open_ms)], device=dev)
+        results[api] = (tot, ssum, osum, multigpu.all_ok(ok, device=dev))
     clk = clocks.stop()
-    seal_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    open_ms = [e[1].elapsed_time(e[2]) for e in ev]
-    total_ms = sum(a + b for a, b in zip(seal_ms, open_ms))
-    ok = bool((auth == 1).all()) and torch.equal(opened, plain_u8)
 
     # e2e through the public API: pinned host plaintext -> H2D -> seal -> D2H
     # frames, then open -> D2H auth flags; copies overlapped across objects.
     e2e = {"ms": float("nan"), "gbs": float("nan"), "h2d": 0, "d2h": 0} if args.no_e2e else \
         run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args)
-
-    from confkv_b200 import multigpu
-
-    total_ms, seal_sum, open_sum, e2e_ms = multigpu.reduce_max(
-        [total_ms, sum(seal_ms), sum(open_ms), e2e["ms"]], device=dev)
-    ok = multigpu.all_ok(ok, device=dev)
+    (e2e_ms,) = multigpu.reduce_max([e2e["ms"]], device=dev)
 
     if rank == 0:
+        head = apis[0]
+        total_ms, seal_sum, open_sum, ok = results[head]
         bytes_per_step = 2 * nobj * P * world  # sealed + opened plaintext, all ranks
+
+        def gbs(ms_sum, nbytes):
+            return nbytes / (ms_sum / args.steps * 1e-3) / 1e9
+
         ms_per_step = total_ms / args.steps
-        value = bytes_per_step / (ms_per_step * 1e-3) / 1e9
-        seal_gbs = nobj * P * world / (seal_sum / args.steps * 1e-3) / 1e9
-        open_gbs = nobj * P * world / (open_sum / args.steps * 1e-3) / 1e9
+        value = gbs(total_ms, bytes_per_step)
         peak, peak_kind = load_peaks()
-        # dominant kernel: seal_kernel, one launch per object; algorithmic
-        # bytes = read P + write P + 29.
-        seal_launch_ms = seal_sum / args.steps / nobj
-        achieved = (2 * P + 29) / (seal_launch_ms * 1e-3) / 1e9
-        traffic = profile_traffic("seal_kernel_kv_llama8b.txt")  # DRAM bytes per launch (ncu)
+        launches_per_step = (2 + 3) if head == "batched" else 3 * nobj
+        # Dominant kernel: the seal kernel. Batched: one seal_batch_kernel
+        # launch per step seals all nobj objects (the one-CTA plan kernel in
+        # the same timed call is a few microseconds); per object: one
+        # seal_kernel launch per object. Algorithmic bytes per object = read
+        # P + write P + 29.
+        kernel = "seal_batch_kernel" if head == "batched" else "seal_kernel"
+        objs_per_launch = nobj if head == "batched" else 1
+        launch_ms = seal_sum / args.steps / (1 if head == "batched" else nobj)
+        achieved = objs_per_launch * (2 * P + 29) / (launch_ms * 1e-3) / 1e9
+        prof = profile_summary(f"{kernel}_kv_llama8b.txt")
+        traffic = prof.get("dram_bytes_per_launch")
         # The path is integer/LSU-bound, not HBM-bound. Two further bounds:
         # (1) the canonical AES+GHASH integer-op count (1162 two-input ops per
         #     16-B block: bitsliced AES 758 + CTR xor 4 + Karatsuba GHASH 400)
         #     at the measured LOP3 issue rate of this GPU (64 lanes / SM /
         #     clock, microbenchmarked) and the clock sampled during the run;
         # (2) the measured binding unit, the L1 data-pipe wavefront rate (1 per
-        #     SM per clock) at the seal kernel's 9.02 wavefronts per block
-        #     (profiles/seal_kernel_kv_llama8b.txt).
+        #     SM per clock) at the kernel's wavefronts per block (ncu summary
+        #     under profiles/).
+        wpb = prof.get("wavefronts_per_block", 9.02)
         sm_hz = (clk["sm_mhz"] if clk else 1965.0) * 1e6
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
-        blocks_per_s = (P / 16) / (seal_launch_ms * 1e-3)
+        seal_gbs_dev = objs_per_launch * P / (launch_ms * 1e-3) / 1e9
+        blocks_per_s = seal_gbs_dev * 1e9 / 16
         int_peak = 64 * n_sm * sm_hz
         int_ach = blocks_per_s * 1162
-        lsu_ceiling_gbs = n_sm * sm_hz / 9.02 * 16 / 1e9
-        seal_gbs_one = P / (seal_launch_ms * 1e-3) / 1e9
+        lsu_ceiling_gbs = n_sm * sm_hz / wpb * 16 / 1e9
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -264,33 +312,44 @@ def run_ours(args, rank, world, local):
             "dtype": "u8",
             "data": "synthetic: bf16 N(0,1) KV chunks from fixed seeds, resident in HBM",
             "config": {"workload": WORKLOAD, "objects_per_gpu": nobj, "object_shape": list(SHAPE),
-                       "object_bytes": P, "step": "seal 32 objects then open 32 frames with tag check",
+                       "object_bytes": P, "step": f"seal {nobj} objects then open {nobj} frames with tag check",
+                       "api": ("one seal_batch_async + one open_batch_async call per step" if head == "batched"
+                               else "one seal_async + one open_async call per object"),
                        "l2": "inputs larger than L2 (1 GiB plaintext per GPU)",
                        "parallelism": f"independent objects per GPU x{world}, no collective"},
-            "seal_gbs": round(seal_gbs, 2),
-            "open_gbs": round(open_gbs, 2),
+            "seal_gbs": round(gbs(seal_sum, nobj * P * world), 2),
+            "open_gbs": round(gbs(open_sum, nobj * P * world), 2),
             "round_trip_ok": ok,
-            "roofline": {"bound": "hbm", "kernel": "seal_kernel", "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                         "algorithmic_bytes_per_launch": 2 * P + 29,
+                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s",
+                         "algorithmic_bytes_per_launch": objs_per_launch * (2 * P + 29),
                          "traffic": traffic},
-            "int_roofline": {"bound": "int", "kernel": "seal_kernel", "ops_per_block": 1162,
+            "int_roofline": {"bound": "int", "kernel": kernel, "ops_per_block": 1162,
                              "achieved": round(int_ach / 1e12, 3), "peak": round(int_peak / 1e12, 3),
                              "unit": "Tops/s", "frac": round(int_ach / int_peak, 3),
                              "peak_source": "measured LOP3 rate 64 lanes/SM/clk x SMs x sampled SM clock"},
-            "lsu_roofline": {"bound": "l1_wavefronts", "kernel": "seal_kernel", "wavefronts_per_block": 9.02,
+            "lsu_roofline": {"bound": "l1_wavefronts", "kernel": kernel, "wavefronts_per_block": wpb,
                              "ceiling_plaintext_gbs": round(lsu_ceiling_gbs, 1),
-                             "achieved_plaintext_gbs": round(seal_gbs_one, 1),
-                             "frac": round(seal_gbs_one / lsu_ceiling_gbs, 3)},
+                             "achieved_plaintext_gbs": round(seal_gbs_dev, 1),
+                             "frac": round(seal_gbs_dev / lsu_ceiling_gbs, 3)},
             "e2e": {"value": round(e2e["gbs"] * world, 2) if world == 1 else
                     round(2 * nobj * P * world / (e2e_ms * 1e-3) / 1e9, 2),
                     "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                    "what": "pinned host plaintext -> H2D -> seal -> D2H frames; open -> D2H auth; "
+                    "what": "pinned host plaintext -> H2D -> seal_async -> D2H frames; open_async -> D2H auth; "
                             "copies overlapped across objects on three streams"},
-            "gpu_launches": 3 * nobj * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if "per_object" in results and head != "per_object":
+            t, ss, os_, okp = results["per_object"]
+            line["per_object"] = {"value": round(gbs(t, bytes_per_step), 2),
+                                  "ms_per_step": round(t / args.steps, 4),
+                                  "seal_gbs": round(gbs(ss, nobj * P * world), 2),
+                                  "open_gbs": round(gbs(os_, nobj * P * world), 2),
+                                  "round_trip_ok": okp, "gpu_launches": 3 * nobj * args.steps,
+                                  "api": "one seal_async + one open_async call per object (reference C-ABI)"}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args)
         print(json.dumps(line), flush=True)
