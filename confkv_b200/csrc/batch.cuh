@@ -2,8 +2,9 @@
 // persistent launches for any number of objects of any sizes and alignments.
 //
 //   batch_plan_kernel    one CTA: validates every descriptor (status), sums
-//                        the rows, picks the tile height J* so the batch has
-//                        about kBatchWaves tiles per SM, gives object i
+//                        the rows, picks the tile height J* by scoring 16
+//                        candidates (1..8 tiles per SM, the tallest object
+//                        in 1..8 equal tiles) with a makespan model, gives object i
 //                        J_i = min(J*, rows_i) and G_i = ceil(n_i / (J_i T))
 //                        tiles, and writes the tile records (object, tile)
 //                        with taller tiles first, so the queue's tail holds
@@ -39,7 +40,12 @@ struct BatchItem {
 };
 static_assert(sizeof(BatchItem) == 64, "batch descriptor is 64 bytes");
 
-constexpr int kBatchWaves = 8;        // target tiles per SM
+constexpr int kBatchWaves = 8;        // most tiles per SM the plan considers
+constexpr int kPlanCandidates = 16;   // tile heights the plan scores
+// Fixed work per tile (fold, tag or verdict, table refill, queue and
+// descriptor fetch) in units of one row of the seal loop, as measured on
+// B200: about 8-10 us per tile against ~2.5 us per 8 KiB row per SM.
+constexpr double kTileOverheadRows = 4.0;
 constexpr int kBatchMaxSms = 256;     // SMs counted for the tile bound
 constexpr uint32_t kBatchExtraTiles = static_cast<uint32_t>(kBatchWaves * kBatchMaxSms);
 constexpr uint32_t kBatchMaxItems = 1u << 20;
@@ -82,27 +88,35 @@ struct BatchArgs {
 // ------------------------------------------------------------------ plan
 
 // `open` selects the descriptor rules: seal needs capacity >= P + 29; open
-// needs frame length >= P + 29 and an auth_ok pointer. sms_waves = tiles the
-// batch should have when it is large (SMs x kBatchWaves).
+// needs frame length >= P + 29 and an auth_ok pointer. sms = SMs the work
+// kernels run on (at most kBatchMaxSms).
 __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* items, uint32_t count,
-                                                                  uint8_t* ws, int open, uint32_t sms_waves)
+                                                                  uint8_t* ws, int open, uint32_t sms)
 {
     __shared__ unsigned long long red[kPlanThreads / 32];
+    __shared__ uint32_t red_max[kPlanThreads / 32];
     __shared__ unsigned int hist[kBuckets];
     __shared__ unsigned int cursor[kBuckets];
     __shared__ unsigned long long total_rows;
+    __shared__ uint32_t max_rows;
+    __shared__ uint32_t cand[kPlanCandidates];
+    __shared__ unsigned long long cand_tiles[kPlanCandidates];
+    __shared__ uint32_t jstar_s;
     BatchHeader* hdr = reinterpret_cast<BatchHeader*>(ws);
     Slot* st = reinterpret_cast<Slot*>(ws + batch_slots_offset());
     TileRec* rec = reinterpret_cast<TileRec*>(ws + batch_tiles_offset(count));
     const int tid = threadIdx.x;
     constexpr uint64_t T = kHornerThreads;
+    pdl_release();
     if (tid < kBuckets) {
         hist[tid] = 0;
     }
+    pdl_wait();  // descriptors and workspace may belong to earlier work on the stream
 
     // Pass 1: validate, rows per object (a zero-length object is one row:
     // its tile writes the header and tag), reset the slot.
     unsigned long long rows_sum = 0;
+    uint32_t rows_max = 0;
     for (uint32_t i = tid; i < count; i += kPlanThreads) {
         BatchItem& it = items[i];
         const uint64_t P = it.plen;
@@ -121,29 +135,100 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         s.aux[1] = 0;
         s.aux[2] = 0;
         rows_sum += rows;
+        rows_max = rows > rows_max ? rows : rows_max;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
         rows_sum += __shfl_xor_sync(0xffffffffu, rows_sum, o);
+        const uint32_t m = __shfl_xor_sync(0xffffffffu, rows_max, o);
+        rows_max = m > rows_max ? m : rows_max;
     }
     if ((tid & 31) == 0) {
         red[tid >> 5] = rows_sum;
+        red_max[tid >> 5] = rows_max;
     }
     __syncthreads();
     if (tid < 32) {
         unsigned long long v = red[tid];
+        uint32_t m = red_max[tid];
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
             v += __shfl_xor_sync(0xffffffffu, v, o);
+            const uint32_t mo = __shfl_xor_sync(0xffffffffu, m, o);
+            m = mo > m ? mo : m;
         }
         if (tid == 0) {
             total_rows = v;
+            max_rows = m;
         }
     }
     __syncthreads();
-    unsigned long long js = (total_rows + sms_waves - 1) / sms_waves;
-    js = js < 1 ? 1 : js;
-    const uint32_t jstar = static_cast<uint32_t>(js > 0x7fffffffull ? 0x7fffffffull : js);
+
+    // Tile height J*. Candidates: the heights giving w = 1..8 tiles per SM
+    // (ceil(R / (w sms))) and the heights cutting the tallest object into
+    // k = 1..8 equal tiles (ceil(max_rows / k)). Each is scored by the
+    // makespan of equal tiles on `sms` SMs, ceil(tiles / sms) x (R / tiles +
+    // kTileOverheadRows), among those whose tile count fits the record area
+    // (the w = 8 height always does); ties go to the taller tile.
+    const unsigned long long R = total_rows;
+    if (tid < kPlanCandidates) {
+        unsigned long long j;
+        if (tid < 8) {
+            const unsigned long long slots = static_cast<unsigned long long>(tid + 1) * sms;
+            j = (R + slots - 1) / slots;
+        } else {
+            const uint32_t k = static_cast<uint32_t>(tid - 7);
+            j = (max_rows + k - 1) / k;
+        }
+        j = j > max_rows ? max_rows : j;
+        cand[tid] = static_cast<uint32_t>(j < 1 ? 1 : j);
+        cand_tiles[tid] = 0;
+    }
+    __syncthreads();
+    {
+        unsigned long long loc[kPlanCandidates];
+#pragma unroll
+        for (int c = 0; c < kPlanCandidates; ++c) {
+            loc[c] = 0;
+        }
+        for (uint32_t i = tid; i < count; i += kPlanThreads) {
+            const uint32_t rows = st[i].aux[0];
+            if (rows == 0) {
+                continue;
+            }
+#pragma unroll
+            for (int c = 0; c < kPlanCandidates; ++c) {
+                const uint32_t J = cand[c];
+                loc[c] += rows <= J ? 1u : (rows + J - 1) / J;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < kPlanCandidates; ++c) {
+            if (loc[c] != 0) {
+                atomicAdd(&cand_tiles[c], loc[c]);
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int best = -1;
+        double best_est = 0.0;
+        for (int c = 0; c < kPlanCandidates; ++c) {
+            const unsigned long long tiles = cand_tiles[c];
+            if (tiles == 0 || tiles > static_cast<unsigned long long>(count) + kBatchExtraTiles) {
+                continue;
+            }
+            const double waves = static_cast<double>((tiles + sms - 1) / sms);
+            const double est = waves * (static_cast<double>(R) / static_cast<double>(tiles) + kTileOverheadRows);
+            if (best < 0 || est < best_est || (est == best_est && cand[c] > cand[best])) {
+                best = c;
+                best_est = est;
+            }
+        }
+        jstar_s = best < 0 ? 1u : cand[best];
+    }
+    __syncthreads();
+    const uint32_t jstar = jstar_s;
 
     // Pass 2: tile height and count per object; histogram of tiles by
     // floor(log2 J).
@@ -296,9 +381,16 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    const uint32_t total = hdr->total_tiles;
     constexpr int64_t T = kHornerThreads;
 
+    pdl_release();
+    fill_aes_smem(smem + kSealAes, a.kt.aes_t);
+    fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
+    for (int i = tid; i < kSealFoldSmemLevels * 512; i += blockDim.x) {
+        reinterpret_cast<uint4*>(smem + kSealFold)[i] = __ldg(a.kt.gh_pow2 + i);
+    }
+    pdl_wait();  // the plan kernel's workspace
+    const uint32_t total = hdr->total_tiles;
     if (tid == 0) {
         *next_s = atomicAdd(&hdr->next_tile[0], 1u);
     }
@@ -307,12 +399,6 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
     if (tile >= total) {
         return;
     }
-    fill_aes_smem(smem + kSealAes, a.kt.aes_t);
-    fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
-    for (int i = tid; i < kSealFoldSmemLevels * 512; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + kSealFold)[i] = __ldg(a.kt.gh_pow2 + i);
-    }
-    __syncthreads();
 
     // Per-tile values are loaded where they are used (the power warp reloads
     // them after the fold) so that only `tile` stays live across the rows.
@@ -405,9 +491,15 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    const uint32_t total = hdr->total_tiles;
     constexpr int64_t T = kHornerThreads;
 
+    pdl_release();
+    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
+    for (int i = tid; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
+        reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);
+    }
+    pdl_wait();  // the plan kernel's workspace
+    const uint32_t total = hdr->total_tiles;
     if (tid == 0) {
         *next_s = atomicAdd(&hdr->next_tile[0], 1u);
     }
@@ -416,11 +508,6 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
     if (tile >= total) {
         return;
     }
-    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
-    for (int i = tid; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);
-    }
-    __syncthreads();
 
     for (;;) {
         unsigned long long uhi = 0, ulo = 0;
@@ -478,8 +565,9 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
 // Gated CTR over the same tiles (rows of kCtrThreads = kHornerThreads
 // blocks). Each tile reads its object's verdict, written by
 // open_ghash_batch_kernel earlier on the stream: authentic -> decrypt,
-// otherwise zero the tile's plaintext bytes. The queue head is read from a
-// two-entry shared buffer so one barrier per tile suffices.
+// otherwise zero the tile's plaintext bytes. Thread 0 takes the next tile
+// after this tile's rows; the index goes through a two-entry shared buffer
+// so one barrier per tile suffices.
 __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const BatchArgs a)
 {
     static_assert(kCtrThreads == kHornerThreads, "CTR tiles reuse the GHASH tile rows");
@@ -490,9 +578,12 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const Ba
     const TileRec* rec = reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count));
     const int tid = threadIdx.x;
     const int lane = tid & 31;
-    const uint32_t total = hdr->total_tiles;
     constexpr int64_t T = kCtrThreads;
 
+    pdl_release();
+    fill_aes_smem(smem, a.kt.aes_t);
+    pdl_wait();  // the verdicts of the GHASH pass
+    const uint32_t total = hdr->total_tiles;
     if (tid == 0) {
         next_s[0] = atomicAdd(&hdr->next_tile[1], 1u);
     }
@@ -501,13 +592,8 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const Ba
     if (tile >= total) {
         return;
     }
-    fill_aes_smem(smem, a.kt.aes_t);
-    __syncthreads();
 
     for (uint32_t k = 1;; ++k) {
-        if (tid == 0) {
-            next_s[k & 1] = atomicAdd(&hdr->next_tile[1], 1u);
-        }
         const TileRec tr = rec[tile];
         const BatchItem& it = a.items[tr.item];
         const Slot& slot = st[tr.item];
@@ -536,6 +622,11 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const Ba
             t.s012[1] = iv.y ^ a.rk[1];
             t.s012[2] = iv.z ^ a.rk[2];
             ctr_rows_any(lq, pt_aligned, t, a.rk, tid, lane);
+        }
+        // Take the next tile only when this one is done: a CTA that reserved
+        // tiles ahead would hold them while other CTAs sit idle.
+        if (tid == 0) {
+            next_s[k & 1] = atomicAdd(&hdr->next_tile[1], 1u);
         }
         __syncthreads();
         const uint32_t next = next_s[k & 1];

@@ -18,6 +18,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <utility>
 
 #include "host_crypto.h"
 #include "kernels.cuh"
@@ -380,9 +381,9 @@ dev::Slot* take_slot(KeyHandle* h)
 
 // Launch with programmatic stream serialization (see pdl_release/pdl_wait):
 // the kernel may start while the previous kernel on the stream drains.
-template <class Arg>
-cudaError_t launch_pdl(void (*kernel)(Arg), uint32_t grid, uint32_t block, uint32_t smem, cudaStream_t s,
-                       const Arg& arg)
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, uint32_t smem, cudaStream_t s,
+                       Args&&... args)
 {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
@@ -394,7 +395,7 @@ cudaError_t launch_pdl(void (*kernel)(Arg), uint32_t grid, uint32_t block, uint3
     attr.val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, arg);
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 template <int SQ, bool A>
@@ -719,9 +720,8 @@ int batch_launch(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* it
     auto* d_items = reinterpret_cast<dev::BatchItem*>(items);
     auto* ws = static_cast<uint8_t*>(workspace);
     const int sms = h->num_sms < dev::kBatchMaxSms ? h->num_sms : dev::kBatchMaxSms;
-    dev::batch_plan_kernel<<<1, dev::kPlanThreads, 0, s>>>(d_items, static_cast<uint32_t>(count), ws, open ? 1 : 0,
-                                                           static_cast<uint32_t>(sms * dev::kBatchWaves));
-    if (cudaGetLastError() != cudaSuccess) {
+    if (launch_pdl(dev::batch_plan_kernel, 1, dev::kPlanThreads, 0, s, d_items, static_cast<uint32_t>(count), ws,
+                   open ? 1 : 0, static_cast<uint32_t>(sms)) != cudaSuccess) {
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
     }
     dev::BatchArgs ba{};
@@ -730,16 +730,14 @@ int batch_launch(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* it
     ba.count = static_cast<uint32_t>(count);
     std::memcpy(ba.rk, h->rk, sizeof(ba.rk));
     ba.kt = h->kt;
+    const uint32_t grid = static_cast<uint32_t>(h->num_sms);
     if (!open) {
-        dev::seal_batch_kernel<<<h->num_sms, dev::kSealThreads, dev::kSealSmem, s>>>(ba);
-        return cuda_rc(cudaGetLastError());
+        return cuda_rc(launch_pdl(dev::seal_batch_kernel, grid, dev::kSealThreads, dev::kSealSmem, s, ba));
     }
-    dev::open_ghash_batch_kernel<<<h->num_sms, dev::kSealThreads, dev::kOpenSmem, s>>>(ba);
-    if (cudaGetLastError() != cudaSuccess) {
+    if (launch_pdl(dev::open_ghash_batch_kernel, grid, dev::kSealThreads, dev::kOpenSmem, s, ba) != cudaSuccess) {
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
     }
-    dev::open_ctr_batch_kernel<<<h->num_sms, dev::kCtrThreads, dev::kCtrBatchSmem, s>>>(ba);
-    return cuda_rc(cudaGetLastError());
+    return cuda_rc(launch_pdl(dev::open_ctr_batch_kernel, grid, dev::kCtrThreads, dev::kCtrBatchSmem, s, ba));
 }
 
 }  // namespace

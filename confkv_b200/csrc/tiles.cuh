@@ -83,7 +83,9 @@ __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk
         chain_push_dyn<kSealGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
     };
 
-    int64_t r = 0;
+    // Rows below r_pad hold no block of the object (tile 0's leading
+    // padding): they would only push zeros into chains that are still zero.
+    int64_t r = base < 0 ? (-base) / T : 0;
 #pragma unroll 1
     for (; r < r_a; ++r) {
         generic_row(r);
@@ -235,7 +237,7 @@ __device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4*
         chain_push_dyn<kOpenGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
     };
 
-    int64_t r = 0;
+    int64_t r = base < 0 ? (-base) / T : 0;  // rows below hold no block of the object
 #pragma unroll 1
     for (; r < r_a; ++r) {
         generic_row(r);
@@ -327,7 +329,7 @@ struct CtrTile {
 template <bool PT_ALIGNED>
 __device__ __forceinline__ void ctr_zero_rows(const CtrTile& t, int tid)
 {
-    for (int64_t r = 0; r < t.rows; ++r) {
+    for (int64_t r = t.base < 0 ? (-t.base) / kCtrThreads : 0; r < t.rows; ++r) {
         const int64_t i = t.base + r * kCtrThreads + tid;
         const int nb = block_bytes(i, t.P);
         uint8_t* d = t.dst + static_cast<uint64_t>(i) * 16u;
@@ -382,7 +384,7 @@ __device__ __forceinline__ void ctr_rows(const CtrTile& t, const uint32_t* rk, i
     if (r_lo > r_hi) {
         r_lo = r_hi = rows;
     }
-    int64_t r = 0;
+    int64_t r = base < 0 ? (-base) / T : 0;  // rows below hold no block of the object
 #pragma unroll 1
     for (; r < r_lo; ++r) {
         generic_row(r);

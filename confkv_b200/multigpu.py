@@ -45,6 +45,19 @@ def reduce_max(values, device=None) -> list[float]:
     return t.cpu().tolist()
 
 
+def reduce_sum(values, device=None) -> list[float]:
+    """Element-wise sum over all ranks (identity without a process group)."""
+    import torch
+    import torch.distributed as dist
+
+    vals = [float(v) for v in values]
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return vals
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.cpu().tolist()
+
+
 def all_ok(flag: bool, device=None) -> bool:
     """True only if every rank passes True."""
     import torch

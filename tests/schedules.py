@@ -20,6 +20,8 @@ OPEN_R = 2           # kOpenChains: rows per interior iteration of open_ghash_ro
 CTR_PAIR = 2
 BATCH_WAVES = 8      # kBatchWaves
 BATCH_MAX_SMS = 256  # kBatchMaxSms
+PLAN_CANDIDATES = 16  # kPlanCandidates
+TILE_OVERHEAD_ROWS = 4.0  # kTileOverheadRows
 BATCH_EXTRA = BATCH_WAVES * BATCH_MAX_SMS
 
 
@@ -33,6 +35,11 @@ def _trunc_div(a, b):
     return q if (a >= 0) == (b > 0) else -q
 
 
+def pad_rows(base):
+    """Leading rows of a tile that hold no block of the object (skipped)."""
+    return _trunc_div(-base, T) if base < 0 else 0
+
+
 def seal_tile_rows(base, rows, P):
     """(generic rows, interior rows) of seal_rows for a tile."""
     n_full = P // 16
@@ -41,7 +48,7 @@ def seal_tile_rows(base, rows, P):
     r_a = min(_trunc_div(r_lo + SEAL_PAIR - 1, SEAL_PAIR) * SEAL_PAIR, r_hi)
     ngroups = _trunc_div(r_hi - r_a, SEAL_PAIR) if r_hi > r_a else 0
     interior = list(range(r_a, r_a + SEAL_PAIR * ngroups))
-    generic = list(range(0, r_a)) + list(range(r_a + SEAL_PAIR * ngroups, rows))
+    generic = list(range(pad_rows(base), r_a)) + list(range(r_a + SEAL_PAIR * ngroups, rows))
     return generic, interior
 
 
@@ -53,7 +60,7 @@ def open_tile_rows(base, rows, P):
     r_a = min(_trunc_div(r_lo + OPEN_R - 1, OPEN_R) * OPEN_R, r_hi)
     ngroups = _trunc_div(r_hi - r_a, OPEN_R) if r_hi > r_a else 0
     interior = list(range(r_a, r_a + OPEN_R * ngroups))
-    generic = list(range(0, r_a)) + list(range(r_a + OPEN_R * ngroups, rows))
+    generic = list(range(pad_rows(base), r_a)) + list(range(r_a + OPEN_R * ngroups, rows))
     return generic, interior
 
 
@@ -66,7 +73,7 @@ def ctr_tile_rows(base, rows, P):
         r_lo = r_hi = rows
     npair = _trunc_div(r_hi - r_lo, CTR_PAIR)
     interior = list(range(r_lo, r_lo + CTR_PAIR * npair))
-    generic = list(range(0, r_lo)) + list(range(r_lo + CTR_PAIR * npair, rows))
+    generic = list(range(pad_rows(base), r_lo)) + list(range(r_lo + CTR_PAIR * npair, rows))
     return generic, interior
 
 
@@ -86,6 +93,30 @@ def tile_base(n, J, G, c):
     return n - (G - c) * J * T
 
 
+def plan_tile_height(rows, sms, count):
+    """Tile height J* of batch_plan_kernel (rows: per object, 0 = invalid)."""
+    R = sum(rows)
+    max_rows = max(rows) if rows else 0
+    cand = []
+    for c in range(PLAN_CANDIDATES):
+        if c < 8:
+            j = cdiv(R, (c + 1) * sms)
+        else:
+            j = cdiv(max_rows, c - 7)
+        j = min(j, max_rows)
+        cand.append(max(1, j))
+    tiles = [sum((1 if r <= J else cdiv(r, J)) for r in rows if r) for J in cand]
+    best, best_est = -1, 0.0
+    for c in range(PLAN_CANDIDATES):
+        t = tiles[c]
+        if t == 0 or t > count + BATCH_EXTRA:
+            continue
+        est = float(cdiv(t, sms)) * (float(R) / float(t) + TILE_OVERHEAD_ROWS)
+        if best < 0 or est < best_est or (est == best_est and cand[c] > cand[best]):
+            best, best_est = c, est
+    return 1 if best < 0 else cand[best]
+
+
 def batch_plan(lens, sms, valid=None):
     """batch_plan_kernel: returns (jstar, [(J, G) or None per object], queue)
     where the queue lists (object, tile) in device order up to the order
@@ -96,8 +127,8 @@ def batch_plan(lens, sms, valid=None):
     for P, ok in zip(lens, valid):
         n = cdiv(P, 16)
         rows.append((1 if n == 0 else cdiv(n, T)) if ok else 0)
-    sms_waves = min(sms, BATCH_MAX_SMS) * BATCH_WAVES
-    jstar = max(1, cdiv(sum(rows), sms_waves))
+    sms = min(sms, BATCH_MAX_SMS)
+    jstar = plan_tile_height(rows, sms, count)
     plan = []
     buckets = {}
     for i, (P, r) in enumerate(zip(lens, rows)):

@@ -8,8 +8,8 @@ import math
 import numpy as np
 import pytest
 
-from schedules import (BATCH_EXTRA, T, batch_plan, cdiv, ctr_tile_rows, open_tile_rows, seal_tile_rows,
-                       tile_base)
+from schedules import (BATCH_EXTRA, T, batch_plan, cdiv, ctr_tile_rows, open_tile_rows, pad_rows,
+                       seal_tile_rows, tile_base)
 
 
 def _ragged(count, seed, lo=4096, hi=1 << 20):
@@ -55,6 +55,23 @@ def test_plan_bound_order_and_partition(name, sms):
             assert J == max(1, cdiv(n, T))
 
 
+def test_plan_tile_height():
+    # 32 x 32 MiB: eight equal waves of 111-row tiles (37 per object)
+    jstar, plan, queue = batch_plan([32 << 20] * 32, 148)
+    assert jstar == 111 and len(queue) == 32 * 37 == 8 * 148
+    # one 32 MiB object: one wave
+    jstar, plan, queue = batch_plan([32 << 20], 148)
+    assert len(queue) <= 148 and jstar == 28
+    # 64 x 1 MiB: every object in two tiles -> 128 tiles, one wave
+    jstar, plan, queue = batch_plan([1 << 20] * 64, 148)
+    assert jstar == 64 and len(queue) == 128
+    # 64 x 2 MiB kv_small objects: two tiles each
+    jstar, plan, queue = batch_plan([2 << 20] * 64, 148)
+    assert jstar == 128 and len(queue) == 128
+    # all invalid / empty
+    assert batch_plan([5, 6], 148, valid=[False, False])[0] == 1
+
+
 def test_plan_skips_invalid():
     lens = [100, 200, 300]
     jstar, plan, queue = batch_plan(lens, 148, valid=[True, False, True])
@@ -63,7 +80,10 @@ def test_plan_skips_invalid():
 
 def _check_tile(base, rows, P, lo_block, sched):
     generic, interior = sched(base, rows, P)
-    assert sorted(generic + interior) == list(range(rows))
+    pad = pad_rows(base)
+    assert sorted(generic + interior) == list(range(pad, rows))
+    # skipped rows hold no block of the object
+    assert all(base + r * T + T - 1 < 0 for r in range(pad))
     n_full = P // 16
     for r in interior:
         assert base + r * T >= lo_block and base + r * T + T - 1 < n_full, (base, rows, P, r)

@@ -30,9 +30,10 @@ def _worker(rank, world, port, q):
         mine = multigpu.round_robin(37, rank, world)
         times = [10.0 + rank, 5.0 * (world - rank)]
         mx = multigpu.reduce_max(times)
+        sm = multigpu.reduce_sum([len(mine)])
         ok_all = multigpu.all_ok(True)
         ok_one_bad = multigpu.all_ok(rank != 1)
-        q.put((rank, mine, mx, ok_all, ok_one_bad))
+        q.put((rank, mine, (mx, sm), ok_all, ok_one_bad))
     finally:
         dist.destroy_process_group()
 
@@ -56,7 +57,7 @@ def test_gloo_world2_partition_and_reductions():
     assert covered == list(range(37))
     assert not set(results[0][0]) & set(results[1][0])
     for rank in range(world):
-        assert results[rank][1] == [11.0, 10.0]
+        assert results[rank][1] == ([11.0, 10.0], [37.0])
         assert results[rank][2] is True
         assert results[rank][3] is False
 
@@ -64,6 +65,7 @@ def test_gloo_world2_partition_and_reductions():
 def test_single_process_helpers():
     assert multigpu.round_robin(5, 0, 1) == [0, 1, 2, 3, 4]
     assert multigpu.reduce_max([1.5, 2.0]) == [1.5, 2.0]
+    assert multigpu.reduce_sum([3]) == [3.0]
     assert multigpu.all_ok(True) and not multigpu.all_ok(False)
     assert list(multigpu.kv_head_shard(8, 3, 8)) == [3]
     with pytest.raises(ValueError):
