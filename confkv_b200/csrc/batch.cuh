@@ -55,17 +55,26 @@ constexpr uint64_t kBatchMaxBlocks = 0xfffffffeull;
 constexpr uint32_t kCtrBatchMisc = kAesBytes;
 constexpr uint32_t kCtrBatchSmem = kCtrBatchMisc + 64;
 
+// Alignment classes: 2 v + p, v = the frame's ciphertext class (seal: store
+// funnel word part 0..3, 4 = aligned; open: load funnel word part, same
+// coding) and p = 1 when the plaintext side (seal src, open dst) is 16-B
+// aligned. Each tile record carries its object's class; the work kernels run
+// a loop specialised for it and switch loops only when the class changes.
+constexpr int kClasses = 10;
+
 struct BatchHeader {
     uint32_t total_tiles;
     uint32_t next_tile[2];   // queue heads: [0] seal / open GHASH, [1] open CTR
     uint32_t iters_max;      // J*
     uint32_t pad[12];
 };
+static_assert(sizeof(BatchHeader) <= 256, "batch header fits its 256-byte area");
 
 struct TileRec {
     uint32_t item;
-    uint32_t cta;            // tile index c within the object
+    uint32_t cta;            // tile index c within the object (bits 0-23) | class << 24
 };
+constexpr uint32_t kTileIndexMask = 0x00ffffffu;
 
 __host__ __device__ constexpr size_t batch_slots_offset() { return 256; }
 __host__ __device__ constexpr size_t batch_tiles_offset(size_t count)
@@ -85,6 +94,41 @@ struct BatchArgs {
     KeyTables kt;
 };
 
+// Ciphertext store class of a frame: sq = word part of 16 - (ct & 15)
+// (4 when aligned), r = its byte part.
+__device__ __forceinline__ void store_class(const uint8_t* ct, int& sq, uint32_t& r)
+{
+    const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(ct) & 15u);
+    sq = 4;
+    r = 0;
+    if (off != 0) {
+        const uint32_t sh = 16u - off;
+        sq = static_cast<int>(sh >> 2);
+        r = sh & 3u;
+    }
+}
+
+// Ciphertext load class of a frame: lq = word part of (ct & 15) (4 when
+// aligned), r = its byte part.
+__device__ __forceinline__ void load_class(const uint8_t* ct, int& lq, uint32_t& r)
+{
+    const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(ct) & 15u);
+    lq = off == 0 ? 4 : static_cast<int>(off >> 2);
+    r = off & 3u;
+}
+
+__device__ __forceinline__ int item_class(const BatchItem& it, int open)
+{
+    int v;
+    uint32_t r;
+    if (open) {
+        load_class(it.src + 13, v, r);
+        return 2 * v + ((reinterpret_cast<uintptr_t>(it.dst) & 15u) == 0);
+    }
+    store_class(it.dst + 13, v, r);
+    return 2 * v + ((reinterpret_cast<uintptr_t>(it.src) & 15u) == 0);
+}
+
 // ------------------------------------------------------------------ plan
 
 // `open` selects the descriptor rules: seal needs capacity >= P + 29; open
@@ -95,8 +139,8 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
 {
     __shared__ unsigned long long red[kPlanThreads / 32];
     __shared__ uint32_t red_max[kPlanThreads / 32];
-    __shared__ unsigned int hist[kBuckets];
-    __shared__ unsigned int cursor[kBuckets];
+    __shared__ unsigned int hist[kBuckets][kClasses];
+    __shared__ unsigned int cursor[kBuckets][kClasses];
     __shared__ unsigned long long total_rows;
     __shared__ uint32_t max_rows;
     __shared__ uint32_t cand[kPlanCandidates];
@@ -108,8 +152,8 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     const int tid = threadIdx.x;
     constexpr uint64_t T = kHornerThreads;
     pdl_release();
-    if (tid < kBuckets) {
-        hist[tid] = 0;
+    for (int i = tid; i < kClasses * kBuckets; i += kPlanThreads) {
+        hist[i / kClasses][i % kClasses] = 0;
     }
     pdl_wait();  // descriptors and workspace may belong to earlier work on the stream
 
@@ -231,7 +275,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     const uint32_t jstar = jstar_s;
 
     // Pass 2: tile height and count per object; histogram of tiles by
-    // floor(log2 J).
+    // (alignment class, floor(log2 J)).
     for (uint32_t i = tid; i < count; i += kPlanThreads) {
         Slot& s = st[i];
         const uint32_t rows = s.aux[0];
@@ -246,14 +290,18 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         G = G < 1 ? 1 : G;
         s.aux[0] = J;
         s.aux[1] = static_cast<uint32_t>(G);
-        atomicAdd(&hist[31 - __clz(static_cast<int>(J))], static_cast<unsigned int>(G));
+        atomicAdd(&hist[31 - __clz(static_cast<int>(J))][item_class(items[i], open)], static_cast<unsigned int>(G));
     }
     __syncthreads();
+    // Records: tallest bucket first, classes in order inside a bucket (so
+    // the queue ends on short tiles and neighbouring tiles share a class).
     if (tid == 0) {
         unsigned int pos = 0;
         for (int b = kBuckets - 1; b >= 0; --b) {
-            cursor[b] = pos;
-            pos += hist[b];
+            for (int c = 0; c < kClasses; ++c) {
+                cursor[b][c] = pos;
+                pos += hist[b][c];
+            }
         }
         hdr->total_tiles = pos;
         hdr->next_tile[0] = 0;
@@ -262,71 +310,18 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     }
     __syncthreads();
 
-    // Pass 3: tile records, tallest bucket first.
+    // Pass 3: tile records.
     for (uint32_t i = tid; i < count; i += kPlanThreads) {
         const Slot& s = st[i];
         const uint32_t G = s.aux[1];
         if (G == 0) {
             continue;
         }
-        const unsigned int p = atomicAdd(&cursor[31 - __clz(static_cast<int>(s.aux[0]))], G);
+        const uint32_t cls = static_cast<uint32_t>(item_class(items[i], open));
+        const unsigned int p = atomicAdd(&cursor[31 - __clz(static_cast<int>(s.aux[0]))][cls], G);
         for (uint32_t c = 0; c < G; ++c) {
-            rec[p + c] = TileRec{i, c};
+            rec[p + c] = TileRec{i, c | (cls << 24)};
         }
-    }
-}
-
-// ------------------------------------------------------------ dispatch
-
-template <int SQ>
-__device__ __forceinline__ uint4 seal_rows_pt(bool pt_aligned, const SealTile& t, const uint32_t* rk,
-                                              const uint4* pow2, int tid, int lane)
-{
-    return pt_aligned ? seal_rows<SQ, true>(t, rk, pow2, tid, lane) : seal_rows<SQ, false>(t, rk, pow2, tid, lane);
-}
-
-__device__ __forceinline__ uint4 seal_rows_any(int sq, bool pt_aligned, const SealTile& t, const uint32_t* rk,
-                                               const uint4* pow2, int tid, int lane)
-{
-    switch (sq) {
-    case 0: return seal_rows_pt<0>(pt_aligned, t, rk, pow2, tid, lane);
-    case 1: return seal_rows_pt<1>(pt_aligned, t, rk, pow2, tid, lane);
-    case 2: return seal_rows_pt<2>(pt_aligned, t, rk, pow2, tid, lane);
-    case 3: return seal_rows_pt<3>(pt_aligned, t, rk, pow2, tid, lane);
-    default: return seal_rows_pt<4>(pt_aligned, t, rk, pow2, tid, lane);
-    }
-}
-
-__device__ __forceinline__ uint4 open_ghash_rows_any(int lq, const OpenTile& t, const uint4* ht, int tid, int lane)
-{
-    switch (lq) {
-    case 0: return open_ghash_rows<0>(t, ht, tid, lane);
-    case 1: return open_ghash_rows<1>(t, ht, tid, lane);
-    case 2: return open_ghash_rows<2>(t, ht, tid, lane);
-    case 3: return open_ghash_rows<3>(t, ht, tid, lane);
-    default: return open_ghash_rows<4>(t, ht, tid, lane);
-    }
-}
-
-template <int LQ>
-__device__ __forceinline__ void ctr_rows_pt(bool pt_aligned, const CtrTile& t, const uint32_t* rk, int tid, int lane)
-{
-    if (pt_aligned) {
-        ctr_rows<LQ, true>(t, rk, tid, lane);
-    } else {
-        ctr_rows<LQ, false>(t, rk, tid, lane);
-    }
-}
-
-__device__ __forceinline__ void ctr_rows_any(int lq, bool pt_aligned, const CtrTile& t, const uint32_t* rk, int tid,
-                                             int lane)
-{
-    switch (lq) {
-    case 0: ctr_rows_pt<0>(pt_aligned, t, rk, tid, lane); break;
-    case 1: ctr_rows_pt<1>(pt_aligned, t, rk, tid, lane); break;
-    case 2: ctr_rows_pt<2>(pt_aligned, t, rk, tid, lane); break;
-    case 3: ctr_rows_pt<3>(pt_aligned, t, rk, tid, lane); break;
-    default: ctr_rows_pt<4>(pt_aligned, t, rk, tid, lane); break;
     }
 }
 
@@ -345,44 +340,130 @@ __device__ __forceinline__ bool batch_object_sum(Slot* slot, uint32_t G, uint4 f
     return cta_accumulate(slot, fold, uhi, ulo, lane, G, shi, slo);
 }
 
-// Ciphertext store class of a frame: sq = word part of 16 - (ct & 15)
-// (4 when aligned), r = its byte part.
-__device__ __forceinline__ void store_class(const uint8_t* ct, int& sq, uint32_t& r)
+// Shared state of the work kernels: the workspace views and the CTA's
+// coordinates.
+struct BatchCta {
+    BatchHeader* hdr;
+    Slot* st;
+    const TileRec* rec;
+    uint32_t total;
+    int tid;
+    int lane;
+    int warp;
+};
+
+__device__ __forceinline__ int tile_class(const BatchCta& c, uint32_t tile)
 {
-    const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(ct) & 15u);
-    sq = 4;
-    r = 0;
-    if (off != 0) {
-        const uint32_t sh = 16u - off;
-        sq = static_cast<int>(sh >> 2);
-        r = sh & 3u;
-    }
+    return static_cast<int>(c.rec[tile].cta >> 24);
 }
 
-// Ciphertext load class of a frame: lq = word part of (ct & 15) (4 when
-// aligned), r = its byte part.
-__device__ __forceinline__ void load_class(const uint8_t* ct, int& lq, uint32_t& r)
+// First queue index of this CTA (all threads); the barriers bracket the
+// shared broadcast.
+__device__ __forceinline__ uint32_t first_tile(volatile uint32_t* next_s, const BatchCta& c, int pass)
 {
-    const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(ct) & 15u);
-    lq = off == 0 ? 4 : static_cast<int>(off >> 2);
-    r = off & 3u;
+    if (c.tid == 0) {
+        *next_s = atomicAdd(&c.hdr->next_tile[pass], 1u);
+    }
+    __syncthreads();
+    const uint32_t t = *next_s;
+    __syncthreads();
+    return t;
 }
 
 // ------------------------------------------------------------------ seal
 
+// Tiles of one alignment class, from `tile` while the queue hands out tiles
+// of this class; returns the first tile of another class (or >= total).
+// Per-tile values are loaded where they are used (the power warp reloads
+// them after the fold) so that only the tile index stays live across the
+// rows. Thread 0 takes the next index after its rows.
+template <int SQ, bool PT>
+__device__ __forceinline__ uint32_t seal_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, uint32_t tile,
+                                               int cls)
+{
+    constexpr int64_t T = kHornerThreads;
+    uint4* part = reinterpret_cast<uint4*>(smem + kSealPart);
+    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kSealMisc);
+    for (;;) {
+        unsigned long long uhi = 0, ulo = 0;
+        uint4 ej0 = make_uint4(0, 0, 0, 0);
+        uint4 lh = make_uint4(0, 0, 0, 0);
+        {
+            const TileRec tr = c.rec[tile];
+            const uint32_t cta = tr.cta & kTileIndexMask;
+            const BatchItem* it = a.items + tr.item;
+            const uint32_t J = c.st[tr.item].aux[0];
+            const uint32_t G = c.st[tr.item].aux[1];
+            const uint64_t P = it->plen;
+            const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
+            const int64_t span = static_cast<int64_t>(J) * T;
+            uint8_t* frame = it->dst;
+            const uint32_t ivw[3] = {it->iv[0], it->iv[1], it->iv[2]};
+            if (cta == 0 && c.tid == 0) {
+                frame[0] = 1;
+                for (int b = 0; b < 12; ++b) {
+                    frame[1 + b] = static_cast<uint8_t>(ivw[b >> 2] >> (8 * (b & 3)));
+                }
+            }
+            if (c.warp == kPowerWarp) {
+                const unsigned long long d = static_cast<unsigned long long>(G - 1 - cta) *
+                                                 static_cast<unsigned long long>(span) + 2ull;
+                seal_power(ivw, a.rk, P, d, a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
+            } else {
+                int sq;
+                uint32_t store_r;
+                store_class(frame + 13, sq, store_r);  // sq == SQ for this class
+                (void)sq;
+                const SealTile t{it->src, frame + 13, P, n - static_cast<int64_t>(G - cta) * span,
+                                 static_cast<int64_t>(J), {ivw[0] ^ a.rk[0], ivw[1] ^ a.rk[1], ivw[2] ^ a.rk[2]},
+                                 store_r};
+                part[c.tid] = seal_rows<SQ, PT>(t, a.rk, a.kt.gh_pow2, c.tid, c.lane);
+                if (c.tid == 0) {
+                    *next_s = atomicAdd(&c.hdr->next_tile[0], 1u);
+                }
+            }
+        }
+        __syncthreads();
+        seal_fold(smem, part, a.kt.gh_pow2, c.tid);
+        const uint32_t next = *next_s;
+
+        if (c.warp == kPowerWarp) {
+            const uint32_t item = c.rec[tile].item;
+            Slot* slot = c.st + item;
+            unsigned long long shi, slo;
+            if (batch_object_sum(slot, slot->aux[1], part[0], uhi, ulo, c.lane, shi, slo)) {
+                const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
+                if (c.lane < 16) {
+                    const BatchItem* it = a.items + item;
+                    it->dst[13 + it->plen + c.lane] = static_cast<uint8_t>(byte_of(tag, c.lane));
+                }
+            }
+        } else if (next < c.total) {
+            // seal_fold stored the late fold tables over the first
+            // kSealLateBytes of the AES region: T0/T1 entries x < 192.
+            for (int i = c.tid; i < 4096; i += kHornerThreads) {
+                const int x = (i >> 3) & 255;
+                if (x < static_cast<int>(kSealLateBytes >> 8)) {
+                    const int kk = i >> 11;
+                    const uint32_t tv = __ldg(a.kt.aes_t + kk * 256 + x);
+                    const uint32_t off = (static_cast<uint32_t>(x) << 8) | (static_cast<uint32_t>(kk & 1) << 7) |
+                                         (static_cast<uint32_t>(i & 7) << 4);
+                    *reinterpret_cast<uint4*>(smem + kSealAes + off) = make_uint4(tv, tv, tv, tv);
+                }
+            }
+        }
+        __syncthreads();
+        if (next >= c.total || tile_class(c, next) != cls) {
+            return next;
+        }
+        tile = next;
+    }
+}
+
 __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const BatchArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem[];
-    uint4* part = reinterpret_cast<uint4*>(smem + kSealPart);
-    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kSealMisc);
-    BatchHeader* hdr = reinterpret_cast<BatchHeader*>(a.ws);
-    Slot* st = reinterpret_cast<Slot*>(a.ws + batch_slots_offset());
-    const TileRec* rec = reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count));
     const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
-    constexpr int64_t T = kHornerThreads;
-
     pdl_release();
     fill_aes_smem(smem + kSealAes, a.kt.aes_t);
     fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
@@ -390,164 +471,79 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
         reinterpret_cast<uint4*>(smem + kSealFold)[i] = __ldg(a.kt.gh_pow2 + i);
     }
     pdl_wait();  // the plan kernel's workspace
-    const uint32_t total = hdr->total_tiles;
-    if (tid == 0) {
-        *next_s = atomicAdd(&hdr->next_tile[0], 1u);
-    }
-    __syncthreads();
-    uint32_t tile = *next_s;
-    if (tile >= total) {
-        return;
-    }
-
-    // Per-tile values are loaded where they are used (the power warp reloads
-    // them after the fold) so that only `tile` stays live across the rows.
-    for (;;) {
-        unsigned long long uhi = 0, ulo = 0;
-        uint4 ej0 = make_uint4(0, 0, 0, 0);
-        uint4 lh = make_uint4(0, 0, 0, 0);
-        {
-            const TileRec tr = rec[tile];
-            const BatchItem* it = a.items + tr.item;
-            const uint32_t J = st[tr.item].aux[0];
-            const uint32_t G = st[tr.item].aux[1];
-            const uint64_t P = it->plen;
-            const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
-            const int64_t span = static_cast<int64_t>(J) * T;
-            uint8_t* frame = it->dst;
-            const uint32_t ivw[3] = {it->iv[0], it->iv[1], it->iv[2]};
-            if (tr.cta == 0 && tid == 0) {
-                frame[0] = 1;
-                for (int b = 0; b < 12; ++b) {
-                    frame[1 + b] = static_cast<uint8_t>(ivw[b >> 2] >> (8 * (b & 3)));
-                }
-            }
-            if (warp == kPowerWarp) {
-                const unsigned long long d = static_cast<unsigned long long>(G - 1 - tr.cta) *
-                                                 static_cast<unsigned long long>(span) + 2ull;
-                seal_power(ivw, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
-            } else {
-                int sq;
-                uint32_t store_r;
-                store_class(frame + 13, sq, store_r);
-                const SealTile t{it->src, frame + 13, P, n - static_cast<int64_t>(G - tr.cta) * span,
-                                 static_cast<int64_t>(J), {ivw[0] ^ a.rk[0], ivw[1] ^ a.rk[1], ivw[2] ^ a.rk[2]},
-                                 store_r};
-                const bool pt_aligned = (reinterpret_cast<uintptr_t>(it->src) & 15u) == 0;
-                part[tid] = seal_rows_any(sq, pt_aligned, t, a.rk, a.kt.gh_pow2, tid, lane);
-                if (tid == 0) {
-                    *next_s = atomicAdd(&hdr->next_tile[0], 1u);
-                }
-            }
+    auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
+    const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
+                     reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count)), hdr->total_tiles,
+                     tid, tid & 31, tid >> 5};
+    uint32_t tile = first_tile(reinterpret_cast<volatile uint32_t*>(smem + kSealMisc), c, 0);
+    while (tile < c.total) {
+        const int cls = tile_class(c, tile);
+        switch (cls) {
+        case 0: tile = seal_class<0, false>(smem, a, c, tile, cls); break;
+        case 1: tile = seal_class<0, true>(smem, a, c, tile, cls); break;
+        case 2: tile = seal_class<1, false>(smem, a, c, tile, cls); break;
+        case 3: tile = seal_class<1, true>(smem, a, c, tile, cls); break;
+        case 4: tile = seal_class<2, false>(smem, a, c, tile, cls); break;
+        case 5: tile = seal_class<2, true>(smem, a, c, tile, cls); break;
+        case 6: tile = seal_class<3, false>(smem, a, c, tile, cls); break;
+        case 7: tile = seal_class<3, true>(smem, a, c, tile, cls); break;
+        case 8: tile = seal_class<4, false>(smem, a, c, tile, cls); break;
+        default: tile = seal_class<4, true>(smem, a, c, tile, cls); break;
         }
-        __syncthreads();
-        seal_fold(smem, part, a.kt.gh_pow2, tid);
-        const uint32_t next = *next_s;
-        const uint32_t total_now = hdr->total_tiles;
-
-        if (warp == kPowerWarp) {
-            const uint32_t item = rec[tile].item;
-            Slot* slot = st + item;
-            unsigned long long shi, slo;
-            if (batch_object_sum(slot, slot->aux[1], part[0], uhi, ulo, lane, shi, slo)) {
-                const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
-                if (lane < 16) {
-                    const BatchItem* it = a.items + item;
-                    it->dst[13 + it->plen + lane] = static_cast<uint8_t>(byte_of(tag, lane));
-                }
-            }
-        } else if (next < total_now) {
-            // seal_fold stored the late fold tables over the first
-            // kSealLateBytes of the AES region: T0/T1 entries x < 192.
-            for (int i = tid; i < 4096; i += kHornerThreads) {
-                const int x = (i >> 3) & 255;
-                if (x < static_cast<int>(kSealLateBytes >> 8)) {
-                    const int k = i >> 11;
-                    const uint32_t tv = __ldg(a.kt.aes_t + k * 256 + x);
-                    const uint32_t off = (static_cast<uint32_t>(x) << 8) | (static_cast<uint32_t>(k & 1) << 7) |
-                                         (static_cast<uint32_t>(i & 7) << 4);
-                    *reinterpret_cast<uint4*>(smem + kSealAes + off) = make_uint4(tv, tv, tv, tv);
-                }
-            }
-        }
-        __syncthreads();
-        if (next >= total_now) {
-            break;
-        }
-        tile = next;
     }
 }
 
 // ------------------------------------------------------------------ open
 
-__global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const BatchArgs a)
+// GHASH + verdict tiles whose frames share load class LQ (both plaintext
+// sides); returns the first tile of another load class (or >= total).
+template <int LQ>
+__device__ __forceinline__ uint32_t open_ghash_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c,
+                                                     uint32_t tile)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    constexpr int64_t T = kHornerThreads;
     uint4* part = reinterpret_cast<uint4*>(smem + kOpenPart);
     volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kOpenMisc);
-    BatchHeader* hdr = reinterpret_cast<BatchHeader*>(a.ws);
-    Slot* st = reinterpret_cast<Slot*>(a.ws + batch_slots_offset());
-    const TileRec* rec = reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count));
-    const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
-    constexpr int64_t T = kHornerThreads;
-
-    pdl_release();
-    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
-    for (int i = tid; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);
-    }
-    pdl_wait();  // the plan kernel's workspace
-    const uint32_t total = hdr->total_tiles;
-    if (tid == 0) {
-        *next_s = atomicAdd(&hdr->next_tile[0], 1u);
-    }
-    __syncthreads();
-    uint32_t tile = *next_s;
-    if (tile >= total) {
-        return;
-    }
-
     for (;;) {
         unsigned long long uhi = 0, ulo = 0;
         uint4 ej0 = make_uint4(0, 0, 0, 0);
         uint4 lh = make_uint4(0, 0, 0, 0);
         {
-            const TileRec tr = rec[tile];
+            const TileRec tr = c.rec[tile];
+            const uint32_t cta = tr.cta & kTileIndexMask;
             const BatchItem* it = a.items + tr.item;
-            const uint32_t J = st[tr.item].aux[0];
-            const uint32_t G = st[tr.item].aux[1];
+            const uint32_t J = c.st[tr.item].aux[0];
+            const uint32_t G = c.st[tr.item].aux[1];
             const uint64_t P = it->plen;
             const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
             const int64_t span = static_cast<int64_t>(J) * T;
             const uint8_t* frame = it->src;
-            if (warp == kPowerWarp) {
-                const unsigned long long d = static_cast<unsigned long long>(G - 1 - tr.cta) *
+            if (c.warp == kPowerWarp) {
+                const unsigned long long d = static_cast<unsigned long long>(G - 1 - cta) *
                                                  static_cast<unsigned long long>(span) + 2ull;
-                open_power(frame, a.kt.aes_t, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
+                open_power(frame, a.kt.aes_t, a.rk, P, d, a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
             } else {
                 int lq;
                 uint32_t load_r;
-                load_class(frame + 13, lq, load_r);
-                const OpenTile t{frame, it->capacity, P, n - static_cast<int64_t>(G - tr.cta) * span,
+                load_class(frame + 13, lq, load_r);  // lq == LQ for this class
+                (void)lq;
+                const OpenTile t{frame, it->capacity, P, n - static_cast<int64_t>(G - cta) * span,
                                  static_cast<int64_t>(J), load_r};
-                part[tid] = open_ghash_rows_any(lq, t, reinterpret_cast<const uint4*>(smem + kOpenHt), tid, lane);
-                if (tid == 0) {
-                    *next_s = atomicAdd(&hdr->next_tile[0], 1u);
+                part[c.tid] = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), c.tid, c.lane);
+                if (c.tid == 0) {
+                    *next_s = atomicAdd(&c.hdr->next_tile[0], 1u);
                 }
             }
         }
         __syncthreads();
         fold_partials<kFoldLevels>(part, reinterpret_cast<const uint4*>(smem + kOpenFold), a.kt.gh_pow2);
         const uint32_t next = *next_s;
-        const uint32_t total_now = hdr->total_tiles;
 
-        if (warp == kPowerWarp) {
-            const uint32_t item = rec[tile].item;
-            Slot* slot = st + item;
+        if (c.warp == kPowerWarp) {
+            const uint32_t item = c.rec[tile].item;
+            Slot* slot = c.st + item;
             unsigned long long shi, slo;
-            if (batch_object_sum(slot, slot->aux[1], part[0], uhi, ulo, lane, shi, slo) && lane == 0) {
+            if (batch_object_sum(slot, slot->aux[1], part[0], uhi, ulo, c.lane, shi, slo) && c.lane == 0) {
                 const BatchItem* it = a.items + item;
                 const int v = open_verdict(it->src, it->plen, shi, slo, lh, ej0);
                 *it->auth_ok = v;
@@ -555,85 +551,120 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
             }
         }
         __syncthreads();
-        if (next >= total_now) {
-            break;
+        if (next >= c.total || (tile_class(c, next) >> 1) != LQ) {
+            return next;
         }
         tile = next;
+    }
+}
+
+__global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const BatchArgs a)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int tid = threadIdx.x;
+    pdl_release();
+    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
+    for (int i = tid; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
+        reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);
+    }
+    pdl_wait();  // the plan kernel's workspace
+    auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
+    const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
+                     reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count)), hdr->total_tiles,
+                     tid, tid & 31, tid >> 5};
+    uint32_t tile = first_tile(reinterpret_cast<volatile uint32_t*>(smem + kOpenMisc), c, 0);
+    while (tile < c.total) {
+        switch (tile_class(c, tile) >> 1) {  // the GHASH pass does not touch the plaintext side
+        case 0: tile = open_ghash_class<0>(smem, a, c, tile); break;
+        case 1: tile = open_ghash_class<1>(smem, a, c, tile); break;
+        case 2: tile = open_ghash_class<2>(smem, a, c, tile); break;
+        case 3: tile = open_ghash_class<3>(smem, a, c, tile); break;
+        default: tile = open_ghash_class<4>(smem, a, c, tile); break;
+        }
     }
 }
 
 // Gated CTR over the same tiles (rows of kCtrThreads = kHornerThreads
 // blocks). Each tile reads its object's verdict, written by
 // open_ghash_batch_kernel earlier on the stream: authentic -> decrypt,
-// otherwise zero the tile's plaintext bytes. Thread 0 takes the next tile
-// after this tile's rows; the index goes through a two-entry shared buffer
-// so one barrier per tile suffices.
-__global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const BatchArgs a)
+// otherwise zero the tile's plaintext bytes. Thread 0 takes the next index
+// after this tile's rows (a CTA that reserved tiles ahead would hold them
+// while other CTAs sit idle); it goes through a two-entry shared buffer so
+// one barrier per tile suffices.
+template <int LQ, bool PT>
+__device__ __forceinline__ uint32_t ctr_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, uint32_t tile,
+                                              int cls, uint32_t& round)
 {
     static_assert(kCtrThreads == kHornerThreads, "CTR tiles reuse the GHASH tile rows");
-    extern __shared__ __align__(16) uint8_t smem[];
-    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kCtrBatchMisc);
-    BatchHeader* hdr = reinterpret_cast<BatchHeader*>(a.ws);
-    const Slot* st = reinterpret_cast<const Slot*>(a.ws + batch_slots_offset());
-    const TileRec* rec = reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count));
-    const int tid = threadIdx.x;
-    const int lane = tid & 31;
     constexpr int64_t T = kCtrThreads;
-
-    pdl_release();
-    fill_aes_smem(smem, a.kt.aes_t);
-    pdl_wait();  // the verdicts of the GHASH pass
-    const uint32_t total = hdr->total_tiles;
-    if (tid == 0) {
-        next_s[0] = atomicAdd(&hdr->next_tile[1], 1u);
-    }
-    __syncthreads();
-    uint32_t tile = next_s[0];
-    if (tile >= total) {
-        return;
-    }
-
-    for (uint32_t k = 1;; ++k) {
-        const TileRec tr = rec[tile];
-        const BatchItem& it = a.items[tr.item];
-        const Slot& slot = st[tr.item];
+    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kCtrBatchMisc);
+    for (;; ++round) {
+        const TileRec tr = c.rec[tile];
+        const uint32_t cta = tr.cta & kTileIndexMask;
+        const BatchItem* it = a.items + tr.item;
+        const Slot& slot = c.st[tr.item];
         const uint32_t J = slot.aux[0];
         const uint32_t G = slot.aux[1];
         const int ok = static_cast<int>(slot.aux[2]);
-        const uint64_t P = it.plen;
+        const uint64_t P = it->plen;
         const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
         const int64_t span = static_cast<int64_t>(J) * T;
-        const uint8_t* frame = it.src;
+        const uint8_t* frame = it->src;
         int lq;
         uint32_t load_r;
-        load_class(frame + 13, lq, load_r);
-        CtrTile t{frame, it.capacity, it.dst, P, n - static_cast<int64_t>(G - tr.cta) * span,
+        load_class(frame + 13, lq, load_r);  // lq == LQ for this class
+        (void)lq;
+        CtrTile t{frame, it->capacity, it->dst, P, n - static_cast<int64_t>(G - cta) * span,
                   static_cast<int64_t>(J), {0u, 0u, 0u}, load_r};
-        const bool pt_aligned = (reinterpret_cast<uintptr_t>(it.dst) & 15u) == 0;
         if (!ok) {
-            if (pt_aligned) {
-                ctr_zero_rows<true>(t, tid);
-            } else {
-                ctr_zero_rows<false>(t, tid);
-            }
+            ctr_zero_rows<PT>(t, c.tid);
         } else {
             const uint4 iv = load_bytes(frame + 1, 12);
             t.s012[0] = iv.x ^ a.rk[0];
             t.s012[1] = iv.y ^ a.rk[1];
             t.s012[2] = iv.z ^ a.rk[2];
-            ctr_rows_any(lq, pt_aligned, t, a.rk, tid, lane);
+            ctr_rows<LQ, PT>(t, a.rk, c.tid, c.lane);
         }
-        // Take the next tile only when this one is done: a CTA that reserved
-        // tiles ahead would hold them while other CTAs sit idle.
-        if (tid == 0) {
-            next_s[k & 1] = atomicAdd(&hdr->next_tile[1], 1u);
+        if (c.tid == 0) {
+            next_s[round & 1] = atomicAdd(&c.hdr->next_tile[1], 1u);
         }
         __syncthreads();
-        const uint32_t next = next_s[k & 1];
-        if (next >= total) {
-            break;
+        const uint32_t next = next_s[round & 1];
+        if (next >= c.total || tile_class(c, next) != cls) {
+            ++round;
+            return next;
         }
         tile = next;
+    }
+}
+
+__global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const BatchArgs a)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int tid = threadIdx.x;
+    pdl_release();
+    fill_aes_smem(smem, a.kt.aes_t);
+    pdl_wait();  // the verdicts of the GHASH pass
+    auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
+    const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
+                     reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count)), hdr->total_tiles,
+                     tid, tid & 31, tid >> 5};
+    uint32_t tile = first_tile(reinterpret_cast<volatile uint32_t*>(smem + kCtrBatchMisc) + 2, c, 1);
+    uint32_t round = 0;  // parity of the shared buffer entry, continued across classes
+    while (tile < c.total) {
+        const int cls = tile_class(c, tile);
+        switch (cls) {
+        case 0: tile = ctr_class<0, false>(smem, a, c, tile, cls, round); break;
+        case 1: tile = ctr_class<0, true>(smem, a, c, tile, cls, round); break;
+        case 2: tile = ctr_class<1, false>(smem, a, c, tile, cls, round); break;
+        case 3: tile = ctr_class<1, true>(smem, a, c, tile, cls, round); break;
+        case 4: tile = ctr_class<2, false>(smem, a, c, tile, cls, round); break;
+        case 5: tile = ctr_class<2, true>(smem, a, c, tile, cls, round); break;
+        case 6: tile = ctr_class<3, false>(smem, a, c, tile, cls, round); break;
+        case 7: tile = ctr_class<3, true>(smem, a, c, tile, cls, round); break;
+        case 8: tile = ctr_class<4, false>(smem, a, c, tile, cls, round); break;
+        default: tile = ctr_class<4, true>(smem, a, c, tile, cls, round); break;
+        }
     }
 }
 

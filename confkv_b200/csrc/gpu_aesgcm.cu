@@ -20,13 +20,23 @@
 #include <new>
 #include <utility>
 
+#include "host_common.h"
 #include "host_crypto.h"
 #include "kernels.cuh"
 #include "tiles.cuh"
-#include "batch.cuh"
 
 namespace confkv {
 namespace dev {
+
+// Writes the shared-window address of the dynamic shared memory (checked
+// against kDynSmemBase once per device by configure_device).
+__global__ void smem_base_probe_kernel(unsigned int* out)
+{
+    extern __shared__ __align__(16) uint8_t probe_smem[];
+    if (threadIdx.x == 0) {
+        out[0] = static_cast<unsigned int>(__cvta_generic_to_shared(probe_smem));
+    }
+}
 
 // ------------------------------------------------------------ seal kernel
 //
@@ -227,53 +237,7 @@ namespace {
 
 using confkv::Gf128;
 namespace dev = confkv::dev;
-
-constexpr size_t kFrameOverhead = 29;
-constexpr uint64_t kMaxBlocks = 0xfffffffeull;
-constexpr int kSlots = 64;
-constexpr int kMaxDevices = 64;
-
-struct KeyHandle {
-    int device = 0;
-    int num_sms = 0;
-    uint32_t rk[confkv::kRoundKeyWords];
-    uint8_t* d_mem = nullptr;  // one allocation: tables + slots
-    dev::KeyTables kt{};
-    dev::Slot* slots = nullptr;
-    std::atomic<uint32_t> next_slot{0};
-};
-
-class DeviceGuard {
-public:
-    explicit DeviceGuard(int target)
-    {
-        if (cudaGetDevice(&old_) != cudaSuccess) {
-            ok_ = false;
-            return;
-        }
-        if (old_ != target) {
-            ok_ = cudaSetDevice(target) == cudaSuccess;
-            changed_ = ok_;
-        }
-    }
-    ~DeviceGuard()
-    {
-        if (changed_) {
-            cudaSetDevice(old_);
-        }
-    }
-    bool ok() const { return ok_; }
-
-private:
-    int old_ = 0;
-    bool changed_ = false;
-    bool ok_ = true;
-};
-
-int cuda_rc(cudaError_t e)
-{
-    return e == cudaSuccess ? LMCACHE_GPU_AESGCM_OK : LMCACHE_GPU_AESGCM_ERR_CUDA;
-}
+using namespace confkv::host;
 
 // Host-side fault injection for tests: CONFKV_B200_FAIL_ALLOC=1 makes
 // key_create report an allocation failure before touching the device.
@@ -283,15 +247,10 @@ bool alloc_fault_injected()
     return v != nullptr && v[0] == '1';
 }
 
-template <class K>
-cudaError_t allow_smem(K kernel, uint32_t bytes)
-{
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(bytes));
-}
+}  // namespace
 
 // Opt every kernel instantiation into its dynamic shared memory once per device.
-cudaError_t configure_device(int device)
+cudaError_t confkv::host::configure_device(int device)
 {
     static std::once_flag flags[kMaxDevices];
     static cudaError_t results[kMaxDevices];
@@ -330,9 +289,7 @@ cudaError_t configure_device(int device)
         chk(allow_smem(dev::open_ctr_kernel<2, false>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<3, false>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<4, false>, dev::kCtrSmem));
-        chk(allow_smem(dev::seal_batch_kernel, dev::kSealSmem));
-        chk(allow_smem(dev::open_ghash_batch_kernel, dev::kOpenSmem));
-        chk(allow_smem(dev::open_ctr_batch_kernel, dev::kCtrBatchSmem));
+        chk(configure_batch_kernels());
         // The hot loops address shared memory as (offset + kDynSmemBase) with
         // the base folded into the load instruction; check it on this device.
         if (e == cudaSuccess) {
@@ -353,6 +310,8 @@ cudaError_t configure_device(int device)
     });
     return results[device];
 }
+
+namespace {
 
 uint32_t le_word(const uint8_t* p)
 {
@@ -377,25 +336,6 @@ void horner_grid(uint64_t n, int num_sms, uint32_t& iters, uint32_t& grid)
 dev::Slot* take_slot(KeyHandle* h)
 {
     return h->slots + (h->next_slot.fetch_add(1, std::memory_order_relaxed) % kSlots);
-}
-
-// Launch with programmatic stream serialization (see pdl_release/pdl_wait):
-// the kernel may start while the previous kernel on the stream drains.
-template <class... KArgs, class... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, uint32_t smem, cudaStream_t s,
-                       Args&&... args)
-{
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr{};
-    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr.val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 template <int SQ, bool A>
@@ -684,81 +624,6 @@ extern "C" int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, co
         }
     }
     return cuda_rc(e);
-}
-
-// ========================================================= batched seal/open
-
-namespace {
-
-static_assert(sizeof(lmcache_gpu_aesgcm_batch_item) == sizeof(dev::BatchItem), "descriptor size");
-static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, auth_ok) == offsetof(dev::BatchItem, auth_ok),
-              "descriptor layout");
-static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, iv) == offsetof(dev::BatchItem, iv), "descriptor layout");
-static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, status) == offsetof(dev::BatchItem, status),
-              "descriptor layout");
-
-int batch_launch(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* items, size_t count,
-                 void* workspace, size_t workspace_bytes, void* stream_ptr, bool open)
-{
-    if (key == nullptr) {
-        return LMCACHE_GPU_AESGCM_ERR_ARGUMENT;
-    }
-    if (count == 0) {
-        return LMCACHE_GPU_AESGCM_OK;
-    }
-    if (items == nullptr || workspace == nullptr || count > dev::kBatchMaxItems ||
-        (reinterpret_cast<uintptr_t>(items) & 15u) != 0 || (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0 ||
-        workspace_bytes < dev::batch_workspace_bytes(count)) {
-        return LMCACHE_GPU_AESGCM_ERR_ARGUMENT;
-    }
-    auto* h = reinterpret_cast<KeyHandle*>(key);
-    DeviceGuard guard(h->device);
-    if (!guard.ok()) {
-        return LMCACHE_GPU_AESGCM_ERR_CUDA;
-    }
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream_ptr);
-    auto* d_items = reinterpret_cast<dev::BatchItem*>(items);
-    auto* ws = static_cast<uint8_t*>(workspace);
-    const int sms = h->num_sms < dev::kBatchMaxSms ? h->num_sms : dev::kBatchMaxSms;
-    if (launch_pdl(dev::batch_plan_kernel, 1, dev::kPlanThreads, 0, s, d_items, static_cast<uint32_t>(count), ws,
-                   open ? 1 : 0, static_cast<uint32_t>(sms)) != cudaSuccess) {
-        return LMCACHE_GPU_AESGCM_ERR_CUDA;
-    }
-    dev::BatchArgs ba{};
-    ba.items = d_items;
-    ba.ws = ws;
-    ba.count = static_cast<uint32_t>(count);
-    std::memcpy(ba.rk, h->rk, sizeof(ba.rk));
-    ba.kt = h->kt;
-    const uint32_t grid = static_cast<uint32_t>(h->num_sms);
-    if (!open) {
-        return cuda_rc(launch_pdl(dev::seal_batch_kernel, grid, dev::kSealThreads, dev::kSealSmem, s, ba));
-    }
-    if (launch_pdl(dev::open_ghash_batch_kernel, grid, dev::kSealThreads, dev::kOpenSmem, s, ba) != cudaSuccess) {
-        return LMCACHE_GPU_AESGCM_ERR_CUDA;
-    }
-    return cuda_rc(launch_pdl(dev::open_ctr_batch_kernel, grid, dev::kCtrThreads, dev::kCtrBatchSmem, s, ba));
-}
-
-}  // namespace
-
-extern "C" size_t lmcache_gpu_aes128gcm_batch_workspace_size(size_t count)
-{
-    return count > dev::kBatchMaxItems ? 0 : dev::batch_workspace_bytes(count);
-}
-
-extern "C" int lmcache_gpu_aes128gcm_seal_batch_async(lmcache_gpu_aesgcm_key_t key,
-                                                      lmcache_gpu_aesgcm_batch_item* items, size_t count,
-                                                      void* workspace, size_t workspace_bytes, void* stream)
-{
-    return batch_launch(key, items, count, workspace, workspace_bytes, stream, false);
-}
-
-extern "C" int lmcache_gpu_aes128gcm_open_batch_async(lmcache_gpu_aesgcm_key_t key,
-                                                      lmcache_gpu_aesgcm_batch_item* items, size_t count,
-                                                      void* workspace, size_t workspace_bytes, void* stream)
-{
-    return batch_launch(key, items, count, workspace, workspace_bytes, stream, true);
 }
 
 // ===================================================== seal without allocation

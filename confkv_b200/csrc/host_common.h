@@ -1,0 +1,102 @@
+// Host-side pieces shared by the translation units of libgpu_aesgcm.so: the
+// key handle, the device guard, launch helpers and the per-device set-up.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <utility>
+
+#include "gpu_aesgcm_api.h"
+#include "host_crypto.h"
+#include "kernels.cuh"
+
+namespace confkv {
+namespace host {
+
+constexpr size_t kFrameOverhead = 29;
+constexpr uint64_t kMaxBlocks = 0xfffffffeull;
+constexpr int kSlots = 64;
+constexpr int kMaxDevices = 64;
+
+struct KeyHandle {
+    int device = 0;
+    int num_sms = 0;
+    uint32_t rk[confkv::kRoundKeyWords];
+    uint8_t* d_mem = nullptr;  // one allocation: tables + slots
+    dev::KeyTables kt{};
+    dev::Slot* slots = nullptr;
+    std::atomic<uint32_t> next_slot{0};
+};
+
+// Makes `target` the current device for the scope of a call and restores
+// the caller's device afterwards.
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int target)
+    {
+        if (cudaGetDevice(&old_) != cudaSuccess) {
+            ok_ = false;
+            return;
+        }
+        if (old_ != target) {
+            ok_ = cudaSetDevice(target) == cudaSuccess;
+            changed_ = ok_;
+        }
+    }
+    ~DeviceGuard()
+    {
+        if (changed_) {
+            cudaSetDevice(old_);
+        }
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+    bool ok() const { return ok_; }
+
+private:
+    int old_ = 0;
+    bool changed_ = false;
+    bool ok_ = true;
+};
+
+inline int cuda_rc(cudaError_t e)
+{
+    return e == cudaSuccess ? LMCACHE_GPU_AESGCM_OK : LMCACHE_GPU_AESGCM_ERR_CUDA;
+}
+
+template <class K>
+cudaError_t allow_smem(K kernel, uint32_t bytes)
+{
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
+// Launch with programmatic stream serialization (see pdl_release/pdl_wait):
+// the kernel may start while the previous kernel on the stream drains.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, uint32_t smem, cudaStream_t s,
+                       Args&&... args)
+{
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Opts every kernel of the library into its dynamic shared memory and checks
+// the shared-memory layout, once per device (gpu_aesgcm.cu).
+cudaError_t configure_device(int device);
+
+// The batched kernels' part of configure_device (batch.cu).
+cudaError_t configure_batch_kernels();
+
+}  // namespace host
+}  // namespace confkv

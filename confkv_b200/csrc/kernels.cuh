@@ -218,14 +218,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t off)
     return v;
 }
 
-__global__ void smem_base_probe_kernel(unsigned int* out)
-{
-    extern __shared__ __align__(16) uint8_t probe_smem[];
-    if (threadIdx.x == 0) {
-        out[0] = static_cast<unsigned int>(__cvta_generic_to_shared(probe_smem));
-    }
-}
-
 // One T-table lookup in the replicated shared-memory tables (region at
 // dynamic offset TAB): index byte m of w, table half/lane from lb (bytes 0
 // and 2 of lb pass through the PRMT).
