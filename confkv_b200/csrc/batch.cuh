@@ -215,61 +215,67 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     // kTileOverheadRows), among those whose tile count fits the record area
     // (the w = 8 height always does); ties go to the taller tile.
     const unsigned long long R = total_rows;
-    if (tid < kPlanCandidates) {
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    // One warp per candidate counts its tiles (a shuffle reduction, no
+    // shared atomics).
+    if (warp < kPlanCandidates) {
         unsigned long long j;
-        if (tid < 8) {
-            const unsigned long long slots = static_cast<unsigned long long>(tid + 1) * sms;
+        if (warp < 8) {
+            const unsigned long long slots = static_cast<unsigned long long>(warp + 1) * sms;
             j = (R + slots - 1) / slots;
         } else {
-            const uint32_t k = static_cast<uint32_t>(tid - 7);
+            const uint32_t k = static_cast<uint32_t>(warp - 7);
             j = (max_rows + k - 1) / k;
         }
         j = j > max_rows ? max_rows : j;
-        cand[tid] = static_cast<uint32_t>(j < 1 ? 1 : j);
-        cand_tiles[tid] = 0;
-    }
-    __syncthreads();
-    {
-        unsigned long long loc[kPlanCandidates];
-#pragma unroll
-        for (int c = 0; c < kPlanCandidates; ++c) {
-            loc[c] = 0;
-        }
-        for (uint32_t i = tid; i < count; i += kPlanThreads) {
+        const uint32_t J = static_cast<uint32_t>(j < 1 ? 1 : j);
+        unsigned long long tiles = 0;
+        for (uint32_t i = lane; i < count; i += 32) {
             const uint32_t rows = st[i].aux[0];
-            if (rows == 0) {
-                continue;
-            }
-#pragma unroll
-            for (int c = 0; c < kPlanCandidates; ++c) {
-                const uint32_t J = cand[c];
-                loc[c] += rows <= J ? 1u : (rows + J - 1) / J;
+            if (rows != 0) {
+                tiles += rows <= J ? 1u : (rows + J - 1) / J;
             }
         }
 #pragma unroll
-        for (int c = 0; c < kPlanCandidates; ++c) {
-            if (loc[c] != 0) {
-                atomicAdd(&cand_tiles[c], loc[c]);
-            }
+        for (int o = 16; o; o >>= 1) {
+            tiles += __shfl_xor_sync(0xffffffffu, tiles, o);
+        }
+        if (lane == 0) {
+            cand[warp] = J;
+            cand_tiles[warp] = tiles;
         }
     }
     __syncthreads();
-    if (tid == 0) {
-        int best = -1;
-        double best_est = 0.0;
-        for (int c = 0; c < kPlanCandidates; ++c) {
-            const unsigned long long tiles = cand_tiles[c];
-            if (tiles == 0 || tiles > static_cast<unsigned long long>(count) + kBatchExtraTiles) {
-                continue;
-            }
-            const double waves = static_cast<double>((tiles + sms - 1) / sms);
-            const double est = waves * (static_cast<double>(R) / static_cast<double>(tiles) + kTileOverheadRows);
-            if (best < 0 || est < best_est || (est == best_est && cand[c] > cand[best])) {
-                best = c;
-                best_est = est;
+    // Warp 0 scores the candidates (lane c = candidate c) and keeps the
+    // smallest estimate, the taller tile on a tie.
+    if (warp == 0) {
+        int valid = 0;
+        double est = 0.0;
+        uint32_t J = 1;
+        if (lane < kPlanCandidates) {
+            const unsigned long long tiles = cand_tiles[lane];
+            J = cand[lane];
+            valid = tiles != 0 && tiles <= static_cast<unsigned long long>(count) + kBatchExtraTiles ? 1 : 0;
+            if (valid) {
+                const double waves = static_cast<double>((tiles + sms - 1) / sms);
+                est = waves * (static_cast<double>(R) / static_cast<double>(tiles) + kTileOverheadRows);
             }
         }
-        jstar_s = best < 0 ? 1u : cand[best];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const int ov = __shfl_xor_sync(0xffffffffu, valid, o);
+            const double oe = __shfl_xor_sync(0xffffffffu, est, o);
+            const uint32_t oj = __shfl_xor_sync(0xffffffffu, J, o);
+            if (ov && (!valid || oe < est || (oe == est && oj > J))) {
+                valid = 1;
+                est = oe;
+                J = oj;
+            }
+        }
+        if (lane == 0) {
+            jstar_s = valid ? J : 1u;
+        }
     }
     __syncthreads();
     const uint32_t jstar = jstar_s;
@@ -295,18 +301,36 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     __syncthreads();
     // Records: tallest bucket first, classes in order inside a bucket (so
     // the queue ends on short tiles and neighbouring tiles share a class).
-    if (tid == 0) {
-        unsigned int pos = 0;
-        for (int b = kBuckets - 1; b >= 0; --b) {
-            for (int c = 0; c < kClasses; ++c) {
-                cursor[b][c] = pos;
-                pos += hist[b][c];
+    // Warp 0: lane l owns bucket 31 - l; an exclusive scan over the lanes
+    // gives each bucket's start.
+    static_assert(kBuckets == 32, "one lane per height bucket");
+    if (warp == 0) {
+        const int b = kBuckets - 1 - lane;
+        unsigned int total = 0;
+#pragma unroll
+        for (int c = 0; c < kClasses; ++c) {
+            total += hist[b][c];
+        }
+        unsigned int incl = total;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) {
+                incl += v;
             }
         }
-        hdr->total_tiles = pos;
-        hdr->next_tile[0] = 0;
-        hdr->next_tile[1] = 0;
-        hdr->iters_max = jstar;
+        unsigned int pos = incl - total;
+#pragma unroll
+        for (int c = 0; c < kClasses; ++c) {
+            cursor[b][c] = pos;
+            pos += hist[b][c];
+        }
+        if (lane == 31) {
+            hdr->total_tiles = incl;
+            hdr->next_tile[0] = 0;
+            hdr->next_tile[1] = 0;
+            hdr->iters_max = jstar;
+        }
     }
     __syncthreads();
 

@@ -23,8 +23,11 @@ LMCACHE_AESGCM_BACKEND switch selects it with the value "gpu".
 
 from __future__ import annotations
 
+import itertools
 import os
 import threading
+from collections import defaultdict
+from concurrent.futures import ThreadPoolExecutor
 
 from cryptography.exceptions import InvalidTag
 from lmcache.v1.distributed.serde.async_processor import AsyncSerdeProcessor
@@ -106,6 +109,20 @@ class GpuSerdeContext:
             self._local.stream = s
         return s
 
+    def batch(self, count: int):
+        """This thread's DeviceBatch with room for `count` objects (grown by
+        doubling; the descriptor array and workspace are reused)."""
+        from .batch import DeviceBatch
+
+        b = getattr(self._local, "batch", None)
+        if b is None or b.capacity < count:
+            cap = max(count, 2 * b.capacity if b is not None else 64)
+            if self._library is None:
+                self._library = GpuAesGcmLibrary()
+            b = DeviceBatch(self._library, cap, self.device)
+            self._local.batch = b
+        return b
+
     def close(self) -> None:
         with self._lock:
             for h in self._handles.values():
@@ -181,14 +198,148 @@ class GpuAesGcmDeserializer(Deserializer):
             raise InvalidTag("gpu aesgcm authentication failed")
 
 
+def _device_view(t, dev, n: int):
+    """`t` itself when it is on the device, else a device copy of its first n
+    bytes (a 1-byte placeholder when n == 0)."""
+    import torch
+
+    if n == 0:
+        return torch.empty(1, dtype=torch.uint8, device=dev)
+    return t if t.is_cuda else t[:n].to(dev, non_blocking=True)
+
+
 class GpuAesGcmSerdeProcessor(AsyncSerdeProcessor):
-    """AsyncSerdeProcessor that also releases the GPU key handles on close."""
+    """AsyncSerdeProcessor whose multi-object submits run as one batched
+    seal / open call per data-encryption key (lmcache_gpu_aes128gcm_*_batch_async)
+    instead of one call per object; single-object submits take the
+    per-object path. A batched deserialize reports False when any object
+    fails authentication; every failed object's destination is zeroed and the
+    authentic ones are written. Also releases the GPU key handles on close."""
 
     def __init__(self, ctx: GpuSerdeContext, max_workers: int = 1):
         super().__init__(GpuAesGcmSerializer(ctx), GpuAesGcmDeserializer(ctx), max_workers=max_workers)
         self._ctx = ctx
+        self._bpool = ThreadPoolExecutor(max_workers=max(1, int(max_workers)))
+        self._bids = itertools.count(1 << 40)   # disjoint from the base class's task ids
+        self._btasks = {}
+        self._block = threading.Lock()
+
+    # ---- batched tasks
+    def _bsubmit(self, fn, srcs, dsts, keys):
+        tid = next(self._bids)
+        with self._block:
+            self._btasks[tid] = self._bpool.submit(fn, list(srcs), list(dsts), list(keys))
+        return tid
+
+    def _bquery(self, tid):
+        with self._block:
+            fut = self._btasks.get(tid)
+        if fut is None or not fut.done():
+            return None
+        with self._block:
+            self._btasks.pop(tid, None)
+        return fut.exception() is None
+
+    def _groups(self, keys):
+        groups = defaultdict(list)
+        for i, k in enumerate(keys):
+            groups[self._ctx.keys.get_key(k.cache_salt)].append(i)
+        return groups
+
+    def _seal_many(self, srcs, dsts, keys):
+        import torch
+
+        ctx = self._ctx
+        dev = torch.device("cuda", ctx.device)
+        stream = ctx.stream()
+        for dek, idx in self._groups(keys).items():
+            handle = ctx.handle(dek)
+            keep, copies, entries = [], [], []
+            with torch.cuda.stream(stream):
+                for i in idx:
+                    src_t, dst_t = _bytes_view(srcs[i]), _bytes_view(dsts[i])
+                    P = src_t.numel()
+                    F = P + FRAME_OVERHEAD
+                    if dst_t.numel() < F:
+                        raise ValueError("gpu aesgcm: destination too small")
+                    src_d = _device_view(src_t, dev, P)
+                    frame_d = dst_t if dst_t.is_cuda else torch.empty(F, dtype=torch.uint8, device=dev)
+                    entries.append((src_d.data_ptr(), frame_d.data_ptr(), P, frame_d.numel(), os.urandom(12)))
+                    keep += [src_d, frame_d]
+                    if not dst_t.is_cuda:
+                        copies.append((dst_t, frame_d, F))
+                batch = ctx.batch(len(entries))
+                batch.seal(handle, entries, stream)
+                for dst_t, frame_d, F in copies:
+                    dst_t[:F].copy_(frame_d[:F], non_blocking=True)
+                status = batch.statuses().to("cpu", non_blocking=True)
+            stream.synchronize()
+            if bool(status.any()):
+                raise ValueError("gpu aesgcm: an object descriptor was rejected")
+        return True
+
+    def _open_many(self, srcs, dsts, keys):
+        import torch
+
+        ctx = self._ctx
+        dev = torch.device("cuda", ctx.device)
+        stream = ctx.stream()
+        failed = False
+        for dek, idx in self._groups(keys).items():
+            handle = ctx.handle(dek)
+            keep, copies, entries = [], [], []
+            with torch.cuda.stream(stream):
+                auth = torch.zeros(len(idx), dtype=torch.int32, device=dev)
+                for j, i in enumerate(idx):
+                    src_t, dst_t = _bytes_view(srcs[i]), _bytes_view(dsts[i])
+                    P = dst_t.numel()
+                    F = P + FRAME_OVERHEAD
+                    if src_t.numel() < F:
+                        raise ValueError("gpu aesgcm: malformed frame")
+                    frame_d = _device_view(src_t, dev, F)
+                    out_d = dst_t if dst_t.is_cuda and P else torch.empty(max(P, 1), dtype=torch.uint8, device=dev)
+                    entries.append((frame_d.data_ptr(), out_d.data_ptr(), P, F, auth.data_ptr() + 4 * j))
+                    keep += [frame_d, out_d]
+                    if P and not dst_t.is_cuda:
+                        copies.append((dst_t, out_d, P))
+                batch = ctx.batch(len(entries))
+                batch.open(handle, entries, stream)
+                for dst_t, out_d, P in copies:
+                    dst_t.copy_(out_d[:P], non_blocking=True)
+                auth_h = auth.to("cpu", non_blocking=True)
+                status = batch.statuses().to("cpu", non_blocking=True)
+            stream.synchronize()
+            if bool(status.any()):
+                raise ValueError("gpu aesgcm: an object descriptor was rejected")
+            failed = failed or bool((auth_h != 1).any())
+        if failed:
+            # the kernels zero-filled every rejected object's plaintext
+            raise InvalidTag("gpu aesgcm authentication failed")
+        return True
+
+    # ---- SerdeProcessor interface
+    def submit_serialize(self, srcs, dsts, keys):
+        if len(srcs) < 2:
+            return super().submit_serialize(srcs, dsts, keys)
+        return self._bsubmit(self._seal_many, srcs, dsts, keys)
+
+    def submit_deserialize(self, srcs, dsts, keys):
+        if len(srcs) < 2:
+            return super().submit_deserialize(srcs, dsts, keys)
+        return self._bsubmit(self._open_many, srcs, dsts, keys)
+
+    def query_serialize_result(self, tid):
+        if tid in self._btasks:
+            return self._bquery(tid)
+        return super().query_serialize_result(tid)
+
+    def query_deserialize_result(self, tid):
+        if tid in self._btasks:
+            return self._bquery(tid)
+        return super().query_deserialize_result(tid)
 
     def close(self):
+        self._bpool.shutdown(wait=True)
         super().close()
         self._ctx.close()
 

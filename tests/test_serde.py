@@ -245,3 +245,62 @@ def test_device_kv_tensor_to_host_frame_and_back(key_path):
     finally:
         gpu.close()
         native.close()
+
+
+def run_ser_many(proc, srcs, dsts, keys):
+    return wait(proc.query_serialize_result, proc.submit_serialize(srcs, dsts, keys))
+
+
+def run_de_many(proc, srcs, dsts, keys):
+    return wait(proc.query_deserialize_result, proc.submit_deserialize(srcs, dsts, keys))
+
+
+@pytest.mark.gpu
+def test_gpu_serde_multi_object_batches(key_path):
+    """A multi-object submit runs as one batched call per data-encryption key
+    (two tenants here): frames open with the reference's native backend, and
+    a batched open of native frames restores every object; one tampered
+    frame makes the task report False with only that object zeroed."""
+    import torch
+
+    sizes = [1, 17, 4096, (1 << 20) + 3, SIZE, 33]
+    keys = [KEY if i % 2 == 0 else OTHER_TENANT for i in range(len(sizes))]
+    rng = np.random.default_rng(5)
+    srcs = []
+    for n in sizes:
+        b = Buf(n)
+        ctypes.memmove(b.address, rng.integers(0, 256, size=n, dtype=np.uint8).tobytes(), n)
+        srcs.append(b)
+    gpu = processor("gpu", key_path)
+    native = processor("native", key_path)
+    try:
+        frames = [Buf(n + 29) for n in sizes]
+        assert run_ser_many(gpu, srcs, frames, keys) is True
+        for s, f, k in zip(srcs, frames, keys):
+            out = Buf(len(s.bytes()))
+            assert run_de(native, f, out, k) is True
+            assert out.bytes() == s.bytes()
+        # native seal -> GPU batched open, host and device destinations mixed
+        nframes = [Buf(n + 29) for n in sizes]
+        for s, f, k in zip(srcs, nframes, keys):
+            assert run_ser(native, s, f, k) is True
+        outs = [Buf(n) if i % 3 else DevObj(torch.zeros(n, dtype=torch.uint8, device="cuda"))
+                for i, n in enumerate(sizes)]
+        assert run_de_many(gpu, nframes, outs, keys) is True
+        for s, o in zip(srcs, outs):
+            got = o.bytes() if isinstance(o, Buf) else o.tensor.cpu().numpy().tobytes()
+            assert got == s.bytes()
+        # one tampered frame: task False, that object zeroed, the rest restored
+        memoryview(nframes[3]._arr).cast("B")[13 + 1000] ^= 0x10
+        outs = [Buf(n) for n in sizes]
+        for o in outs:
+            ctypes.memset(o.address, 0xCC, len(o.bytes()))
+        assert run_de_many(gpu, nframes, outs, keys) is False
+        for i, (s, o) in enumerate(zip(srcs, outs)):
+            if i == 3:
+                assert not any(o.bytes())
+            else:
+                assert o.bytes() == s.bytes()
+    finally:
+        gpu.close()
+        native.close()
