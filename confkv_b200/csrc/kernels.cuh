@@ -883,6 +883,52 @@ __device__ __forceinline__ void store_prefix_aligned(uint8_t* dst, uint4 v, uint
     }
 }
 
+// Bytes [4q + r, 4q + r + 16) of the 32-byte window (d, e) -- two adjacent
+// aligned 16-byte chunks -- for a runtime word offset q (0..3) and byte
+// offset r (in fsel = funnel_sel(r)).
+__device__ __forceinline__ uint4 window16(uint4 d, uint4 e, uint32_t q, uint32_t fsel)
+{
+    uint32_t w0 = d.x, w1 = d.y, w2 = d.z, w3 = d.w, w4 = e.x, w5 = e.y;
+    if (q & 2u) {
+        w0 = w2;
+        w1 = w3;
+        w2 = w4;
+        w3 = w5;
+        w4 = e.z;
+        w5 = e.w;
+    }
+    if (q & 1u) {
+        w0 = w1;
+        w1 = w2;
+        w2 = w3;
+        w3 = w4;
+        w4 = w5;
+    }
+    return make_uint4(funnel(w0, w1, fsel), funnel(w1, w2, fsel), funnel(w2, w3, fsel), funnel(w3, w4, fsel));
+}
+
+// Store of block c at p = dst + 16 i for a row whose 32 lanes all hold full
+// blocks inside the object, dst misaligned by 16 - s (s = 4 q + r, 1..15,
+// runtime): lanes 0..30 write the aligned chunk at p + s built from their
+// block and the next lane's; lane 31 writes the first 16 - s bytes of that
+// chunk and lane 0 its block's first s bytes. Every lane of the warp must
+// call this.
+__device__ __forceinline__ void store_funnel_rt(uint8_t* p, uint4 c, uint32_t s, uint32_t q, uint32_t fsel,
+                                                int lane)
+{
+    const uint4 nb = make_uint4(__shfl_down_sync(0xffffffffu, c.x, 1), __shfl_down_sync(0xffffffffu, c.y, 1),
+                                __shfl_down_sync(0xffffffffu, c.z, 1), __shfl_down_sync(0xffffffffu, c.w, 1));
+    const uint4 o = window16(c, nb, q, fsel);
+    if (lane < 31) {
+        *reinterpret_cast<uint4*>(p + s) = o;
+    } else {
+        store_prefix_aligned(p + s, o, 16u - s);
+    }
+    if (lane == 0) {
+        store_bytes(p, c, 0, static_cast<int>(s));
+    }
+}
+
 // Store of ciphertext block i at ctp = ct + 16 i for a row whose 32 lanes all
 // hold full blocks inside the object. SQ = 4: ct aligned, one vector store.
 // Otherwise lanes 0..30 write the aligned chunk at ctp + s built from their

@@ -61,13 +61,20 @@ __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk
     }
 
     // The interior loop takes kPair = 2 rows per iteration; it starts on an
-    // even row so row r lands in chain r mod R (R divides kPair).
+    // even row so row r lands in chain r mod R (R divides kPair). A
+    // misaligned plaintext is read as the two aligned 16-byte chunks around
+    // each block, so its interior blocks are 1 .. n_full - 2 (both chunks
+    // inside the object).
     constexpr int64_t kPair = 2;
     static_assert(kPair % R == 0, "chains must divide the rows per iteration");
+    constexpr int64_t kLoBlock = PT_ALIGNED ? 0 : 1;
     const int64_t n_full = static_cast<int64_t>(P / 16u);
-    const int64_t r_lo = base >= 0 ? 0 : (-base + T - 1) / T;
-    int64_t r_hi = (n_full - base) / T;
+    const int64_t r_lo = base >= kLoBlock ? 0 : (kLoBlock - base + T - 1) / T;
+    int64_t r_hi = (n_full - (PT_ALIGNED ? 0 : 1) - base) / T;
     r_hi = r_hi > rows ? rows : r_hi;
+    const uint32_t src_off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(t.src) & 15u);
+    const uint32_t src_q = src_off >> 2;
+    const uint32_t src_fsel = funnel_sel(src_off & 3u);
     int64_t r_a = (r_lo + kPair - 1) / kPair * kPair;
     r_a = r_a > r_hi ? r_hi : r_a;
     const int64_t ngroups = r_hi > r_a ? (r_hi - r_a) / kPair : 0;
@@ -94,20 +101,31 @@ __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk
         // Two rows per iteration: two AES chains (rounds 1-2 from the
         // counter cache), the GHASH chain, next pair's plaintext prefetched.
         const uint64_t i0 = static_cast<uint64_t>(base + r_a * T + tid);
-        const uint8_t* sp = t.src + i0 * 16u;
+        // aligned: the block itself; misaligned: the aligned chunk holding its first byte
+        const uint8_t* sp = reinterpret_cast<const uint8_t*>(
+            reinterpret_cast<uintptr_t>(t.src + i0 * 16u) & ~static_cast<uintptr_t>(PT_ALIGNED ? 0 : 15));
         uint8_t* cp = t.ct + i0 * 16u;
         uint32_t ctr = static_cast<uint32_t>(i0) + 2u;
         CtrCache cc{0xffffffffu, 0u, {0u, 0u, 0u, 0u}};
-        uint4 pf0 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(sp)) : load_bytes(sp, 16);
-        uint4 pf1 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(sp + kRowBytes)) : load_bytes(sp + kRowBytes, 16);
+        auto ld = [](const uint8_t* q) __attribute__((always_inline)) {
+            return __ldg(reinterpret_cast<const uint4*>(q));
+        };
+        uint4 pf0 = ld(sp);
+        uint4 pf1 = ld(sp + kRowBytes);
+        uint4 pg0 = PT_ALIGNED ? make_uint4(0, 0, 0, 0) : ld(sp + 16);
+        uint4 pg1 = PT_ALIGNED ? make_uint4(0, 0, 0, 0) : ld(sp + kRowBytes + 16);
 #pragma unroll 1
         for (int64_t g = 0; g < ngroups; ++g) {
-            const uint4 p0 = pf0;
-            const uint4 p1 = pf1;
+            const uint4 p0 = PT_ALIGNED ? pf0 : window16(pf0, pg0, src_q, src_fsel);
+            const uint4 p1 = PT_ALIGNED ? pf1 : window16(pf1, pg1, src_q, src_fsel);
             if (g + 1 < ngroups) {
                 const uint8_t* nx = sp + 2 * kRowBytes;
-                pf0 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(nx)) : load_bytes(nx, 16);
-                pf1 = PT_ALIGNED ? __ldg(reinterpret_cast<const uint4*>(nx + kRowBytes)) : load_bytes(nx + kRowBytes, 16);
+                pf0 = ld(nx);
+                pf1 = ld(nx + kRowBytes);
+                if (!PT_ALIGNED) {
+                    pg0 = ld(nx + 16);
+                    pg1 = ld(nx + kRowBytes + 16);
+                }
             }
             const uint4 m0 = gh_mul_rep<kSealGh>(ch.q[0], lb_lo, lb_hi);
             uint32_t x[4], y[4];
@@ -359,6 +377,10 @@ __device__ __forceinline__ void ctr_rows(const CtrTile& t, const uint32_t* rk, i
     aes_lane_bases(lb, lane);
     const uint32_t rk3x = bswap32(rk[3]);
     const uint32_t fsel = funnel_sel(t.load_r);
+    // misaligned destination: s = 16 - (dst & 15) for the funnel stores
+    const uint32_t dst_s = 16u - static_cast<uint32_t>(reinterpret_cast<uintptr_t>(t.dst) & 15u);
+    const uint32_t dst_q = (dst_s >> 2) & 3u;
+    const uint32_t dst_fsel = funnel_sel(dst_s & 3u);
 
     auto store_pt = [&](int64_t i, uint4 p) __attribute__((always_inline)) {
         const int nb = block_bytes(i, P);
@@ -424,8 +446,8 @@ __device__ __forceinline__ void ctr_rows(const CtrTile& t, const uint32_t* rk, i
                 *reinterpret_cast<uint4*>(dp) = p0;
                 *reinterpret_cast<uint4*>(dp + kRowBytes) = p1;
             } else {
-                store_bytes(dp, p0, 0, 16);
-                store_bytes(dp + kRowBytes, p1, 0, 16);
+                store_funnel_rt(dp, p0, dst_s, dst_q, dst_fsel, lane);
+                store_funnel_rt(dp + kRowBytes, p1, dst_s, dst_q, dst_fsel, lane);
             }
             cp += 2 * kRowBytes;
             dp += 2 * kRowBytes;

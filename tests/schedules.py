@@ -40,16 +40,31 @@ def pad_rows(base):
     return _trunc_div(-base, T) if base < 0 else 0
 
 
-def seal_tile_rows(base, rows, P):
-    """(generic rows, interior rows) of seal_rows for a tile."""
+def _split(pad, r_a, n_interior, rows):
+    """The row loops of the tile functions: r runs from the first non-padding
+    row up to r_a (generic), then the interior rows [r_a, r_a + n_interior)
+    when there are any, then generic rows from wherever r stands to `rows`."""
+    generic = list(range(pad, r_a))
+    r = max(pad, r_a)
+    interior = []
+    if n_interior > 0:
+        interior = list(range(r_a, r_a + n_interior))
+        r = r_a + n_interior
+    generic += list(range(r, rows))
+    return generic, interior
+
+
+def seal_tile_rows(base, rows, P, pt_aligned=True):
+    """(generic rows, interior rows) of seal_rows for a tile. A misaligned
+    plaintext reads the two aligned chunks around a block, so its interior
+    blocks are 1 .. n_full - 2."""
     n_full = P // 16
-    r_lo = 0 if base >= 0 else _trunc_div(-base + T - 1, T)
-    r_hi = min(_trunc_div(n_full - base, T), rows)
+    lo_block = 0 if pt_aligned else 1
+    r_lo = 0 if base >= lo_block else _trunc_div(lo_block - base + T - 1, T)
+    r_hi = min(_trunc_div(n_full - (0 if pt_aligned else 1) - base, T), rows)
     r_a = min(_trunc_div(r_lo + SEAL_PAIR - 1, SEAL_PAIR) * SEAL_PAIR, r_hi)
     ngroups = _trunc_div(r_hi - r_a, SEAL_PAIR) if r_hi > r_a else 0
-    interior = list(range(r_a, r_a + SEAL_PAIR * ngroups))
-    generic = list(range(pad_rows(base), r_a)) + list(range(r_a + SEAL_PAIR * ngroups, rows))
-    return generic, interior
+    return _split(pad_rows(base), r_a, SEAL_PAIR * ngroups, rows)
 
 
 def open_tile_rows(base, rows, P):
@@ -59,9 +74,7 @@ def open_tile_rows(base, rows, P):
     r_hi = min(_trunc_div(n_full - base, T), rows)
     r_a = min(_trunc_div(r_lo + OPEN_R - 1, OPEN_R) * OPEN_R, r_hi)
     ngroups = _trunc_div(r_hi - r_a, OPEN_R) if r_hi > r_a else 0
-    interior = list(range(r_a, r_a + OPEN_R * ngroups))
-    generic = list(range(pad_rows(base), r_a)) + list(range(r_a + OPEN_R * ngroups, rows))
-    return generic, interior
+    return _split(pad_rows(base), r_a, OPEN_R * ngroups, rows)
 
 
 def ctr_tile_rows(base, rows, P):
@@ -72,9 +85,7 @@ def ctr_tile_rows(base, rows, P):
     if r_lo > r_hi:
         r_lo = r_hi = rows
     npair = _trunc_div(r_hi - r_lo, CTR_PAIR)
-    interior = list(range(r_lo, r_lo + CTR_PAIR * npair))
-    generic = list(range(pad_rows(base), r_lo)) + list(range(r_lo + CTR_PAIR * npair, rows))
-    return generic, interior
+    return _split(pad_rows(base), r_lo, CTR_PAIR * npair, rows)
 
 
 def horner_grid(n, sms):

@@ -78,7 +78,7 @@ def test_plan_skips_invalid():
     assert plan[1] is None and all(q[0] != 1 for q in queue)
 
 
-def _check_tile(base, rows, P, lo_block, sched):
+def _check_tile(base, rows, P, lo_block, sched, hi_margin=0):
     generic, interior = sched(base, rows, P)
     pad = pad_rows(base)
     assert sorted(generic + interior) == list(range(pad, rows))
@@ -86,7 +86,7 @@ def _check_tile(base, rows, P, lo_block, sched):
     assert all(base + r * T + T - 1 < 0 for r in range(pad))
     n_full = P // 16
     for r in interior:
-        assert base + r * T >= lo_block and base + r * T + T - 1 < n_full, (base, rows, P, r)
+        assert base + r * T >= lo_block and base + r * T + T - 1 < n_full - hi_margin, (base, rows, P, r)
 
 
 SIZES = [0, 1, 15, 16, 17, 4095, 4096, 8191, 8192, 8193, 16 * 512 * 3 + 5, 16 * 512 * 80 - 1, (1 << 20) + 15,
@@ -103,5 +103,8 @@ def test_tile_rows_every_tile(P, J):
     for c in tiles:
         base = tile_base(n, J, G, c)
         _check_tile(base, J, P, 0, seal_tile_rows)
+        # misaligned plaintext: both aligned chunks of every interior block
+        # lie inside the object
+        _check_tile(base, J, P, 1, lambda b, r, p: seal_tile_rows(b, r, p, pt_aligned=False), hi_margin=1)
         _check_tile(base, J, P, 1, open_tile_rows)
         _check_tile(base, J, P, 1, ctr_tile_rows)
