@@ -20,25 +20,15 @@
 //   [0, 256)            BatchHeader
 //   [256, ...)          one Slot per object: acc, ticket, aux = {J, G, verdict}
 //   [tiles_offset, ...) TileRec per tile, at most count + kBatchExtraTiles
+//   [small_offset, ...) small objects (item indices), largest first
 #pragma once
 
+#include "small.cuh"
 #include "tiles.cuh"
 
 namespace confkv {
 namespace dev {
 
-// Device view of lmcache_gpu_aesgcm_batch_item (include/gpu_aesgcm_api.h).
-struct BatchItem {
-    const uint8_t* src;   // seal: plaintext; open: frame
-    uint8_t* dst;         // seal: frame; open: plaintext
-    uint64_t plen;
-    uint64_t capacity;    // seal: dst capacity; open: frame length
-    int* auth_ok;         // open only
-    uint32_t iv[3];       // seal only: IV bytes as little-endian words
-    int32_t status;       // written by the plan: 0 or ERR_ARGUMENT
-    uint64_t reserved;
-};
-static_assert(sizeof(BatchItem) == 64, "batch descriptor is 64 bytes");
 
 constexpr int kBatchWaves = 8;        // most tiles per SM the plan considers
 constexpr int kPlanCandidates = 16;   // tile heights the plan scores
@@ -52,8 +42,9 @@ constexpr uint32_t kBatchMaxItems = 1u << 20;
 constexpr int kPlanThreads = 1024;
 constexpr int kBuckets = 32;
 constexpr uint64_t kBatchMaxBlocks = 0xfffffffeull;
-constexpr uint32_t kCtrBatchMisc = kAesBytes;
+constexpr uint32_t kCtrBatchMisc = kSmallSmem;      // after the small-object tables
 constexpr uint32_t kCtrBatchSmem = kCtrBatchMisc + 64;
+constexpr int kSmallBuckets = 11;                   // floor(log2 n) of a small object, n <= 1024
 
 // Alignment classes: 2 v + p, v = the frame's ciphertext class (seal: store
 // funnel word part 0..3, 4 = aligned; open: load funnel word part, same
@@ -66,7 +57,9 @@ struct BatchHeader {
     uint32_t total_tiles;
     uint32_t next_tile[2];   // queue heads: [0] seal / open GHASH, [1] open CTR
     uint32_t iters_max;      // J*
-    uint32_t pad[12];
+    uint32_t small_count;    // objects of at most kSmallMaxBlocks blocks, one warp each
+    uint32_t small_next[2];  // small-object queue heads: [0] seal, [1] open
+    uint32_t pad[9];
 };
 static_assert(sizeof(BatchHeader) <= 256, "batch header fits its 256-byte area");
 
@@ -81,9 +74,13 @@ __host__ __device__ constexpr size_t batch_tiles_offset(size_t count)
 {
     return 256 + (count * sizeof(Slot) + 255) / 256 * 256;
 }
-__host__ __device__ constexpr size_t batch_workspace_bytes(size_t count)
+__host__ __device__ constexpr size_t batch_small_offset(size_t count)
 {
     return batch_tiles_offset(count) + (count + kBatchExtraTiles) * sizeof(TileRec);
+}
+__host__ __device__ constexpr size_t batch_workspace_bytes(size_t count)
+{
+    return batch_small_offset(count) + count * sizeof(uint32_t);
 }
 
 struct BatchArgs {
@@ -145,8 +142,12 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     __shared__ uint32_t max_rows;
     __shared__ uint32_t cand[kPlanCandidates];
     __shared__ unsigned long long cand_tiles[kPlanCandidates];
+    __shared__ uint32_t cand_part[kPlanThreads / 32][kPlanCandidates];
     __shared__ uint32_t jstar_s;
+    __shared__ unsigned int small_hist[kSmallBuckets];
+    __shared__ unsigned int small_cursor[kSmallBuckets];
     BatchHeader* hdr = reinterpret_cast<BatchHeader*>(ws);
+    uint32_t* small_list = reinterpret_cast<uint32_t*>(ws + batch_small_offset(count));
     Slot* st = reinterpret_cast<Slot*>(ws + batch_slots_offset());
     TileRec* rec = reinterpret_cast<TileRec*>(ws + batch_tiles_offset(count));
     const int tid = threadIdx.x;
@@ -155,6 +156,10 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     for (int i = tid; i < kClasses * kBuckets; i += kPlanThreads) {
         hist[i / kClasses][i % kClasses] = 0;
     }
+    if (tid < kSmallBuckets) {
+        small_hist[tid] = 0;
+    }
+    __syncthreads();
     pdl_wait();  // descriptors and workspace may belong to earlier work on the stream
 
     // Pass 1: validate, rows per object (a zero-length object is one row:
@@ -169,7 +174,10 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         if (open) {
             ok = ok && it.auth_ok != nullptr;
         }
-        const uint32_t rows = ok ? static_cast<uint32_t>(n == 0 ? 1 : (n + T - 1) / T) : 0u;
+        // small objects go to the warp-per-object list (aux[2] = bucket + 1),
+        // the others to the tile planner (aux[0] = rows)
+        const bool small = ok && n <= kSmallMaxBlocks;
+        const uint32_t rows = ok && !small ? static_cast<uint32_t>((n + T - 1) / T) : 0u;
         it.status = ok ? 0 : -1;
         Slot& s = st[i];
         s.acc_hi = 0;
@@ -178,6 +186,11 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         s.aux[0] = rows;
         s.aux[1] = 0;
         s.aux[2] = 0;
+        if (small) {
+            const int b = 31 - __clz(static_cast<int>(n | 1u));
+            s.aux[2] = static_cast<uint32_t>(b + 1);
+            atomicAdd(&small_hist[b], 1u);
+        }
         rows_sum += rows;
         rows_max = rows > rows_max ? rows : rows_max;
     }
@@ -217,34 +230,57 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     const unsigned long long R = total_rows;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    // One warp per candidate counts its tiles (a shuffle reduction, no
-    // shared atomics).
-    if (warp < kPlanCandidates) {
+    // Tile counts per candidate: every thread counts its own objects for all
+    // candidates, then a warp shuffle reduction and a sum over the warps.
+    if (tid < kPlanCandidates) {
         unsigned long long j;
-        if (warp < 8) {
-            const unsigned long long slots = static_cast<unsigned long long>(warp + 1) * sms;
+        if (tid < 8) {
+            const unsigned long long slots = static_cast<unsigned long long>(tid + 1) * sms;
             j = (R + slots - 1) / slots;
         } else {
-            const uint32_t k = static_cast<uint32_t>(warp - 7);
+            const uint32_t k = static_cast<uint32_t>(tid - 7);
             j = (max_rows + k - 1) / k;
         }
         j = j > max_rows ? max_rows : j;
-        const uint32_t J = static_cast<uint32_t>(j < 1 ? 1 : j);
-        unsigned long long tiles = 0;
-        for (uint32_t i = lane; i < count; i += 32) {
+        cand[tid] = static_cast<uint32_t>(j < 1 ? 1 : j);
+    }
+    __syncthreads();
+    {
+        uint32_t loc[kPlanCandidates];
+#pragma unroll
+        for (int c = 0; c < kPlanCandidates; ++c) {
+            loc[c] = 0;
+        }
+        for (uint32_t i = tid; i < count; i += kPlanThreads) {
             const uint32_t rows = st[i].aux[0];
-            if (rows != 0) {
-                tiles += rows <= J ? 1u : (rows + J - 1) / J;
+            if (rows == 0) {
+                continue;
+            }
+#pragma unroll
+            for (int c = 0; c < kPlanCandidates; ++c) {
+                const uint32_t J = cand[c];
+                loc[c] += rows <= J ? 1u : (rows + J - 1) / J;
             }
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            tiles += __shfl_xor_sync(0xffffffffu, tiles, o);
+        for (int c = 0; c < kPlanCandidates; ++c) {
+            uint32_t v = loc[c];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                v += __shfl_xor_sync(0xffffffffu, v, o);
+            }
+            if (lane == 0) {
+                cand_part[warp][c] = v;
+            }
         }
-        if (lane == 0) {
-            cand[warp] = J;
-            cand_tiles[warp] = tiles;
+    }
+    __syncthreads();
+    if (tid < kPlanCandidates) {
+        unsigned long long t = 0;
+        for (int w = 0; w < kPlanThreads / 32; ++w) {
+            t += cand_part[w][tid];
         }
+        cand_tiles[tid] = t;
     }
     __syncthreads();
     // Warp 0 scores the candidates (lane c = candidate c) and keeps the
@@ -331,14 +367,27 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
             hdr->next_tile[1] = 0;
             hdr->iters_max = jstar;
         }
+    } else if (warp == 1 && lane == 0) {
+        // small objects: largest bucket first
+        unsigned int pos = 0;
+        for (int b = kSmallBuckets - 1; b >= 0; --b) {
+            small_cursor[b] = pos;
+            pos += small_hist[b];
+        }
+        hdr->small_count = pos;
+        hdr->small_next[0] = 0;
+        hdr->small_next[1] = 0;
     }
     __syncthreads();
 
-    // Pass 3: tile records.
+    // Pass 3: tile records and the small-object list.
     for (uint32_t i = tid; i < count; i += kPlanThreads) {
         const Slot& s = st[i];
         const uint32_t G = s.aux[1];
         if (G == 0) {
+            if (s.aux[2] != 0 && s.aux[0] == 0) {
+                small_list[atomicAdd(&small_cursor[s.aux[2] - 1], 1u)] = i;
+            }
             continue;
         }
         const uint32_t cls = static_cast<uint32_t>(item_class(items[i], open));
@@ -515,6 +564,38 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
         default: tile = seal_class<4, true>(smem, a, c, tile, cls); break;
         }
     }
+
+    // Small objects, one warp each, once the tiles are gone: restore the AES
+    // tables the last fold may have overwritten, then H^32 and H^8.
+    const uint32_t small_count = hdr->small_count;
+    if (small_count == 0) {
+        return;
+    }
+    __syncthreads();
+    for (int i = tid; i < 4096; i += blockDim.x) {
+        const int x = (i >> 3) & 255;
+        if (x < static_cast<int>(kSealLateBytes >> 8)) {
+            const int kk = i >> 11;
+            const uint32_t tv = __ldg(a.kt.aes_t + kk * 256 + x);
+            const uint32_t off = (static_cast<uint32_t>(x) << 8) | (static_cast<uint32_t>(kk & 1) << 7) |
+                                 (static_cast<uint32_t>(i & 7) << 4);
+            *reinterpret_cast<uint4*>(smem + kSealAes + off) = make_uint4(tv, tv, tv, tv);
+        }
+    }
+    small_fill_seal_tables(smem, a.kt.gh_pow2);
+    __syncthreads();
+    const uint32_t* small_list = reinterpret_cast<const uint32_t*>(a.ws + batch_small_offset(a.count));
+    for (;;) {
+        uint32_t k = 0;
+        if (c.lane == 0) {
+            k = atomicAdd(&hdr->small_next[0], 1u);
+        }
+        k = __shfl_sync(0xffffffffu, k, 0);
+        if (k >= small_count) {
+            break;
+        }
+        seal_object_warp(a.items + small_list[k], a.rk, a.kt.gh_pow2, smem, c.lane);
+    }
 }
 
 // ------------------------------------------------------------------ open
@@ -668,6 +749,7 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const Ba
     const int tid = threadIdx.x;
     pdl_release();
     fill_aes_smem(smem, a.kt.aes_t);
+    small_fill_open_tables(smem, a.kt.gh_pow2);
     pdl_wait();  // the verdicts of the GHASH pass
     auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
     const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
@@ -689,6 +771,22 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const Ba
         case 8: tile = ctr_class<4, false>(smem, a, c, tile, cls, round); break;
         default: tile = ctr_class<4, true>(smem, a, c, tile, cls, round); break;
         }
+    }
+
+    // Small objects: one warp opens a whole object (GHASH, tag check, CTR),
+    // so its plaintext waits for nothing outside the warp.
+    const uint32_t small_count = hdr->small_count;
+    const uint32_t* small_list = reinterpret_cast<const uint32_t*>(a.ws + batch_small_offset(a.count));
+    for (;;) {
+        uint32_t k = 0;
+        if (c.lane == 0) {
+            k = atomicAdd(&hdr->small_next[1], 1u);
+        }
+        k = __shfl_sync(0xffffffffu, k, 0);
+        if (k >= small_count) {
+            break;
+        }
+        open_object_warp(a.items + small_list[k], a.rk, a.kt.gh_pow2, smem, c.lane);
     }
 }
 

@@ -141,6 +141,19 @@ __device__ __forceinline__ void pdl_release()
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Device view of lmcache_gpu_aesgcm_batch_item (include/gpu_aesgcm_api.h).
+struct BatchItem {
+    const uint8_t* src;   // seal: plaintext; open: frame
+    uint8_t* dst;         // seal: frame; open: plaintext
+    uint64_t plen;
+    uint64_t capacity;    // seal: dst capacity; open: frame length
+    int* auth_ok;         // open only
+    uint32_t iv[3];       // seal only: IV bytes as little-endian words
+    int32_t status;       // written by the plan: 0 or ERR_ARGUMENT
+    uint64_t reserved;
+};
+static_assert(sizeof(BatchItem) == 64, "batch descriptor is 64 bytes");
+
 // ---------------------------------------------------------------- helpers
 
 __device__ __forceinline__ uint32_t bswap32(uint32_t x)
@@ -927,6 +940,52 @@ __device__ __forceinline__ void store_funnel_rt(uint8_t* p, uint4 c, uint32_t s,
     if (lane == 0) {
         store_bytes(p, c, 0, static_cast<int>(s));
     }
+}
+
+// store_ct_block for a ciphertext pointer misaligned by a runtime 16 - s
+// (s = 4 q + r in 1..15, fsel = funnel_sel(r)): same chunk / byte split.
+// Every lane of the warp must call this.
+__device__ __forceinline__ void store_ct_block_rt(uint8_t* ct, int64_t i, uint4 c, int nb, uint64_t P, uint32_t s,
+                                                  uint32_t q, uint32_t fsel, int lane)
+{
+    const uint64_t off = static_cast<uint64_t>(i) * 16u;
+    const uint4 nbv = make_uint4(__shfl_down_sync(0xffffffffu, c.x, 1), __shfl_down_sync(0xffffffffu, c.y, 1),
+                                 __shfl_down_sync(0xffffffffu, c.z, 1), __shfl_down_sync(0xffffffffu, c.w, 1));
+    const bool valid = nb > 0;
+    const bool full = valid && lane < 31 && off + s + 16 <= P;
+    const bool prev_full = valid && lane > 0 && i >= 1 && off + s <= P;
+    if (full) {
+        *reinterpret_cast<uint4*>(ct + off + s) = window16(c, nbv, q, fsel);
+    } else if (valid) {
+        store_bytes(ct + off, c, static_cast<int>(s), nb);
+    }
+    if (valid && !prev_full) {
+        store_bytes(ct + off, c, 0, nb < static_cast<int>(s) ? nb : static_cast<int>(s));
+    }
+}
+
+// Ciphertext block i of a frame (zero outside the object) with a runtime
+// load class: off = (frame + 13) & 15, q = off >> 2, fsel = funnel_sel(off
+// & 3). Full blocks whose two aligned chunks lie inside the frame take two
+// vector loads and a funnel; edge blocks take byte loads.
+__device__ __forceinline__ uint4 ct_block_rt(const uint8_t* frame, uint64_t frame_len, int64_t i, uint64_t P,
+                                             uint32_t off, uint32_t q, uint32_t fsel)
+{
+    const int nb = block_bytes(i, P);
+    if (nb == 0) {
+        return make_uint4(0, 0, 0, 0);
+    }
+    const uint8_t* ct = frame + 13 + static_cast<uint64_t>(i) * 16u;
+    if (nb == 16) {
+        if (off == 0) {
+            return *reinterpret_cast<const uint4*>(ct);
+        }
+        const uint8_t* c0 = ct - off;
+        if (c0 >= frame && c0 + 32 <= frame + frame_len) {
+            return window16(*reinterpret_cast<const uint4*>(c0), *reinterpret_cast<const uint4*>(c0 + 16), q, fsel);
+        }
+    }
+    return load_bytes(ct, nb);
 }
 
 // Store of ciphertext block i at ctp = ct + 16 i for a row whose 32 lanes all

@@ -21,6 +21,7 @@ CTR_PAIR = 2
 BATCH_WAVES = 8      # kBatchWaves
 BATCH_MAX_SMS = 256  # kBatchMaxSms
 PLAN_CANDIDATES = 16  # kPlanCandidates
+SMALL_MAX_BLOCKS = 1024  # kSmallMaxBlocks
 TILE_OVERHEAD_ROWS = 4.0  # kTileOverheadRows
 BATCH_EXTRA = BATCH_WAVES * BATCH_MAX_SMS
 
@@ -129,15 +130,18 @@ def plan_tile_height(rows, sms, count):
 
 
 def batch_plan(lens, sms, valid=None):
-    """batch_plan_kernel: returns (jstar, [(J, G) or None per object], queue)
-    where the queue lists (object, tile) in device order up to the order
-    inside one bucket (the device fills a bucket with atomics)."""
+    """batch_plan_kernel: returns (jstar, [(J, G), or None for an invalid or
+    small object, per object], queue) where the queue lists (object, tile) in
+    device order up to the order inside one bucket (the device fills a bucket
+    with atomics)."""
     count = len(lens)
     valid = valid if valid is not None else [True] * count
     rows = []
     for P, ok in zip(lens, valid):
         n = cdiv(P, 16)
-        rows.append((1 if n == 0 else cdiv(n, T)) if ok else 0)
+        # objects of at most SMALL_MAX_BLOCKS blocks take the warp-per-object
+        # path and get no tiles
+        rows.append(cdiv(n, T) if ok and n > SMALL_MAX_BLOCKS else 0)
     sms = min(sms, BATCH_MAX_SMS)
     jstar = plan_tile_height(rows, sms, count)
     plan = []

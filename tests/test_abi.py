@@ -131,9 +131,9 @@ def test_seal_noalloc_argument_errors(cpu_lib):
 def test_batch_workspace_size(cpu_lib):
     ws = cpu_lib.batch_workspace_size
     # header 256 B, one 32-B slot per object (rounded to 256 B), 8-B tile
-    # records for count + 2048 tiles
+    # records for count + 2048 tiles, a 4-B small-object list entry each
     for count in (1, 7, 8, 9, 4096, 1 << 20):
-        assert ws(count) == 256 + (count * 32 + 255) // 256 * 256 + (count + 2048) * 8
+        assert ws(count) == 256 + (count * 32 + 255) // 256 * 256 + (count + 2048) * 8 + count * 4
     assert ws((1 << 20) + 1) == 0
 
 

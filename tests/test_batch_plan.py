@@ -8,8 +8,8 @@ import math
 import numpy as np
 import pytest
 
-from schedules import (BATCH_EXTRA, T, batch_plan, cdiv, ctr_tile_rows, open_tile_rows, pad_rows,
-                       seal_tile_rows, tile_base)
+from schedules import (BATCH_EXTRA, SMALL_MAX_BLOCKS, T, batch_plan, cdiv, ctr_tile_rows, open_tile_rows,
+                       pad_rows, seal_tile_rows, tile_base)
 
 
 def _ragged(count, seed, lo=4096, hi=1 << 20):
@@ -41,8 +41,11 @@ def test_plan_bound_order_and_partition(name, sms):
     assert all((a.bit_length() >= b.bit_length()) for a, b in zip(js, js[1:]))
     assert len(set(queue)) == len(queue)
     for i, P in enumerate(lens):
-        J, G = plan[i]
         n = cdiv(P, 16)
+        if n <= SMALL_MAX_BLOCKS:
+            assert plan[i] is None and all(q[0] != i for q in queue)   # one warp, no tiles
+            continue
+        J, G = plan[i]
         assert 1 <= J <= jstar and G >= 1
         assert sum(1 for q in queue if q[0] == i) == G if len(lens) < 200 else True
         # tiles cover [0, n) exactly once; only tile 0 may start below 0
