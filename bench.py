@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--objects", type=int, default=OBJECTS, help="objects per GPU per step (profiling runs)")
     ap.add_argument("--cpu-sample-objects", type=int, default=0,
                     help="objects per OpenSSL thread in the cpu_baseline sample (0 = auto)")
+    ap.add_argument("--cpu-sweep", action="store_true",
+                    help="with --impl reference: also time seal and open of single objects 4 KiB..1 GiB "
+                         "on all host cores (the CPU side of the size sweep), one JSON line per size")
     return ap.parse_args()
 
 
@@ -494,6 +497,51 @@ def cpu_baseline(args) -> dict:
                       f"reference lmcache_aes128gcm_seal/open (OpenSSL EVP)"}
 
 
+def cpu_sweep_sizes(lib, key: bytes, threads: int) -> None:
+    """Seal and open of single objects of 2^k bytes (k = 12..30) with the
+    reference OpenSSL backend on `threads` host threads (fewer for large
+    objects so the buffers stay under ~8 GiB), ~2 GiB of plaintext per leg."""
+    for k in range(12, 31):
+        P = 1 << k
+        nth = max(1, min(threads, (8 << 30) // (3 * P)))
+        per = max(1, min(1 << 16, (2 << 30) // (P * nth)))  # ~2 GiB per leg
+        src = np.random.default_rng(k).integers(0, 256, size=P, dtype=np.uint8)
+        bufs = [(np.empty(P + 29, dtype=np.uint8), np.empty(P, dtype=np.uint8)) for _ in range(nth)]
+        errors = []
+
+        def run(op):
+            barrier = threading.Barrier(nth + 1)
+
+            def worker(t):
+                f, o = bufs[t]
+                barrier.wait()
+                for _ in range(per):
+                    if op == "seal":
+                        rc = lib.lmcache_aes128gcm_seal(key, src.ctypes.data, P, f.ctypes.data, P + 29)
+                    else:
+                        rc = lib.lmcache_aes128gcm_open(key, f.ctypes.data, P + 29, o.ctypes.data, P)
+                    if rc != 0:
+                        errors.append(op)
+
+            ths = [threading.Thread(target=worker, args=(t,)) for t in range(nth)]
+            for th in ths:
+                th.start()
+            barrier.wait()
+            t0 = time.perf_counter()
+            for th in ths:
+                th.join()
+            return time.perf_counter() - t0
+
+        run("seal")  # warm-up, and frames for the open leg
+        ts = run("seal")
+        to = run("open")
+        assert not errors and np.array_equal(bufs[0][1], src)
+        total = P * per * nth
+        print(json.dumps({"sweep": "cpu_reference", "object_bytes": P, "threads": nth, "objects": per * nth,
+                          "seal_gbs": round(total / ts / 1e9, 2), "open_gbs": round(total / to / 1e9, 2),
+                          "impl": "reference (OpenSSL EVP lmcache_aes128gcm_seal/open)"}), flush=True)
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -527,6 +575,8 @@ def run_reference(args, rank, world):
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+    if args.cpu_sweep:
+        cpu_sweep_sizes(lib, key, threads)
 
 
 def main():
