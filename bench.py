@@ -15,8 +15,9 @@ and e2e (host buffers, copies timed) goes through the per-object calls.
                   [--api both|batched|per_object]
 
 --impl reference times the reference's own OpenSSL CPU backend
-(lmcache_aes128gcm_seal/open from oracle/_ref/libcpu_seal.so) on the host
-cores with one thread per core, on the same objects, metric and unit.
+(lmcache_aes128gcm_seal/open from oracle/_ref/libcpu_seal.so, driven by the
+native pthread loop oracle/_ref/libcpu_threads.so) on the host cores with one
+thread per core, on the same objects, metric and unit.
 """
 
 from __future__ import annotations
@@ -28,11 +29,9 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import time
 from pathlib import Path
 
-import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
@@ -426,63 +425,35 @@ def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
 # ------------------------------------------------------- CPU (reference)
 
 def load_ref_lib():
-    so = ROOT / "oracle" / "_ref" / "libcpu_seal.so"
+    """The native pthread driver around the reference's OpenSSL backend
+    (oracle/_ref/libcpu_threads.so linked to oracle/_ref/libcpu_seal.so)."""
+    so = ROOT / "oracle" / "_ref" / "libcpu_threads.so"
     if not so.exists():
         subprocess.run(["make", "-C", str(ROOT / "oracle"), "ref"], capture_output=True)
     if not so.exists():
         return None
     lib = ctypes.CDLL(str(so))
-    vp, sz = ctypes.c_void_p, ctypes.c_size_t
-    lib.lmcache_aes128gcm_seal.argtypes = [vp, vp, sz, vp, sz]
-    lib.lmcache_aes128gcm_seal.restype = ctypes.c_int
-    lib.lmcache_aes128gcm_open.argtypes = [vp, vp, sz, vp, sz]
-    lib.lmcache_aes128gcm_open.restype = ctypes.c_int
+    dp = ctypes.POINTER(ctypes.c_double)
+    lib.cpu_threads_sweep.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_long, dp, dp]
+    lib.cpu_threads_sweep.restype = ctypes.c_int
     return lib
 
 
-def openssl_threads_run(lib, key: bytes, objects_per_thread: int, threads: int, P: int) -> float:
-    """Each thread seals then opens `objects_per_thread` objects of P bytes
-    (its own bf16 N(0,1) buffer); returns wall seconds for the whole batch."""
-    from confkv_b200 import workloads
-
-    src = workloads.bf16_batch(SHAPE, 1, seed=SEED * 100).view(-1).view(__import__("torch").uint8).numpy()
-    bufs = []
-    for _ in range(threads):
-        s = np.array(src, copy=True)
-        f = np.empty(P + 29, dtype=np.uint8)
-        o = np.empty(P, dtype=np.uint8)
-        f[:] = 0
-        o[:] = 0
-        bufs.append((s, f, o))
-    errors = []
-    start_evt = threading.Barrier(threads + 1)
-
-    def worker(t):
-        s, f, o = bufs[t]
-        start_evt.wait()
-        for _ in range(objects_per_thread):
-            if lib.lmcache_aes128gcm_seal(key, s.ctypes.data, P, f.ctypes.data, P + 29) != 0:
-                errors.append("seal")
-            if lib.lmcache_aes128gcm_open(key, f.ctypes.data, P + 29, o.ctypes.data, P) != 0:
-                errors.append("open")
-
-    ths = [threading.Thread(target=worker, args=(t,)) for t in range(threads)]
-    for th in ths:
-        th.start()
-    start_evt.wait()
-    t0 = time.perf_counter()
-    for th in ths:
-        th.join()
-    dt = time.perf_counter() - t0
-    assert not errors, errors[:3]
-    assert np.array_equal(bufs[0][2], bufs[0][0])
-    return dt
+def openssl_threads_run(lib, key: bytes, per: int, threads: int, P: int) -> tuple[float, float]:
+    """`threads` native threads each seal `per` objects of P bytes, then open
+    them `per` times (reference lmcache_aes128gcm_seal/open); returns the wall
+    seconds of the seal leg and of the open leg."""
+    ts, to = ctypes.c_double(), ctypes.c_double()
+    kb = (ctypes.c_uint8 * 16).from_buffer_copy(key)
+    rc = lib.cpu_threads_sweep(kb, P, threads, per, ctypes.byref(ts), ctypes.byref(to))
+    assert rc == 0, "reference backend failed"
+    return ts.value, to.value
 
 
 def cpu_baseline(args) -> dict:
     lib = load_ref_lib()
     if lib is None:
-        return {"unavailable": "oracle/_ref/libcpu_seal.so missing"}
+        return {"unavailable": "oracle/_ref/libcpu_threads.so missing"}
     from confkv_b200 import workloads
 
     P = workloads.nbytes_of(SHAPE)
@@ -490,56 +461,28 @@ def cpu_baseline(args) -> dict:
     per = args.cpu_sample_objects or max(1, 64 // threads)
     key = workloads.make_key(SEED)
     openssl_threads_run(lib, key, 1, threads, P)  # warm-up: page-in buffers
-    dt = openssl_threads_run(lib, key, per, threads, P)
-    gbs = 2 * per * threads * P / dt / 1e9
+    ts, to = openssl_threads_run(lib, key, per, threads, P)
+    gbs = 2 * per * threads * P / (ts + to) / 1e9
     return {"value": round(gbs, 2), "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": f"{per} x 32 MiB bf16 KV object(s) sealed+opened per thread, {threads} threads, "
+            "sample": f"{per} x 32 MiB object(s) sealed then opened per thread, {threads} native threads, "
                       f"reference lmcache_aes128gcm_seal/open (OpenSSL EVP)"}
 
 
 def cpu_sweep_sizes(lib, key: bytes, threads: int) -> None:
     """Seal and open of single objects of 2^k bytes (k = 12..30) with the
-    reference OpenSSL backend on `threads` host threads (fewer for large
-    objects so the buffers stay under ~8 GiB), ~2 GiB of plaintext per leg."""
+    reference OpenSSL backend on `threads` native host threads (fewer for
+    large objects so the buffers stay under ~8 GiB), ~2 GiB of plaintext per
+    leg."""
     for k in range(12, 31):
         P = 1 << k
         nth = max(1, min(threads, (8 << 30) // (3 * P)))
-        per = max(1, min(1 << 16, (2 << 30) // (P * nth)))  # ~2 GiB per leg
-        src = np.random.default_rng(k).integers(0, 256, size=P, dtype=np.uint8)
-        bufs = [(np.empty(P + 29, dtype=np.uint8), np.empty(P, dtype=np.uint8)) for _ in range(nth)]
-        errors = []
-
-        def run(op):
-            barrier = threading.Barrier(nth + 1)
-
-            def worker(t):
-                f, o = bufs[t]
-                barrier.wait()
-                for _ in range(per):
-                    if op == "seal":
-                        rc = lib.lmcache_aes128gcm_seal(key, src.ctypes.data, P, f.ctypes.data, P + 29)
-                    else:
-                        rc = lib.lmcache_aes128gcm_open(key, f.ctypes.data, P + 29, o.ctypes.data, P)
-                    if rc != 0:
-                        errors.append(op)
-
-            ths = [threading.Thread(target=worker, args=(t,)) for t in range(nth)]
-            for th in ths:
-                th.start()
-            barrier.wait()
-            t0 = time.perf_counter()
-            for th in ths:
-                th.join()
-            return time.perf_counter() - t0
-
-        run("seal")  # warm-up, and frames for the open leg
-        ts = run("seal")
-        to = run("open")
-        assert not errors and np.array_equal(bufs[0][1], src)
+        per = max(1, min(1 << 19, (2 << 30) // (P * nth)))
+        ts, to = openssl_threads_run(lib, key, per, nth, P)
         total = P * per * nth
         print(json.dumps({"sweep": "cpu_reference", "object_bytes": P, "threads": nth, "objects": per * nth,
                           "seal_gbs": round(total / ts / 1e9, 2), "open_gbs": round(total / to / 1e9, 2),
-                          "impl": "reference (OpenSSL EVP lmcache_aes128gcm_seal/open)"}), flush=True)
+                          "impl": "reference (OpenSSL EVP lmcache_aes128gcm_seal/open), native threads"}),
+              flush=True)
 
 
 def run_reference(args, rank, world):
@@ -559,19 +502,19 @@ def run_reference(args, rank, world):
     per = max(1, -(-total_objects // threads))
     for _ in range(args.warmup):
         openssl_threads_run(lib, key, per, threads, P)
-    times = [openssl_threads_run(lib, key, per, threads, P) for _ in range(args.steps)]
+    times = [sum(openssl_threads_run(lib, key, per, threads, P)) for _ in range(args.steps)]
     objs_done = per * threads
     ms = statistics.mean(times) * 1e3
     value = 2 * objs_done * P / (ms * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u8", "data": "synthetic: bf16 N(0,1) KV chunk, host buffers",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic: random bytes, 32 MiB host buffers",
         "config": {"workload": WORKLOAD, "objects_per_step": objs_done, "object_bytes": P,
-                   "step": "seal then open each object on host threads"},
+                   "step": "seal then open each object on native host threads"},
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": f"{objs_done} x 32 MiB objects per step over {threads} threads"},
+                         "sample": f"{objs_done} x 32 MiB objects per step over {threads} native threads"},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
