@@ -226,3 +226,46 @@ def test_batch_many_small_objects(gpu_lib, oracle):
         expected = oracle.evp_seal_many(key, ivs, pts)
         for i in range(len(lens)):
             assert np.array_equal(frames[fr_off[i]:fr_off[i] + lens[i] + 29], expected[i]), (i, lens[i])
+
+
+def test_batch_two_hundred_thousand_tiny_objects(gpu_lib, oracle):
+    """200,000 objects of 0..256 bytes in one seal and one open call (the
+    warp-per-object path, a plan over hundreds of objects per thread); every
+    frame equals OpenSSL's; one object in 1,000 is tampered and rejected."""
+    rng = np.random.default_rng(77)
+    count = 200_000
+    lens = rng.integers(0, 257, size=count).astype(np.int64)
+    key = rng.bytes(16)
+    ivs = [rng.bytes(12) for _ in range(count)]
+    pt_all = rng.integers(0, 256, size=int(lens.sum()) + 16, dtype=np.uint8)
+    pt_off, pt_total = _packed(lens)
+    fr_off, fr_total = _packed(lens + 29)
+    pts = [pt_all[pt_off[i]:pt_off[i] + lens[i]] for i in range(count)]
+    d_plain = torch.from_numpy(pt_all).cuda()
+    d_frames = torch.zeros(fr_total + 16, dtype=torch.uint8, device="cuda")
+    d_out = torch.full((pt_total + 16,), 0xCC, dtype=torch.uint8, device="cuda")
+    d_auth = torch.full((count,), 7, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    batch = DeviceBatch(gpu_lib, count)
+    with GpuAes128GcmKey(gpu_lib, key) as k:
+        batch.seal(k, _seal_entries(d_plain, pt_off, d_frames, fr_off, lens, ivs), s)
+        s.synchronize()
+        assert not batch.statuses().any()
+        frames = d_frames.cpu().numpy()
+        expected = oracle.evp_seal_many(key, ivs, pts)
+        for i in range(count):
+            assert np.array_equal(frames[fr_off[i]:fr_off[i] + lens[i] + 29], expected[i]), i
+        bad = set(int(x) for x in rng.choice(count, size=count // 1000, replace=False))
+        for i in bad:
+            frames[fr_off[i] + 13 + int(lens[i]) + int(rng.integers(0, 16))] ^= 0x20   # a tag byte
+        d_frames.copy_(torch.from_numpy(frames))
+        batch.open(k, _open_entries(d_frames, fr_off, d_out, pt_off, lens, d_auth, range(count)), s)
+        s.synchronize()
+    auth = d_auth.cpu().numpy()
+    out = d_out.cpu().numpy()
+    for i in range(count):
+        seg = out[pt_off[i]:pt_off[i] + lens[i]]
+        if i in bad:
+            assert auth[i] == 0 and not seg.any(), i
+        else:
+            assert auth[i] == 1 and np.array_equal(seg, pts[i]), i
