@@ -71,19 +71,26 @@ __device__ __forceinline__ uint4 shfl4(uint4 v, int src)
                       __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
 }
 
-// GHASH of the object from the lane chains (valid in every lane):
-// (sum_l q_l H^(31-l)) * H^2 + L * H.
-__device__ __forceinline__ uint4 small_ghash(uint4 q, uint64_t P, const uint8_t* smem, const uint4* pow2)
+// GHASH of the object from the lane chains (returned in every lane):
+// (sum_l q_l H^(31-l)) * H^2 + L * H. Only the lanes whose result is used
+// multiply (16, 8, 4, 2, 1 at the fold levels, then lane 0), which keeps the
+// shared-memory traffic of the fold at a fifth of an all-lane fold.
+__device__ __forceinline__ uint4 small_ghash(uint4 q, uint64_t P, const uint8_t* smem, const uint4* pow2, int lane)
 {
 #pragma unroll
     for (int k = 0; k < 5; ++k) {
         const uint4 right = shfl_down4(q, 1 << k);
-        q = xor4(gh_mul_compact(q, small_fold_table(smem, pow2, k)), right);
+        if ((lane & ((2 << k) - 1)) == 0) {
+            q = xor4(gh_mul_compact(q, small_fold_table(smem, pow2, k)), right);
+        }
     }
-    const uint4 f = shfl4(q, 0);
-    return xor4(gh_mul_compact(f, small_fold_table(smem, pow2, 1)),
-                gh_mul_compact(be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull),
-                               small_fold_table(smem, pow2, 0)));
+    uint4 s = make_uint4(0, 0, 0, 0);
+    if (lane == 0) {
+        s = xor4(gh_mul_compact(q, small_fold_table(smem, pow2, 1)),
+                 gh_mul_compact(be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull),
+                                small_fold_table(smem, pow2, 0)));
+    }
+    return shfl4(s, 0);
 }
 
 // Geometry of an object split into warp rows.
@@ -165,7 +172,7 @@ __device__ __forceinline__ void seal_object_warp(const BatchItem* it, const uint
         }
         q = xor4(gh_mul_rep<kSmallGh>(q, lb_lo, lb_hi), c);
     }
-    const uint4 s = small_ghash(q, g.P, smem, pow2);
+    const uint4 s = small_ghash(q, g.P, smem, pow2, lane);
     uint32_t w[4] = {s012[0], s012[1], s012[2], bswap32(1u) ^ rk[3]};
     aes_rounds_smem<0>(w, rk, lb);
     const uint4 tag = xor4(s, make_uint4(w[0], w[1], w[2], w[3]));
@@ -206,7 +213,7 @@ __device__ __forceinline__ void open_object_warp(const BatchItem* it, const uint
                                                           : ct_block_rt(frame, frame_len, i, g.P, lo_off, lq, lfs);
         q = xor4(gh_mul_rep<kSmallGh>(q, lb_lo, lb_hi), c);
     }
-    const uint4 s = small_ghash(q, g.P, smem, pow2);
+    const uint4 s = small_ghash(q, g.P, smem, pow2, lane);
     uint32_t lb[4];
     aes_lane_bases(lb, lane);
     const uint4 iv = load_bytes(frame + 1, 12);
