@@ -10,6 +10,7 @@ the stream, the library does the work.
     batch.seal(key, [(src_ptr, frame_ptr, P, frame_capacity, iv), ...], stream)
     batch.open(key, [(frame_ptr, out_ptr, P, frame_len, auth_ptr), ...], stream)
     batch.statuses()   # int32 per object on the device: 0 or -1 (skipped)
+    batch.fault()      # device int32: nonzero if a work kernel gave up a bounded wait
 """
 
 from __future__ import annotations
@@ -20,6 +21,7 @@ from .gpu_aesgcm import BatchItem, GpuAes128GcmKey, GpuAesGcmLibrary, pack_batch
 
 ITEM_BYTES = 64
 STATUS_OFFSET = BatchItem.status.offset
+FAULT_OFFSET = 28   # LMCACHE_GPU_AESGCM_BATCH_FAULT_OFFSET: uint32 in the workspace
 
 
 class DeviceBatch:
@@ -72,3 +74,8 @@ class DeviceBatch:
         """Per-object status of the last call (int32, device): 0 or -1."""
         view = self.items[:self.count * ITEM_BYTES].view(self.count, ITEM_BYTES)
         return view[:, STATUS_OFFSET:STATUS_OFFSET + 4].contiguous().view(torch.int32).reshape(-1)
+
+    def fault(self) -> torch.Tensor:
+        """Fault word of the last call (int32, device): 0 unless a work kernel
+        gave up on one of its bounded internal waits (outputs then invalid)."""
+        return self.workspace[FAULT_OFFSET:FAULT_OFFSET + 4].view(torch.int32).reshape(())

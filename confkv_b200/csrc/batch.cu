@@ -17,12 +17,13 @@ static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, auth_ok) == offsetof(dev::
 static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, iv) == offsetof(dev::BatchItem, iv), "descriptor layout");
 static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, status) == offsetof(dev::BatchItem, status),
               "descriptor layout");
+static_assert(offsetof(dev::BatchHeader, fault) == LMCACHE_GPU_AESGCM_BATCH_FAULT_OFFSET, "fault word offset");
 
 cudaError_t confkv::host::configure_batch_kernels()
 {
-    cudaError_t e = allow_smem(dev::seal_batch_kernel, dev::kSealSmem);
+    cudaError_t e = allow_smem(dev::seal_batch_kernel, dev::kSealBatchSmem);
     if (e == cudaSuccess) {
-        e = allow_smem(dev::open_ghash_batch_kernel, dev::kOpenSmem);
+        e = allow_smem(dev::open_ghash_batch_kernel, dev::kOpenBatchSmem);
     }
     if (e == cudaSuccess) {
         e = allow_smem(dev::open_ctr_batch_kernel, dev::kCtrBatchSmem);
@@ -71,8 +72,8 @@ int batch_launch(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* it
     const uint32_t grid = static_cast<uint32_t>(h->num_sms);
     int rc;
     if (!open) {
-        rc = cuda_rc(launch_pdl(dev::seal_batch_kernel, grid, dev::kSealThreads, dev::kSealSmem, s, ba));
-    } else if (launch_pdl(dev::open_ghash_batch_kernel, grid, dev::kSealThreads, dev::kOpenSmem, s, ba) !=
+        rc = cuda_rc(launch_pdl(dev::seal_batch_kernel, grid, dev::kSealThreads, dev::kSealBatchSmem, s, ba));
+    } else if (launch_pdl(dev::open_ghash_batch_kernel, grid, dev::kSealThreads, dev::kOpenBatchSmem, s, ba) !=
                cudaSuccess) {
         rc = LMCACHE_GPU_AESGCM_ERR_CUDA;
     } else {

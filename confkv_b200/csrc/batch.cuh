@@ -46,6 +46,26 @@ constexpr uint32_t kCtrBatchMisc = kSmallSmem;      // after the small-object ta
 constexpr uint32_t kCtrBatchSmem = kCtrBatchMisc + 64;
 constexpr int kSmallBuckets = 11;                   // floor(log2 n) of a small object, n <= 1024
 
+// Hand-off from the row warps to the power warp (two-stage fold, tiles.cuh):
+// two buffers of 32 partials, and per buffer a FULL mbarrier (the 16 row
+// warps arrived) and an EMPTY one (the power warp took the values).
+constexpr uint32_t kHandoffBytes = 2 * 32 * 16;
+constexpr uint32_t kHandoffSyncBytes = 64;
+// Batched seal shared memory: AES tables, the chain table H^512 (H^32 for
+// small objects), the row-warp fold tables H^8, H^1, H^2, H^4 (the slots the
+// small-object path reads), the hand-off buffers and their mbarriers.
+constexpr uint32_t kSealBatchFold = kAesBytes + kGhBytes;
+constexpr uint32_t kSealBatchHandoff = kSealBatchFold + 4 * 8192u;
+constexpr uint32_t kSealBatchSync = kSealBatchHandoff + kHandoffBytes;
+constexpr uint32_t kSealBatchSmem = kSealBatchSync + kHandoffSyncBytes;
+static_assert(kSealBatchFold == kSmallFold, "the small-object path reads the seal fold slots");
+static_assert(kSealBatchSmem <= 227u * 1024u, "batched seal shared memory exceeds the per-block limit");
+// Batched open-GHASH shared memory: the single-object layout up to the
+// compact H^512 table, then the hand-off.
+constexpr uint32_t kOpenBatchHandoff = kOpenHt + 8192u;
+constexpr uint32_t kOpenBatchSync = kOpenBatchHandoff + kHandoffBytes;
+constexpr uint32_t kOpenBatchSmem = kOpenBatchSync + kHandoffSyncBytes;
+
 // Alignment classes: 2 v + p, v = the frame's ciphertext class (seal: store
 // funnel word part 0..3, 4 = aligned; open: load funnel word part, same
 // coding) and p = 1 when the plaintext side (seal src, open dst) is 16-B
@@ -59,7 +79,8 @@ struct BatchHeader {
     uint32_t iters_max;      // J*
     uint32_t small_count;    // objects of at most kSmallMaxBlocks blocks, one warp each
     uint32_t small_next[2];  // small-object queue heads: [0] seal, [1] open
-    uint32_t pad[9];
+    uint32_t fault;          // nonzero: a work kernel's hand-off wait gave up (results invalid)
+    uint32_t pad[8];
 };
 static_assert(sizeof(BatchHeader) <= 256, "batch header fits its 256-byte area");
 
@@ -366,6 +387,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
             hdr->next_tile[0] = 0;
             hdr->next_tile[1] = 0;
             hdr->iters_max = jstar;
+            hdr->fault = 0;
         }
     } else if (warp == 1 && lane == 0) {
         // small objects: largest bucket first
@@ -443,24 +465,122 @@ __device__ __forceinline__ uint32_t first_tile(volatile uint32_t* next_s, const 
     return t;
 }
 
+// ------------------------------------------------------------- hand-off
+//
+// Seal and open-GHASH CTAs run their tiles as a pipeline: the 16 row warps
+// compute a tile's rows and the first fold stage, hand 32 values to the power
+// warp and go on with the next tile, while the power warp finishes the fold,
+// the object's sum and the tag (seal) or verdict (open). Hand-off j uses
+// buffer j & 1; its FULL mbarrier completes when the 16 row warps arrived,
+// its EMPTY mbarrier when the power warp has read the values, so a buffer is
+// rewritten only after it was read. Both sides take the tiles in the same
+// queue order: thread 0 takes the next index after its rows and passes it
+// along with the values.
+
+// Shared-memory views of the hand-off (kHandoffBytes of buffers at part_off,
+// kHandoffSyncBytes of mbarriers and words at sync_off).
+struct Handoff {
+    uint4* part;               // [2][32] fold values V_p
+    uint64_t* full;            // [2]
+    uint64_t* empty;           // [2]
+    volatile uint32_t* next;   // [2] queue index taken after the buffer's tile
+    volatile uint32_t* first;  // first queue index of the CTA
+    volatile uint32_t* abort;  // raised by a wait that gave up
+};
+
+__device__ __forceinline__ Handoff handoff_at(uint8_t* smem, uint32_t part_off, uint32_t sync_off)
+{
+    uint8_t* s = smem + sync_off;
+    return Handoff{reinterpret_cast<uint4*>(smem + part_off), reinterpret_cast<uint64_t*>(s),
+                   reinterpret_cast<uint64_t*>(s + 16), reinterpret_cast<volatile uint32_t*>(s + 32),
+                   reinterpret_cast<volatile uint32_t*>(s + 40), reinterpret_cast<volatile uint32_t*>(s + 44)};
+}
+
+// Thread 0, before the CTA's first barrier.
+__device__ __forceinline__ void handoff_init(const Handoff& h)
+{
+    mbar_init(h.full, kHornerThreads / 32);
+    mbar_init(h.full + 1, kHornerThreads / 32);
+    mbar_init(h.empty, 1);
+    mbar_init(h.empty + 1, 1);
+    *h.abort = 0u;
+}
+
+// Row warps, hand-off j: wait until the power warp has read the buffer's
+// previous values (the first use of each buffer passes at once), store the
+// warp's V_2w and V_2w+1 and, thread 0, the queue index it took, arrive, and
+// wait for the other row warps so that every thread reads the next index.
+// False, in the whole warp, when a wait gave up.
+__device__ __forceinline__ bool row_handoff(const Handoff& h, uint32_t j, uint4 v, uint32_t taken,
+                                            const BatchCta& c, uint32_t& next)
+{
+    const uint32_t b = j & 1u;
+    const uint32_t parity = (j >> 1) & 1u;
+    if (!__all_sync(0xffffffffu, mbar_wait(h.empty + b, parity ^ 1u, h.abort))) {
+        return false;
+    }
+    if (c.lane < 2) {
+        h.part[32 * b + 2 * c.warp + c.lane] = v;
+    }
+    if (c.tid == 0) {
+        h.next[b] = taken;
+    }
+    __syncwarp();
+    if (c.lane == 0) {
+        mbar_arrive(h.full + b);
+    }
+    if (!__all_sync(0xffffffffu, mbar_wait(h.full + b, parity, h.abort))) {
+        return false;
+    }
+    next = h.next[b];
+    return true;
+}
+
+// Power warp, hand-off j: wait for the row warps' values (lane p takes V_p)
+// and the next queue index, then free the buffer.
+__device__ __forceinline__ bool power_take(const Handoff& h, uint32_t j, int lane, uint4& v, uint32_t& next)
+{
+    const uint32_t b = j & 1u;
+    if (!__all_sync(0xffffffffu, mbar_wait(h.full + b, (j >> 1) & 1u, h.abort))) {
+        return false;
+    }
+    v = h.part[32 * b + lane];
+    next = h.next[b];
+    __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(h.empty + b);
+    }
+    return true;
+}
+
+// Work-kernel epilogue of the tile phase (all threads): a CTA whose hand-off
+// gave up marks the batch as faulted and reports true.
+__device__ __forceinline__ bool handoff_failed(const Handoff& h, const BatchCta& c)
+{
+    __syncthreads();
+    if (*h.abort == 0u) {
+        return false;
+    }
+    if (c.tid == 0) {
+        atomicOr(&c.hdr->fault, 1u);
+    }
+    return true;
+}
+
 // ------------------------------------------------------------------ seal
 
-// Tiles of one alignment class, from `tile` while the queue hands out tiles
-// of this class; returns the first tile of another class (or >= total).
-// Per-tile values are loaded where they are used (the power warp reloads
-// them after the fold) so that only the tile index stays live across the
-// rows. Thread 0 takes the next index after its rows.
+// Row warps: tiles of one alignment class, from `tile` while the queue hands
+// out tiles of this class; returns the first tile of another class (or >=
+// total). Per-tile values are loaded where they are used so that only the
+// tile index stays live across the rows.
 template <int SQ, bool PT>
-__device__ __forceinline__ uint32_t seal_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, uint32_t tile,
-                                               int cls)
+__device__ __forceinline__ uint32_t seal_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c,
+                                               const Handoff& h, uint32_t tile, int cls, uint32_t& j)
 {
     constexpr int64_t T = kHornerThreads;
-    uint4* part = reinterpret_cast<uint4*>(smem + kSealPart);
-    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kSealMisc);
+    const uint4* ft = reinterpret_cast<const uint4*>(smem + kSealBatchFold);
     for (;;) {
-        unsigned long long uhi = 0, ulo = 0;
-        uint4 ej0 = make_uint4(0, 0, 0, 0);
-        uint4 lh = make_uint4(0, 0, 0, 0);
+        uint4 q;
         {
             const TileRec tr = c.rec[tile];
             const uint32_t cta = tr.cta & kTileIndexMask;
@@ -478,56 +598,65 @@ __device__ __forceinline__ uint32_t seal_class(uint8_t* smem, const BatchArgs& a
                     frame[1 + b] = static_cast<uint8_t>(ivw[b >> 2] >> (8 * (b & 3)));
                 }
             }
-            if (c.warp == kPowerWarp) {
-                const unsigned long long d = static_cast<unsigned long long>(G - 1 - cta) *
-                                                 static_cast<unsigned long long>(span) + 2ull;
-                seal_power(ivw, a.rk, P, d, a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
-            } else {
-                int sq;
-                uint32_t store_r;
-                store_class(frame + 13, sq, store_r);  // sq == SQ for this class
-                (void)sq;
-                const SealTile t{it->src, frame + 13, P, n - static_cast<int64_t>(G - cta) * span,
-                                 static_cast<int64_t>(J), {ivw[0] ^ a.rk[0], ivw[1] ^ a.rk[1], ivw[2] ^ a.rk[2]},
-                                 store_r};
-                part[c.tid] = seal_rows<SQ, PT>(t, a.rk, a.kt.gh_pow2, c.tid, c.lane);
-                if (c.tid == 0) {
-                    *next_s = atomicAdd(&c.hdr->next_tile[0], 1u);
-                }
-            }
+            int sq;
+            uint32_t store_r;
+            store_class(frame + 13, sq, store_r);  // sq == SQ for this class
+            (void)sq;
+            const SealTile t{it->src, frame + 13, P, n - static_cast<int64_t>(G - cta) * span,
+                             static_cast<int64_t>(J), {ivw[0] ^ a.rk[0], ivw[1] ^ a.rk[1], ivw[2] ^ a.rk[2]},
+                             store_r};
+            q = seal_rows<SQ, PT>(t, a.rk, a.kt.gh_pow2, c.tid, c.lane);
         }
-        __syncthreads();
-        seal_fold(smem, part, a.kt.gh_pow2, c.tid);
-        const uint32_t next = *next_s;
-
-        if (c.warp == kPowerWarp) {
-            const uint32_t item = c.rec[tile].item;
-            Slot* slot = c.st + item;
-            unsigned long long shi, slo;
-            if (batch_object_sum(slot, slot->aux[1], part[0], uhi, ulo, c.lane, shi, slo)) {
-                const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
-                if (c.lane < 16) {
-                    const BatchItem* it = a.items + item;
-                    it->dst[13 + it->plen + c.lane] = static_cast<uint8_t>(byte_of(tag, c.lane));
-                }
-            }
-        } else if (next < c.total) {
-            // seal_fold stored the late fold tables over the first
-            // kSealLateBytes of the AES region: T0/T1 entries x < 192.
-            for (int i = c.tid; i < 4096; i += kHornerThreads) {
-                const int x = (i >> 3) & 255;
-                if (x < static_cast<int>(kSealLateBytes >> 8)) {
-                    const int kk = i >> 11;
-                    const uint32_t tv = __ldg(a.kt.aes_t + kk * 256 + x);
-                    const uint32_t off = (static_cast<uint32_t>(x) << 8) | (static_cast<uint32_t>(kk & 1) << 7) |
-                                         (static_cast<uint32_t>(i & 7) << 4);
-                    *reinterpret_cast<uint4*>(smem + kSealAes + off) = make_uint4(tv, tv, tv, tv);
-                }
-            }
+        uint32_t taken = 0;
+        if (c.tid == 0) {
+            taken = atomicAdd(&c.hdr->next_tile[0], 1u);
         }
-        __syncthreads();
+        const uint4 v = warp_fold_pairs<true>(q, ft, c.lane);
+        uint32_t next;
+        if (!row_handoff(h, j, v, taken, c, next)) {
+            return c.total;
+        }
+        ++j;
         if (next >= c.total || tile_class(c, next) != cls) {
             return next;
+        }
+        tile = next;
+    }
+}
+
+// Power warp of the batched seal, over the same tiles as the row warps:
+// E_K(J0), L*H and the basis of H^d while the tile's rows run, then the fold
+// levels 4..8 (the key's global tables), the object's sum and, once the
+// object's last tile is in, its tag.
+__device__ __forceinline__ void seal_power_loop(const BatchArgs& a, const BatchCta& c, const Handoff& h,
+                                                uint32_t tile)
+{
+    constexpr unsigned long long T = kHornerThreads;
+    for (uint32_t j = 0; tile < c.total; ++j) {
+        const TileRec tr = c.rec[tile];
+        const uint32_t cta = tr.cta & kTileIndexMask;
+        Slot* slot = c.st + tr.item;
+        const BatchItem* it = a.items + tr.item;
+        const uint32_t J = slot->aux[0];
+        const uint32_t G = slot->aux[1];
+        const uint64_t P = it->plen;
+        const uint32_t ivw[3] = {it->iv[0], it->iv[1], it->iv[2]};
+        const unsigned long long d = static_cast<unsigned long long>(G - 1 - cta) * J * T + 2ull;
+        uint4 ej0, lh;
+        unsigned long long uhi, ulo;
+        seal_power(ivw, a.rk, P, d, a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
+        uint4 v;
+        uint32_t next;
+        if (!power_take(h, j, c.lane, v, next)) {
+            return;
+        }
+        const uint4 fold = power_fold(v, a.kt.gh_pow2 + 4 * 512, c.lane);
+        unsigned long long shi, slo;
+        if (batch_object_sum(slot, G, fold, uhi, ulo, c.lane, shi, slo)) {
+            const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
+            if (c.lane < 16) {
+                it->dst[13 + P + c.lane] = static_cast<uint8_t>(byte_of(tag, c.lane));
+            }
         }
         tile = next;
     }
@@ -540,49 +669,48 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
     pdl_release();
     fill_aes_smem(smem + kSealAes, a.kt.aes_t);
     fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
-    for (int i = tid; i < kSealFoldSmemLevels * 512; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + kSealFold)[i] = __ldg(a.kt.gh_pow2 + i);
+    fill_small_fold(smem, a.kt.gh_pow2);
+    const Handoff h = handoff_at(smem, kSealBatchHandoff, kSealBatchSync);
+    if (tid == 0) {
+        handoff_init(h);
     }
     pdl_wait();  // the plan kernel's workspace
     auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
     const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
                      reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count)), hdr->total_tiles,
                      tid, tid & 31, tid >> 5};
-    uint32_t tile = first_tile(reinterpret_cast<volatile uint32_t*>(smem + kSealMisc), c, 0);
-    while (tile < c.total) {
-        const int cls = tile_class(c, tile);
-        switch (cls) {
-        case 0: tile = seal_class<0, false>(smem, a, c, tile, cls); break;
-        case 1: tile = seal_class<0, true>(smem, a, c, tile, cls); break;
-        case 2: tile = seal_class<1, false>(smem, a, c, tile, cls); break;
-        case 3: tile = seal_class<1, true>(smem, a, c, tile, cls); break;
-        case 4: tile = seal_class<2, false>(smem, a, c, tile, cls); break;
-        case 5: tile = seal_class<2, true>(smem, a, c, tile, cls); break;
-        case 6: tile = seal_class<3, false>(smem, a, c, tile, cls); break;
-        case 7: tile = seal_class<3, true>(smem, a, c, tile, cls); break;
-        case 8: tile = seal_class<4, false>(smem, a, c, tile, cls); break;
-        default: tile = seal_class<4, true>(smem, a, c, tile, cls); break;
+    uint32_t tile = first_tile(h.first, c, 0);
+    if (c.warp == kPowerWarp) {
+        seal_power_loop(a, c, h, tile);
+    } else {
+        uint32_t j = 0;
+        while (tile < c.total) {
+            const int cls = tile_class(c, tile);
+            switch (cls) {
+            case 0: tile = seal_class<0, false>(smem, a, c, h, tile, cls, j); break;
+            case 1: tile = seal_class<0, true>(smem, a, c, h, tile, cls, j); break;
+            case 2: tile = seal_class<1, false>(smem, a, c, h, tile, cls, j); break;
+            case 3: tile = seal_class<1, true>(smem, a, c, h, tile, cls, j); break;
+            case 4: tile = seal_class<2, false>(smem, a, c, h, tile, cls, j); break;
+            case 5: tile = seal_class<2, true>(smem, a, c, h, tile, cls, j); break;
+            case 6: tile = seal_class<3, false>(smem, a, c, h, tile, cls, j); break;
+            case 7: tile = seal_class<3, true>(smem, a, c, h, tile, cls, j); break;
+            case 8: tile = seal_class<4, false>(smem, a, c, h, tile, cls, j); break;
+            default: tile = seal_class<4, true>(smem, a, c, h, tile, cls, j); break;
+            }
         }
     }
+    if (handoff_failed(h, c)) {
+        return;
+    }
 
-    // Small objects, one warp each, once the tiles are gone: restore the AES
-    // tables the last fold may have overwritten, then H^32 and H^8.
+    // Small objects, one warp each, once the tiles are gone: H^32 over the
+    // chain table (the fold slots already hold H^8, H^1, H^2, H^4).
     const uint32_t small_count = hdr->small_count;
     if (small_count == 0) {
         return;
     }
-    __syncthreads();
-    for (int i = tid; i < 4096; i += blockDim.x) {
-        const int x = (i >> 3) & 255;
-        if (x < static_cast<int>(kSealLateBytes >> 8)) {
-            const int kk = i >> 11;
-            const uint32_t tv = __ldg(a.kt.aes_t + kk * 256 + x);
-            const uint32_t off = (static_cast<uint32_t>(x) << 8) | (static_cast<uint32_t>(kk & 1) << 7) |
-                                 (static_cast<uint32_t>(i & 7) << 4);
-            *reinterpret_cast<uint4*>(smem + kSealAes + off) = make_uint4(tv, tv, tv, tv);
-        }
-    }
-    small_fill_seal_tables(smem, a.kt.gh_pow2);
+    fill_gh_smem(smem + kSmallGh, a.kt.gh_pow2 + 5 * 512);
     __syncthreads();
     const uint32_t* small_list = reinterpret_cast<const uint32_t*>(a.ws + batch_small_offset(a.count));
     for (;;) {
@@ -600,19 +728,17 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
 
 // ------------------------------------------------------------------ open
 
-// GHASH + verdict tiles whose frames share load class LQ (both plaintext
-// sides); returns the first tile of another load class (or >= total).
+// Row warps of the GHASH pass: tiles whose frames share load class LQ (both
+// plaintext sides); returns the first tile of another load class (or >=
+// total).
 template <int LQ>
 __device__ __forceinline__ uint32_t open_ghash_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c,
-                                                     uint32_t tile)
+                                                     const Handoff& h, uint32_t tile, uint32_t& j)
 {
     constexpr int64_t T = kHornerThreads;
-    uint4* part = reinterpret_cast<uint4*>(smem + kOpenPart);
-    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kOpenMisc);
+    const uint4* ft = reinterpret_cast<const uint4*>(smem + kOpenFold);
     for (;;) {
-        unsigned long long uhi = 0, ulo = 0;
-        uint4 ej0 = make_uint4(0, 0, 0, 0);
-        uint4 lh = make_uint4(0, 0, 0, 0);
+        uint4 q;
         {
             const TileRec tr = c.rec[tile];
             const uint32_t cta = tr.cta & kTileIndexMask;
@@ -623,41 +749,62 @@ __device__ __forceinline__ uint32_t open_ghash_class(uint8_t* smem, const BatchA
             const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
             const int64_t span = static_cast<int64_t>(J) * T;
             const uint8_t* frame = it->src;
-            if (c.warp == kPowerWarp) {
-                const unsigned long long d = static_cast<unsigned long long>(G - 1 - cta) *
-                                                 static_cast<unsigned long long>(span) + 2ull;
-                open_power(frame, a.kt.aes_t, a.rk, P, d, a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
-            } else {
-                int lq;
-                uint32_t load_r;
-                load_class(frame + 13, lq, load_r);  // lq == LQ for this class
-                (void)lq;
-                const OpenTile t{frame, it->capacity, P, n - static_cast<int64_t>(G - cta) * span,
-                                 static_cast<int64_t>(J), load_r};
-                part[c.tid] = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), c.tid, c.lane);
-                if (c.tid == 0) {
-                    *next_s = atomicAdd(&c.hdr->next_tile[0], 1u);
-                }
-            }
+            int lq;
+            uint32_t load_r;
+            load_class(frame + 13, lq, load_r);  // lq == LQ for this class
+            (void)lq;
+            const OpenTile t{frame, it->capacity, P, n - static_cast<int64_t>(G - cta) * span,
+                             static_cast<int64_t>(J), load_r};
+            q = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), c.tid, c.lane);
         }
-        __syncthreads();
-        fold_partials<kFoldLevels>(part, reinterpret_cast<const uint4*>(smem + kOpenFold), a.kt.gh_pow2);
-        const uint32_t next = *next_s;
-
-        if (c.warp == kPowerWarp) {
-            const uint32_t item = c.rec[tile].item;
-            Slot* slot = c.st + item;
-            unsigned long long shi, slo;
-            if (batch_object_sum(slot, slot->aux[1], part[0], uhi, ulo, c.lane, shi, slo) && c.lane == 0) {
-                const BatchItem* it = a.items + item;
-                const int v = open_verdict(it->src, it->plen, shi, slo, lh, ej0);
-                *it->auth_ok = v;
-                slot->aux[2] = static_cast<unsigned int>(v);
-            }
+        uint32_t taken = 0;
+        if (c.tid == 0) {
+            taken = atomicAdd(&c.hdr->next_tile[0], 1u);
         }
-        __syncthreads();
+        const uint4 v = warp_fold_pairs<false>(q, ft, c.lane);
+        uint32_t next;
+        if (!row_handoff(h, j, v, taken, c, next)) {
+            return c.total;
+        }
+        ++j;
         if (next >= c.total || (tile_class(c, next) >> 1) != LQ) {
             return next;
+        }
+        tile = next;
+    }
+}
+
+// Power warp of the GHASH pass: E_K(J0), L*H and the basis of H^d while the
+// rows run, then fold levels 4..8 (shared tables), the object's sum and, once
+// its last tile is in, the verdict (auth_ok and the object's slot).
+__device__ __forceinline__ void open_power_loop(const uint8_t* smem, const BatchArgs& a, const BatchCta& c,
+                                                const Handoff& h, uint32_t tile)
+{
+    constexpr unsigned long long T = kHornerThreads;
+    const uint4* t4 = reinterpret_cast<const uint4*>(smem + kOpenFold) + 4 * 512;
+    for (uint32_t j = 0; tile < c.total; ++j) {
+        const TileRec tr = c.rec[tile];
+        const uint32_t cta = tr.cta & kTileIndexMask;
+        Slot* slot = c.st + tr.item;
+        const BatchItem* it = a.items + tr.item;
+        const uint32_t J = slot->aux[0];
+        const uint32_t G = slot->aux[1];
+        const uint64_t P = it->plen;
+        const unsigned long long d = static_cast<unsigned long long>(G - 1 - cta) * J * T + 2ull;
+        uint4 ej0, lh;
+        unsigned long long uhi, ulo;
+        open_power(it->src, a.kt.aes_t, a.rk, P, d, a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
+        uint4 v;
+        uint32_t next;
+        if (!power_take(h, j, c.lane, v, next)) {
+            return;
+        }
+        const uint4 fold = power_fold(v, t4, c.lane);
+        unsigned long long shi, slo;
+        if (batch_object_sum(slot, G, fold, uhi, ulo, c.lane, shi, slo) && c.lane == 0) {
+            const int ok = open_verdict(it->src, P, shi, slo, lh, ej0);
+            *it->auth_ok = ok;
+            slot->aux[2] = static_cast<unsigned int>(ok);
         }
         tile = next;
     }
@@ -672,21 +819,31 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
     for (int i = tid; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
         reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);
     }
+    const Handoff h = handoff_at(smem, kOpenBatchHandoff, kOpenBatchSync);
+    if (tid == 0) {
+        handoff_init(h);
+    }
     pdl_wait();  // the plan kernel's workspace
     auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
     const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
                      reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count)), hdr->total_tiles,
                      tid, tid & 31, tid >> 5};
-    uint32_t tile = first_tile(reinterpret_cast<volatile uint32_t*>(smem + kOpenMisc), c, 0);
-    while (tile < c.total) {
-        switch (tile_class(c, tile) >> 1) {  // the GHASH pass does not touch the plaintext side
-        case 0: tile = open_ghash_class<0>(smem, a, c, tile); break;
-        case 1: tile = open_ghash_class<1>(smem, a, c, tile); break;
-        case 2: tile = open_ghash_class<2>(smem, a, c, tile); break;
-        case 3: tile = open_ghash_class<3>(smem, a, c, tile); break;
-        default: tile = open_ghash_class<4>(smem, a, c, tile); break;
+    uint32_t tile = first_tile(h.first, c, 0);
+    if (c.warp == kPowerWarp) {
+        open_power_loop(smem, a, c, h, tile);
+    } else {
+        uint32_t j = 0;
+        while (tile < c.total) {
+            switch (tile_class(c, tile) >> 1) {  // the GHASH pass does not touch the plaintext side
+            case 0: tile = open_ghash_class<0>(smem, a, c, h, tile, j); break;
+            case 1: tile = open_ghash_class<1>(smem, a, c, h, tile, j); break;
+            case 2: tile = open_ghash_class<2>(smem, a, c, h, tile, j); break;
+            case 3: tile = open_ghash_class<3>(smem, a, c, h, tile, j); break;
+            default: tile = open_ghash_class<4>(smem, a, c, h, tile, j); break;
+            }
         }
     }
+    handoff_failed(h, c);
 }
 
 // Gated CTR over the same tiles (rows of kCtrThreads = kHornerThreads

@@ -141,6 +141,76 @@ __device__ __forceinline__ void pdl_release()
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ------------------------------------------------ shared-memory mbarriers
+//
+// Warps of one CTA hand data to one another through shared memory guarded by
+// mbarriers (arrive = release, completed wait = acquire, CTA scope). Every
+// wait is bounded: it gives up after kWaitLimitNs of %globaltimer (or
+// kWaitLimitPolls polls) or as soon as another thread of the CTA has given up,
+// raising the CTA's shared abort word, so a broken hand-off ends the kernel
+// with an error instead of hanging it. The limit is far above any legitimate
+// wait (a wait lasts at most one tile of rows, milliseconds).
+constexpr unsigned long long kWaitLimitNs = 10ull * 1000ull * 1000ull * 1000ull;
+constexpr uint32_t kWaitLimitPolls = 1u << 30;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// True once the phase of `bar` with parity `parity` has completed.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity)
+{
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for the phase of `bar` with parity `parity`; false when the
+// limit ran out (the caller's thread raises *abort) or *abort was raised.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort)
+{
+    if (mbar_test(bar, parity)) {
+        return true;
+    }
+    const unsigned long long t0 = global_ns();
+    for (uint32_t polls = 0; polls < kWaitLimitPolls; ++polls) {
+        if (mbar_test(bar, parity)) {
+            return true;
+        }
+        if (*abort != 0u) {
+            return false;
+        }
+        if (global_ns() - t0 > kWaitLimitNs) {
+            break;
+        }
+    }
+    *abort = 1u;
+    return false;
+}
+
 // Device view of lmcache_gpu_aesgcm_batch_item (include/gpu_aesgcm_api.h).
 struct BatchItem {
     const uint8_t* src;   // seal: plaintext; open: frame
@@ -186,6 +256,18 @@ __device__ __forceinline__ uint32_t byte_of(const uint4& v, int b)
 __device__ __forceinline__ uint4 xor4(uint4 a, uint4 b)
 {
     return make_uint4(a.x ^ b.x, a.y ^ b.y, a.z ^ b.z, a.w ^ b.w);
+}
+
+__device__ __forceinline__ uint4 shfl_down4(uint4 v, int d)
+{
+    return make_uint4(__shfl_down_sync(0xffffffffu, v.x, d), __shfl_down_sync(0xffffffffu, v.y, d),
+                      __shfl_down_sync(0xffffffffu, v.z, d), __shfl_down_sync(0xffffffffu, v.w, d));
+}
+
+__device__ __forceinline__ uint4 shfl4(uint4 v, int src)
+{
+    return make_uint4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
+                      __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
 }
 
 // Raw block bytes (LE words) <-> (hi, lo) big-endian halves.

@@ -27,8 +27,6 @@ constexpr uint64_t kSmallMaxBlocks = 1024;
 constexpr uint32_t kSmallGh = kAesBytes;
 constexpr uint32_t kSmallFold = kAesBytes + kGhBytes;
 constexpr uint32_t kSmallSmem = kSmallFold + 4 * 8192u;
-static_assert(kSmallFold == kSealPart && kSmallFold + 8192u == kSealFold,
-              "the seal kernel keeps H^1, H^2, H^4 where the small-object path reads them");
 
 // Compact table of fold level k (H^(2^k)) for the small-object fold.
 __device__ __forceinline__ const uint4* small_fold_table(const uint8_t* smem, const uint4* pow2, int k)
@@ -37,20 +35,9 @@ __device__ __forceinline__ const uint4* small_fold_table(const uint8_t* smem, co
     return k == 4 ? pow2 + 4 * 512 : (k == 3 ? ft : ft + (k + 1) * 512);
 }
 
-// Fills the small-object tables that the seal kernel does not already hold:
-// H^32 over the GHASH region and H^8 over the partials. All threads.
-__device__ __forceinline__ void small_fill_seal_tables(uint8_t* smem, const uint4* pow2)
+// Compact tables of H^8, H^1, H^2, H^4 into the fold slots. All threads.
+__device__ __forceinline__ void fill_small_fold(uint8_t* smem, const uint4* pow2)
 {
-    fill_gh_smem(smem + kSmallGh, pow2 + 5 * 512);
-    for (int i = threadIdx.x; i < 512; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + kSmallFold)[i] = __ldg(pow2 + 3 * 512 + i);
-    }
-}
-
-// Fills all small-object tables above the AES region (open-CTR kernel).
-__device__ __forceinline__ void small_fill_open_tables(uint8_t* smem, const uint4* pow2)
-{
-    fill_gh_smem(smem + kSmallGh, pow2 + 5 * 512);
     uint4* ft = reinterpret_cast<uint4*>(smem + kSmallFold);
     for (int i = threadIdx.x; i < 4 * 512; i += blockDim.x) {
         const int k = i >> 9;  // slot k holds H^8, H^1, H^2, H^4
@@ -59,16 +46,11 @@ __device__ __forceinline__ void small_fill_open_tables(uint8_t* smem, const uint
     }
 }
 
-__device__ __forceinline__ uint4 shfl_down4(uint4 v, int d)
+// Fills all small-object tables above the AES region (open-CTR kernel).
+__device__ __forceinline__ void small_fill_open_tables(uint8_t* smem, const uint4* pow2)
 {
-    return make_uint4(__shfl_down_sync(0xffffffffu, v.x, d), __shfl_down_sync(0xffffffffu, v.y, d),
-                      __shfl_down_sync(0xffffffffu, v.z, d), __shfl_down_sync(0xffffffffu, v.w, d));
-}
-
-__device__ __forceinline__ uint4 shfl4(uint4 v, int src)
-{
-    return make_uint4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
-                      __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
+    fill_gh_smem(smem + kSmallGh, pow2 + 5 * 512);
+    fill_small_fold(smem, pow2);
 }
 
 // GHASH of the object from the lane chains (returned in every lane):

@@ -207,6 +207,53 @@ __device__ __forceinline__ void seal_fold(uint8_t* smem, uint4* part, const uint
     fold_partials<kFoldLevels>(part, late_tabs, pow2, kSealFoldSmemLevels, kFoldLevels);
 }
 
+// ------------------------------------------------------- two-stage fold
+//
+// The persistent batched kernels fold a tile's kHornerThreads partials Q_t in
+// two stages, so the row warps hand their tile over and start the next one
+// without waiting for the tile's epilogue:
+//   row warps   warp w folds its 32 partials with levels 0..3 into
+//               V_p = sum_{t in [16p, 16p+16)} Q_t H^(16p+15-t), p = 2w, 2w+1
+//               (warp_fold_pairs);
+//   power warp  folds V_0..V_31 with levels 4..8 into
+//               sum_p V_p H^(16 (31-p)) = sum_t Q_t H^(511-t) (power_fold),
+//               the value fold_partials leaves in part[0].
+
+// Levels 0..3 of a warp's fold. At level k, lanes i < 16 >> k combine the
+// values of lanes 2i and 2i+1 as v_2i H^(2^k) + v_(2i+1): the active lanes stay
+// contiguous, so a lookup of the compact tables costs as few shared-memory
+// wavefronts as in a full warp. Lanes 0 and 1 return V_2w and V_2w+1. The
+// compact table of H^(2^k) is at ft + 512 slot(k), slot(k) = k, or
+// (k + 1) & 3 when SMALL_SLOTS (the small-object order H^8, H^1, H^2, H^4).
+template <bool SMALL_SLOTS>
+__device__ __forceinline__ uint4 warp_fold_pairs(uint4 q, const uint4* ft, int lane)
+{
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint4 a = shfl4(q, (2 * lane) & 31);
+        const uint4 b = shfl4(q, (2 * lane + 1) & 31);
+        if (lane < (16 >> k)) {
+            q = xor4(gh_mul_compact(a, ft + 512 * (SMALL_SLOTS ? ((k + 1) & 3) : k)), b);
+        }
+    }
+    return q;
+}
+
+// Levels 4..8 on the power warp: lane p holds V_p; t4 is the compact table of
+// H^16, followed by those of H^32 .. H^256 (shared or global memory). Returns
+// the tile's fold in every lane.
+__device__ __forceinline__ uint4 power_fold(uint4 v, const uint4* t4, int lane)
+{
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+        const uint4 right = shfl_down4(v, 1 << k);
+        if ((lane & ((2 << k) - 1)) == 0) {
+            v = xor4(gh_mul_compact(v, t4 + 512 * k), right);
+        }
+    }
+    return shfl4(v, 0);
+}
+
 // ---------------------------------------------------------------- open
 
 struct OpenTile {

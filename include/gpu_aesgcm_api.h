@@ -123,6 +123,10 @@ int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key_len, const
  * workspace: DEVICE buffer, 16-byte aligned, at least
  *   lmcache_gpu_aes128gcm_batch_workspace_size(count) bytes, any contents; the
  *   call owns it until its work on `stream` completes (one call at a time).
+ *   After the call, the uint32 at byte offset
+ *   LMCACHE_GPU_AESGCM_BATCH_FAULT_OFFSET is nonzero if a work kernel gave up
+ *   on one of its internal waits (bounded; a fault, never expected): the
+ *   call's frames, tags and verdicts are then invalid.
  * Host-side errors (null key/items/workspace, misalignment, a short
  * workspace, count above 2^20) return ERR_ARGUMENT before any launch;
  * count == 0 is a no-op.
@@ -137,6 +141,8 @@ typedef struct lmcache_gpu_aesgcm_batch_item {
     int32_t status;           /* written by the device */
     uint64_t reserved;        /* set to 0 */
 } lmcache_gpu_aesgcm_batch_item;
+
+#define LMCACHE_GPU_AESGCM_BATCH_FAULT_OFFSET 28
 
 /* Workspace bytes for a batch of `count` objects; 0 when count > 2^20. */
 size_t lmcache_gpu_aes128gcm_batch_workspace_size(size_t count);

@@ -58,6 +58,7 @@ def test_batch_ragged_adversarial(gpu_lib, oracle):
     with GpuAes128GcmKey(gpu_lib, key) as kgood, GpuAes128GcmKey(gpu_lib, wrong) as kwrong:
         batch.seal(kgood, _seal_entries(d_plain, pt_off, d_frames, fr_off, lens, ivs), s)
         s.synchronize()
+        assert int(batch.fault()) == 0
         assert not batch.statuses().any()
         host_frames = d_frames.cpu().numpy()
         assert (host_frames[fr_total:] == 0xAB).all()
@@ -70,8 +71,10 @@ def test_batch_ragged_adversarial(gpu_lib, oracle):
         good_idx = [i for i in range(len(lens)) if i not in case.wrong_key]
         batch.open(kgood, _open_entries(d_frames, fr_off, d_out, pt_off, lens, d_auth, good_idx), s)
         s.synchronize()
+        assert int(batch.fault()) == 0
         batch.open(kwrong, _open_entries(d_frames, fr_off, d_out, pt_off, lens, d_auth, sorted(case.wrong_key)), s)
         s.synchronize()
+        assert int(batch.fault()) == 0
     auth = d_auth.cpu().numpy()
     out = d_out.cpu().numpy()
     assert (out[pt_total:] == 0xCC).all()
@@ -113,6 +116,7 @@ def test_batch_edge_sizes_alignments(gpu_lib, oracle, src_mis, dst_mis):
     with GpuAes128GcmKey(gpu_lib, key) as k:
         batch.seal(k, _seal_entries(d_plain, pt_off, d_frames, fr_off, lens, ivs), s)
         s.synchronize()
+        assert int(batch.fault()) == 0
         frames = d_frames.cpu().numpy()
         expected = oracle.evp_seal_many(key, ivs, pts)
         mask = np.zeros(frames.size, dtype=bool)
@@ -122,6 +126,7 @@ def test_batch_edge_sizes_alignments(gpu_lib, oracle, src_mis, dst_mis):
         assert (frames[~mask] == 0xAB).all()
         batch.open(k, _open_entries(d_frames, fr_off, d_out, pt_off, lens, d_auth, range(len(lens))), s)
         s.synchronize()
+        assert int(batch.fault()) == 0
     assert (d_auth.cpu().numpy() == 1).all()
     out = d_out.cpu().numpy()
     mask = np.zeros(out.size, dtype=bool)
@@ -155,11 +160,13 @@ def test_batch_multi_tile_objects_match_single_seal(gpu_lib):
                              dst_ptr=d_single.data_ptr() + int(fr_off[i]), dst_capacity=int(lens[i]) + 29,
                              iv=ivs[i], stream_ptr=s.cuda_stream)
             s.synchronize()
+            assert int(batch.fault()) == 0
             assert torch.equal(d_batch, d_single)
         d_out = torch.zeros_like(d_plain)
         d_auth = torch.zeros(len(lens), dtype=torch.int32, device="cuda")
         batch.open(k, _open_entries(d_batch, fr_off, d_out, pt_off, lens, d_auth, range(len(lens))), s)
         s.synchronize()
+        assert int(batch.fault()) == 0
     assert (d_auth == 1).all()
     for i in range(len(lens)):
         a, n = int(pt_off[i]), int(lens[i])
@@ -184,6 +191,7 @@ def test_batch_invalid_descriptors_are_skipped(gpu_lib):
     with GpuAes128GcmKey(gpu_lib, key) as k:
         batch.seal(k, entries, s)
         s.synchronize()
+        assert int(batch.fault()) == 0
         assert batch.statuses().cpu().tolist() == [0, -1, -1, 0]
         frames = d_frames.cpu().numpy()
         assert (frames[n + 29:3 * (n + 29)] == 0xAB).all()
@@ -198,6 +206,7 @@ def test_batch_invalid_descriptors_are_skipped(gpu_lib):
              (base_f + 3 * (n + 29), d_out.data_ptr() + 3 * n, n, n + 29, d_auth.data_ptr() + 12)]
         batch.open(k, o, s)
         s.synchronize()
+        assert int(batch.fault()) == 0
         assert batch.statuses().cpu().tolist() == [0, -1, -1, 0]
     assert d_auth.cpu().tolist() == [1, 7, 7, 1]
     out = d_out.cpu().numpy()
@@ -222,6 +231,7 @@ def test_batch_many_small_objects(gpu_lib, oracle):
         with GpuAes128GcmKey(gpu_lib, key) as k:
             batch.seal(k, _seal_entries(d_plain, pt_off, d_frames, fr_off, lens, ivs), s)
             s.synchronize()
+            assert int(batch.fault()) == 0
         frames = d_frames.cpu().numpy()
         expected = oracle.evp_seal_many(key, ivs, pts)
         for i in range(len(lens)):
@@ -250,6 +260,7 @@ def test_batch_two_hundred_thousand_tiny_objects(gpu_lib, oracle):
     with GpuAes128GcmKey(gpu_lib, key) as k:
         batch.seal(k, _seal_entries(d_plain, pt_off, d_frames, fr_off, lens, ivs), s)
         s.synchronize()
+        assert int(batch.fault()) == 0
         assert not batch.statuses().any()
         frames = d_frames.cpu().numpy()
         expected = oracle.evp_seal_many(key, ivs, pts)
@@ -261,6 +272,7 @@ def test_batch_two_hundred_thousand_tiny_objects(gpu_lib, oracle):
         d_frames.copy_(torch.from_numpy(frames))
         batch.open(k, _open_entries(d_frames, fr_off, d_out, pt_off, lens, d_auth, range(count)), s)
         s.synchronize()
+        assert int(batch.fault()) == 0
     auth = d_auth.cpu().numpy()
     out = d_out.cpu().numpy()
     for i in range(count):
