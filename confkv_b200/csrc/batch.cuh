@@ -1,25 +1,34 @@
 // Batched seal / open: one plan launch and one (seal) or two (open)
 // persistent launches for any number of objects of any sizes and alignments.
 //
-//   batch_plan_kernel    one CTA: validates every descriptor (status), sums
-//                        the rows, picks the tile height J* by scoring 16
-//                        candidates (1..8 tiles per SM, the tallest object
-//                        in 1..8 equal tiles) with a makespan model, gives object i
-//                        J_i = min(J*, rows_i) and G_i = ceil(n_i / (J_i T))
-//                        tiles, and writes the tile records (object, tile)
-//                        with taller tiles first, so the queue's tail holds
-//                        the short ones.
-//   seal_batch_kernel    one CTA per SM; each takes tiles from the queue
-//   open_ghash_batch_    (atomic head) and runs the same tile bodies as the
-//   kernel               single-object kernels (tiles.cuh). A one-tile
-//   open_ctr_batch_      object needs no atomics; others accumulate through
-//   kernel               their slot and the last tile writes the tag / the
-//                        verdict. No CTA waits for another.
+// Objects of more than kSmallMaxBlocks blocks ("tile objects") are cut into
+// rows of kHornerThreads blocks, aligned to the object's end (only row 0 can
+// start before block 0). The batch's rows form one row space, tile objects
+// back to back, which is cut into M chunks of equal estimated cost (rows
+// plus a fixed charge per tile object). As in stream-K, a chunk may end
+// inside one object and start inside another, so every SM gets the same
+// work whatever the object sizes. The part of one object inside one chunk
+// is a segment; it is processed like a tile (tiles.cuh) and its GHASH share
+// is combined through the object's slot, the last segment writing the tag
+// or verdict.
+//
+//   batch_plan_kernel    one CTA: validates every descriptor (status), lays
+//                        out the row space (tile objects grouped by
+//                        alignment class), picks M, counts each object's
+//                        segments and records the tile object holding each
+//                        chunk's first row; small objects go to a list,
+//                        largest first.
+//   seal_batch_kernel    one CTA per SM; each takes chunks from a queue
+//   open_ghash_batch_    (atomic head) and walks their segments. No CTA waits
+//   kernel               for another. After the chunks, small objects, one
+//   open_ctr_batch_      warp each (seal, open-CTR).
+//   kernel
 //
 // Device-written workspace (caller-owned, any contents on entry):
 //   [0, 256)            BatchHeader
-//   [256, ...)          one Slot per object: acc, ticket, aux = {J, G, verdict}
-//   [tiles_offset, ...) TileRec per tile, at most count + kBatchExtraTiles
+//   [256, ...)          one Slot per object: acc, ticket, aux = {rows, segments, verdict}
+//   [objs_offset, ...)  TileObj per tile object, then a sentinel
+//   [chunks_offset, ...) ChunkRec per chunk (first row, first tile object), then a sentinel
 //   [small_offset, ...) small objects (item indices), largest first
 #pragma once
 
@@ -29,18 +38,12 @@
 namespace confkv {
 namespace dev {
 
-
-constexpr int kBatchWaves = 8;        // most tiles per SM the plan considers
-constexpr int kPlanCandidates = 16;   // tile heights the plan scores
-// Fixed work per tile (fold, tag or verdict, table refill, queue and
-// descriptor fetch) in units of one row of the seal loop, as measured on
-// B200: about 8-10 us per tile against ~2.5 us per 8 KiB row per SM.
-constexpr double kTileOverheadRows = 4.0;
-constexpr int kBatchMaxSms = 256;     // SMs counted for the tile bound
-constexpr uint32_t kBatchExtraTiles = static_cast<uint32_t>(kBatchWaves * kBatchMaxSms);
+constexpr int kBatchMaxSms = 256;     // SMs the plan spreads chunks over
+constexpr int kChunksPerSm = 4;       // chunks per SM for tall batches (the queue evens out SMs that start late)
+constexpr uint32_t kMinChunkRows = 64;  // fewer chunks per SM while chunks would be shorter than this
+constexpr uint32_t kMaxChunks = static_cast<uint32_t>(kChunksPerSm * kBatchMaxSms);
 constexpr uint32_t kBatchMaxItems = 1u << 20;
 constexpr int kPlanThreads = 1024;
-constexpr int kBuckets = 32;
 constexpr uint64_t kBatchMaxBlocks = 0xfffffffeull;
 constexpr uint32_t kCtrBatchMisc = kSmallSmem;      // after the small-object tables
 constexpr uint32_t kCtrBatchSmem = kCtrBatchMisc + 64;
@@ -50,58 +53,108 @@ constexpr int kSmallBuckets = 11;                   // floor(log2 n) of a small 
 // two buffers of 32 partials, and per buffer a FULL mbarrier (the 16 row
 // warps arrived) and an EMPTY one (the power warp took the values).
 constexpr uint32_t kHandoffBytes = 2 * 32 * 16;
-constexpr uint32_t kHandoffSyncBytes = 64;
+constexpr uint32_t kHandoffSyncBytes = 96;   // mbarriers, queue words, the CTA context
+constexpr uint32_t kWalkBytes = (kHornerThreads / 32) * 16;  // one WalkSlot per row warp
 // Batched seal shared memory: AES tables, the chain table H^512 (H^32 for
 // small objects), the row-warp fold tables H^8, H^1, H^2, H^4 (the slots the
 // small-object path reads), the hand-off buffers and their mbarriers.
 constexpr uint32_t kSealBatchFold = kAesBytes + kGhBytes;
 constexpr uint32_t kSealBatchHandoff = kSealBatchFold + 4 * 8192u;
 constexpr uint32_t kSealBatchSync = kSealBatchHandoff + kHandoffBytes;
-constexpr uint32_t kSealBatchSmem = kSealBatchSync + kHandoffSyncBytes;
+constexpr uint32_t kSealBatchWalk = kSealBatchSync + kHandoffSyncBytes;
+constexpr uint32_t kSealBatchSmem = kSealBatchWalk + kWalkBytes;
 static_assert(kSealBatchFold == kSmallFold, "the small-object path reads the seal fold slots");
 static_assert(kSealBatchSmem <= 227u * 1024u, "batched seal shared memory exceeds the per-block limit");
 // Batched open-GHASH shared memory: the single-object layout up to the
 // compact H^512 table, then the hand-off.
 constexpr uint32_t kOpenBatchHandoff = kOpenHt + 8192u;
 constexpr uint32_t kOpenBatchSync = kOpenBatchHandoff + kHandoffBytes;
-constexpr uint32_t kOpenBatchSmem = kOpenBatchSync + kHandoffSyncBytes;
+constexpr uint32_t kOpenBatchWalk = kOpenBatchSync + kHandoffSyncBytes;
+constexpr uint32_t kOpenBatchSmem = kOpenBatchWalk + kWalkBytes;
 
 // Alignment classes: 2 v + p, v = the frame's ciphertext class (seal: store
 // funnel word part 0..3, 4 = aligned; open: load funnel word part, same
 // coding) and p = 1 when the plaintext side (seal src, open dst) is 16-B
-// aligned. Each tile record carries its object's class; the work kernels run
-// a loop specialised for it and switch loops only when the class changes.
+// aligned. Each tile object carries its class; the work kernels run a loop
+// specialised for it and switch loops only when the class changes.
 constexpr int kClasses = 10;
 
 struct BatchHeader {
-    uint32_t total_tiles;
-    uint32_t next_tile[2];   // queue heads: [0] seal / open GHASH, [1] open CTR
-    uint32_t iters_max;      // J*
-    uint32_t small_count;    // objects of at most kSmallMaxBlocks blocks, one warp each
-    uint32_t small_next[2];  // small-object queue heads: [0] seal, [1] open
-    uint32_t fault;          // nonzero: a work kernel's hand-off wait gave up (results invalid)
-    uint32_t pad[8];
+    unsigned long long total_rows;  // R: rows of all tile objects
+    uint32_t chunks;                // M (0 when there are no tile objects)
+    uint32_t next_chunk[2];         // queue heads: [0] seal / open GHASH, [1] open CTR
+    uint32_t tile_objects;          // K
+    uint32_t small_count;           // objects of at most kSmallMaxBlocks blocks, one warp each
+    uint32_t fault;                 // nonzero: a work kernel's hand-off wait gave up (results invalid)
+    uint32_t small_next[2];         // small-object queue heads: [0] seal, [1] open
+    uint32_t pad[6];
 };
 static_assert(sizeof(BatchHeader) <= 256, "batch header fits its 256-byte area");
 
-struct TileRec {
+// A tile object in the row space: its first row, descriptor index, rows and
+// alignment class.
+struct TileObj {
+    unsigned long long row_start;
     uint32_t item;
-    uint32_t cta;            // tile index c within the object (bits 0-23) | class << 24
+    uint32_t meta;                  // rows (bits 0-23) | class << 24
 };
-constexpr uint32_t kTileIndexMask = 0x00ffffffu;
+constexpr uint32_t kRowsMask = 0x00ffffffu;
+static_assert((kBatchMaxBlocks + kHornerThreads - 1) / kHornerThreads <= kRowsMask, "rows fit the meta field");
 
+__host__ __device__ constexpr size_t batch_round256(size_t x) { return (x + 255) / 256 * 256; }
 __host__ __device__ constexpr size_t batch_slots_offset() { return 256; }
-__host__ __device__ constexpr size_t batch_tiles_offset(size_t count)
+__host__ __device__ constexpr size_t batch_objs_offset(size_t count)
 {
-    return 256 + (count * sizeof(Slot) + 255) / 256 * 256;
+    return 256 + batch_round256(count * sizeof(Slot));
 }
+__host__ __device__ constexpr size_t batch_chunks_offset(size_t count)
+{
+    return batch_objs_offset(count) + batch_round256((count + 1) * sizeof(TileObj));
+}
+// Planned per-segment overhead, in rows of the seal loop: a segment's fold,
+// hand-off, descriptor fetch and pipeline start cost about three rows on
+// B200, so chunks of many small objects get fewer rows.
+constexpr uint32_t kSegmentCostRows = 5;
+
+// A chunk of the row space: its first row and the tile object holding it.
+struct ChunkRec {
+    unsigned long long row_start;
+    uint32_t first;
+    uint32_t pad;
+};
+
 __host__ __device__ constexpr size_t batch_small_offset(size_t count)
 {
-    return batch_tiles_offset(count) + (count + kBatchExtraTiles) * sizeof(TileRec);
+    return batch_chunks_offset(count) + (kMaxChunks + 1) * sizeof(ChunkRec);
 }
 __host__ __device__ constexpr size_t batch_workspace_bytes(size_t count)
 {
     return batch_small_offset(count) + count * sizeof(uint32_t);
+}
+
+// First row of chunk c and the chunk holding row x (0 <= x < R), for M
+// chunks of R rows: chunk c = [floor(c R / M), floor((c+1) R / M)).
+__host__ __device__ __forceinline__ unsigned long long chunk_row(uint32_t c, unsigned long long R, uint32_t M)
+{
+    return static_cast<unsigned long long>(c) * R / M;
+}
+__host__ __device__ __forceinline__ uint32_t chunk_of(unsigned long long x, unsigned long long R, uint32_t M)
+{
+    return static_cast<uint32_t>(((x + 1) * M - 1) / R);
+}
+
+// Chunks for R rows on `sms` SMs: kChunksPerSm per SM, fewer while a chunk
+// would be shorter than kMinChunkRows, at least one per SM, never more than
+// R (so no chunk is empty).
+__host__ __device__ __forceinline__ uint32_t batch_chunk_count(unsigned long long R, uint32_t sms)
+{
+    if (R == 0) {
+        return 0;
+    }
+    unsigned long long per = R / (static_cast<unsigned long long>(sms) * kMinChunkRows);
+    per = per < 1 ? 1 : (per > kChunksPerSm ? kChunksPerSm : per);
+    const unsigned long long m = per * sms;
+    return static_cast<uint32_t>(m < R ? m : R);
 }
 
 struct BatchArgs {
@@ -149,247 +202,143 @@ __device__ __forceinline__ int item_class(const BatchItem& it, int open)
 
 // ------------------------------------------------------------------ plan
 
+// Block-wide exclusive scan of one 64-bit value per thread (kPlanThreads
+// threads, all calling); `warp_sums` holds kPlanThreads / 32 values. Returns
+// the thread's exclusive prefix; *total gets the sum.
+__device__ __forceinline__ unsigned long long plan_scan(unsigned long long v, unsigned long long* warp_sums,
+                                                        unsigned long long* total)
+{
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    unsigned long long incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const unsigned long long u = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) {
+            incl += u;
+        }
+    }
+    if (lane == 31) {
+        warp_sums[warp] = incl;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        unsigned long long w = warp_sums[lane];
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const unsigned long long u = __shfl_up_sync(0xffffffffu, w, d);
+            if (lane >= d) {
+                w += u;
+            }
+        }
+        warp_sums[lane] = w;
+    }
+    __syncthreads();
+    *total = warp_sums[kPlanThreads / 32 - 1];
+    const unsigned long long before = warp > 0 ? warp_sums[warp - 1] : 0ull;
+    __syncthreads();  // warp_sums may be reused
+    return before + incl - v;
+}
+
 // `open` selects the descriptor rules: seal needs capacity >= P + 29; open
 // needs frame length >= P + 29 and an auth_ok pointer. sms = SMs the work
-// kernels run on (at most kBatchMaxSms).
+// kernels run on (at most kBatchMaxSms). The row space holds the tile
+// objects grouped by alignment class (so a CTA's segments mostly share one
+// specialised loop); the order inside a class follows the atomics.
 __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* items, uint32_t count,
                                                                   uint8_t* ws, int open, uint32_t sms)
 {
-    __shared__ unsigned long long red[kPlanThreads / 32];
-    __shared__ uint32_t red_max[kPlanThreads / 32];
-    __shared__ unsigned int hist[kBuckets][kClasses];
-    __shared__ unsigned int cursor[kBuckets][kClasses];
-    __shared__ unsigned long long total_rows;
-    __shared__ uint32_t max_rows;
-    __shared__ uint32_t cand[kPlanCandidates];
-    __shared__ unsigned long long cand_tiles[kPlanCandidates];
-    __shared__ uint32_t cand_part[kPlanThreads / 32][kPlanCandidates];
-    __shared__ uint32_t jstar_s;
+    __shared__ unsigned long long warp_sums[kPlanThreads / 32];
+    __shared__ unsigned long long class_rows[kClasses];
+    __shared__ unsigned int class_objs[kClasses];
+    __shared__ unsigned int class_cursor[kClasses];
+    __shared__ unsigned long long total_rows_s;
+    __shared__ uint32_t tile_objs_s;
+    __shared__ uint32_t chunks_s;
     __shared__ unsigned int small_hist[kSmallBuckets];
     __shared__ unsigned int small_cursor[kSmallBuckets];
     BatchHeader* hdr = reinterpret_cast<BatchHeader*>(ws);
-    uint32_t* small_list = reinterpret_cast<uint32_t*>(ws + batch_small_offset(count));
     Slot* st = reinterpret_cast<Slot*>(ws + batch_slots_offset());
-    TileRec* rec = reinterpret_cast<TileRec*>(ws + batch_tiles_offset(count));
+    TileObj* objs = reinterpret_cast<TileObj*>(ws + batch_objs_offset(count));
+    ChunkRec* chunks = reinterpret_cast<ChunkRec*>(ws + batch_chunks_offset(count));
+    uint32_t* small_list = reinterpret_cast<uint32_t*>(ws + batch_small_offset(count));
     const int tid = threadIdx.x;
+    const int lane = tid & 31;
     constexpr uint64_t T = kHornerThreads;
     pdl_release();
-    for (int i = tid; i < kClasses * kBuckets; i += kPlanThreads) {
-        hist[i / kClasses][i % kClasses] = 0;
-    }
     if (tid < kSmallBuckets) {
         small_hist[tid] = 0;
+    }
+    if (tid < kClasses) {
+        class_rows[tid] = 0;
+        class_objs[tid] = 0;
     }
     __syncthreads();
     pdl_wait();  // descriptors and workspace may belong to earlier work on the stream
 
-    // Pass 1: validate, rows per object (a zero-length object is one row:
-    // its tile writes the header and tag), reset the slot.
-    unsigned long long rows_sum = 0;
-    uint32_t rows_max = 0;
-    for (uint32_t i = tid; i < count; i += kPlanThreads) {
-        BatchItem& it = items[i];
-        const uint64_t P = it.plen;
-        const uint64_t n = P / 16u + ((P & 15u) != 0);
-        bool ok = it.src != nullptr && it.dst != nullptr && n <= kBatchMaxBlocks && it.capacity >= P + 29u;
-        if (open) {
-            ok = ok && it.auth_ok != nullptr;
-        }
-        // small objects go to the warp-per-object list (aux[2] = bucket + 1),
-        // the others to the tile planner (aux[0] = rows)
-        const bool small = ok && n <= kSmallMaxBlocks;
-        const uint32_t rows = ok && !small ? static_cast<uint32_t>((n + T - 1) / T) : 0u;
-        it.status = ok ? 0 : -1;
-        Slot& s = st[i];
-        s.acc_hi = 0;
-        s.acc_lo = 0;
-        s.ticket = 0;
-        s.aux[0] = rows;
-        s.aux[1] = 0;
-        s.aux[2] = 0;
-        if (small) {
-            const int b = 31 - __clz(static_cast<int>(n | 1u));
-            s.aux[2] = static_cast<uint32_t>(b + 1);
-            atomicAdd(&small_hist[b], 1u);
-        }
-        rows_sum += rows;
-        rows_max = rows > rows_max ? rows : rows_max;
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        rows_sum += __shfl_xor_sync(0xffffffffu, rows_sum, o);
-        const uint32_t m = __shfl_xor_sync(0xffffffffu, rows_max, o);
-        rows_max = m > rows_max ? m : rows_max;
-    }
-    if ((tid & 31) == 0) {
-        red[tid >> 5] = rows_sum;
-        red_max[tid >> 5] = rows_max;
-    }
-    __syncthreads();
-    if (tid < 32) {
-        unsigned long long v = red[tid];
-        uint32_t m = red_max[tid];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            v += __shfl_xor_sync(0xffffffffu, v, o);
-            const uint32_t mo = __shfl_xor_sync(0xffffffffu, m, o);
-            m = mo > m ? mo : m;
-        }
-        if (tid == 0) {
-            total_rows = v;
-            max_rows = m;
-        }
-    }
-    __syncthreads();
-
-    // Tile height J*. Candidates: the heights giving w = 1..8 tiles per SM
-    // (ceil(R / (w sms))) and the heights cutting the tallest object into
-    // k = 1..8 equal tiles (ceil(max_rows / k)). Each is scored by the
-    // makespan of equal tiles on `sms` SMs, ceil(tiles / sms) x (R / tiles +
-    // kTileOverheadRows), among those whose tile count fits the record area
-    // (the w = 8 height always does); ties go to the taller tile.
-    const unsigned long long R = total_rows;
-    const int warp = tid >> 5;
-    const int lane = tid & 31;
-    // Tile counts per candidate: every thread counts its own objects for all
-    // candidates, then a warp shuffle reduction and a sum over the warps.
-    if (tid < kPlanCandidates) {
-        unsigned long long j;
-        if (tid < 8) {
-            const unsigned long long slots = static_cast<unsigned long long>(tid + 1) * sms;
-            j = (R + slots - 1) / slots;
-        } else {
-            const uint32_t k = static_cast<uint32_t>(tid - 7);
-            j = (max_rows + k - 1) / k;
-        }
-        j = j > max_rows ? max_rows : j;
-        cand[tid] = static_cast<uint32_t>(j < 1 ? 1 : j);
-    }
-    __syncthreads();
-    {
-        uint32_t loc[kPlanCandidates];
-#pragma unroll
-        for (int c = 0; c < kPlanCandidates; ++c) {
-            loc[c] = 0;
-        }
-        for (uint32_t i = tid; i < count; i += kPlanThreads) {
-            const uint32_t rows = st[i].aux[0];
-            if (rows == 0) {
-                continue;
+    // Pass 1: validate, rows per tile object (small and invalid objects have
+    // none), reset the slot (aux[1] keeps the class until pass 3), the
+    // small-object histogram and the per-class totals (one shared atomic per
+    // class present in a warp).
+    for (uint32_t base = 0; base < count; base += kPlanThreads) {
+        const uint32_t i = base + static_cast<uint32_t>(tid);
+        int key = -1;
+        uint32_t rows = 0;
+        if (i < count) {
+            BatchItem& it = items[i];
+            const uint64_t P = it.plen;
+            const uint64_t n = P / 16u + ((P & 15u) != 0);
+            bool ok = it.src != nullptr && it.dst != nullptr && n <= kBatchMaxBlocks && it.capacity >= P + 29u;
+            if (open) {
+                ok = ok && it.auth_ok != nullptr;
             }
-#pragma unroll
-            for (int c = 0; c < kPlanCandidates; ++c) {
-                const uint32_t J = cand[c];
-                loc[c] += rows <= J ? 1u : (rows + J - 1) / J;
+            const bool small = ok && n <= kSmallMaxBlocks;
+            rows = ok && !small ? static_cast<uint32_t>((n + T - 1) / T) : 0u;
+            it.status = ok ? 0 : -1;
+            if (rows != 0) {
+                key = item_class(it, open);
+            }
+            Slot& s = st[i];
+            s.acc_hi = 0;
+            s.acc_lo = 0;
+            s.ticket = 0;
+            s.aux[0] = rows;
+            s.aux[1] = static_cast<uint32_t>(key);
+            s.aux[2] = 0;
+            if (small) {
+                const int b = 31 - __clz(static_cast<int>(n | 1u));
+                s.aux[2] = static_cast<uint32_t>(b + 1);
+                atomicAdd(&small_hist[b], 1u);
             }
         }
-#pragma unroll
-        for (int c = 0; c < kPlanCandidates; ++c) {
-            uint32_t v = loc[c];
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                v += __shfl_xor_sync(0xffffffffu, v, o);
-            }
-            if (lane == 0) {
-                cand_part[warp][c] = v;
-            }
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        const unsigned sum = __reduce_add_sync(peers, rows);  // at most 32 x 2^23
+        if (key >= 0 && lane == __ffs(peers) - 1) {
+            atomicAdd(&class_rows[key], static_cast<unsigned long long>(sum));
+            atomicAdd(&class_objs[key], static_cast<unsigned>(__popc(peers)));
         }
     }
     __syncthreads();
-    if (tid < kPlanCandidates) {
-        unsigned long long t = 0;
-        for (int w = 0; w < kPlanThreads / 32; ++w) {
-            t += cand_part[w][tid];
-        }
-        cand_tiles[tid] = t;
-    }
-    __syncthreads();
-    // Warp 0 scores the candidates (lane c = candidate c) and keeps the
-    // smallest estimate, the taller tile on a tie.
-    if (warp == 0) {
-        int valid = 0;
-        double est = 0.0;
-        uint32_t J = 1;
-        if (lane < kPlanCandidates) {
-            const unsigned long long tiles = cand_tiles[lane];
-            J = cand[lane];
-            valid = tiles != 0 && tiles <= static_cast<unsigned long long>(count) + kBatchExtraTiles ? 1 : 0;
-            if (valid) {
-                const double waves = static_cast<double>((tiles + sms - 1) / sms);
-                est = waves * (static_cast<double>(R) / static_cast<double>(tiles) + kTileOverheadRows);
-            }
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            const int ov = __shfl_xor_sync(0xffffffffu, valid, o);
-            const double oe = __shfl_xor_sync(0xffffffffu, est, o);
-            const uint32_t oj = __shfl_xor_sync(0xffffffffu, J, o);
-            if (ov && (!valid || oe < est || (oe == est && oj > J))) {
-                valid = 1;
-                est = oe;
-                J = oj;
-            }
-        }
-        if (lane == 0) {
-            jstar_s = valid ? J : 1u;
-        }
-    }
-    __syncthreads();
-    const uint32_t jstar = jstar_s;
-
-    // Pass 2: tile height and count per object; histogram of tiles by
-    // (alignment class, floor(log2 J)).
-    for (uint32_t i = tid; i < count; i += kPlanThreads) {
-        Slot& s = st[i];
-        const uint32_t rows = s.aux[0];
-        if (rows == 0) {
-            continue;
-        }
-        const uint32_t J = rows < jstar ? rows : jstar;
-        const uint64_t P = items[i].plen;
-        const uint64_t n = P / 16u + ((P & 15u) != 0);
-        const uint64_t span = static_cast<uint64_t>(J) * T;
-        uint64_t G = (n + span - 1) / span;
-        G = G < 1 ? 1 : G;
-        s.aux[0] = J;
-        s.aux[1] = static_cast<uint32_t>(G);
-        atomicAdd(&hist[31 - __clz(static_cast<int>(J))][item_class(items[i], open)], static_cast<unsigned int>(G));
-    }
-    __syncthreads();
-    // Records: tallest bucket first, classes in order inside a bucket (so
-    // the queue ends on short tiles and neighbouring tiles share a class).
-    // Warp 0: lane l owns bucket 31 - l; an exclusive scan over the lanes
-    // gives each bucket's start.
-    static_assert(kBuckets == 32, "one lane per height bucket");
-    if (warp == 0) {
-        const int b = kBuckets - 1 - lane;
-        unsigned int total = 0;
-#pragma unroll
+    if (tid == 0) {
+        unsigned long long R = 0;
+        uint32_t K = 0;
         for (int c = 0; c < kClasses; ++c) {
-            total += hist[b][c];
+            class_cursor[c] = K;
+            K += class_objs[c];
+            R += class_rows[c];
         }
-        unsigned int incl = total;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const unsigned int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) {
-                incl += v;
-            }
-        }
-        unsigned int pos = incl - total;
-#pragma unroll
-        for (int c = 0; c < kClasses; ++c) {
-            cursor[b][c] = pos;
-            pos += hist[b][c];
-        }
-        if (lane == 31) {
-            hdr->total_tiles = incl;
-            hdr->next_tile[0] = 0;
-            hdr->next_tile[1] = 0;
-            hdr->iters_max = jstar;
-            hdr->fault = 0;
-        }
-    } else if (warp == 1 && lane == 0) {
+        const uint32_t M = batch_chunk_count(R, sms);
+        total_rows_s = R;
+        tile_objs_s = K;
+        chunks_s = M;
+        hdr->total_rows = R;
+        hdr->chunks = M;
+        hdr->next_chunk[0] = 0;
+        hdr->next_chunk[1] = 0;
+        hdr->tile_objects = K;
+        hdr->fault = 0;
+        objs[K] = TileObj{R, 0xffffffffu, 0u};
+    } else if (tid == 32) {
         // small objects: largest bucket first
         unsigned int pos = 0;
         for (int b = kSmallBuckets - 1; b >= 0; --b) {
@@ -402,21 +351,79 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     }
     __syncthreads();
 
-    // Pass 3: tile records and the small-object list.
-    for (uint32_t i = tid; i < count; i += kPlanThreads) {
-        const Slot& s = st[i];
-        const uint32_t G = s.aux[1];
-        if (G == 0) {
-            if (s.aux[2] != 0 && s.aux[0] == 0) {
+    // Pass 2: place the tile objects, class by class; the small-object list.
+    for (uint32_t base = 0; base < count; base += kPlanThreads) {
+        const uint32_t i = base + static_cast<uint32_t>(tid);
+        int key = -1;
+        uint32_t rows = 0;
+        if (i < count) {
+            const Slot& s = st[i];
+            rows = s.aux[0];
+            if (rows != 0) {
+                key = static_cast<int>(s.aux[1]);
+            } else if (s.aux[2] != 0) {
                 small_list[atomicAdd(&small_cursor[s.aux[2] - 1], 1u)] = i;
             }
-            continue;
         }
-        const uint32_t cls = static_cast<uint32_t>(item_class(items[i], open));
-        const unsigned int p = atomicAdd(&cursor[31 - __clz(static_cast<int>(s.aux[0]))][cls], G);
-        for (uint32_t c = 0; c < G; ++c) {
-            rec[p + c] = TileRec{i, c | (cls << 24)};
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        if (key >= 0) {
+            const int leader = __ffs(peers) - 1;
+            unsigned pos = 0;
+            if (lane == leader) {
+                pos = atomicAdd(&class_cursor[key], static_cast<unsigned>(__popc(peers)));
+            }
+            pos = __shfl_sync(peers, pos, leader) + static_cast<unsigned>(__popc(peers & ((1u << lane) - 1u)));
+            objs[pos].item = i;
+            objs[pos].meta = rows | (static_cast<uint32_t>(key) << 24);
         }
+    }
+    __syncthreads();
+
+    // Pass 3: row starts (a scan over contiguous ranges of the placed
+    // objects), each object's segment count, the tile object holding each
+    // chunk's first row.
+    const unsigned long long R = total_rows_s;
+    const uint32_t K = tile_objs_s;
+    const uint32_t M = chunks_s;
+    const uint32_t per = (K + kPlanThreads - 1) / kPlanThreads;
+    const uint32_t lo = static_cast<uint32_t>(tid) * per < K ? static_cast<uint32_t>(tid) * per : K;
+    const uint32_t hi = lo + per < K ? lo + per : K;
+    unsigned long long mine = 0;
+    for (uint32_t k = lo; k < hi; ++k) {
+        mine += objs[k].meta & kRowsMask;
+    }
+    unsigned long long total;
+    unsigned long long row = plan_scan(mine, warp_sums, &total);
+    // Chunks are cut in a cost space where tile object k weighs its rows
+    // plus o (kSegmentCostRows): object k covers costs [P_k, P_k + o + rows)
+    // with P_k = S_k + o k, its overhead first. Chunk c starts at cost
+    // x_c = floor(c C / M), C = R + o K, which maps to row
+    // S_k + max(0, x_c - P_k - o) of the object holding x_c; row r of object k
+    // (cost y = P_k + o + r - S_k) lies in chunk chunk_of(y, C, M). Narrow
+    // chunks (under 2 (o + 1) cost units) drop the overhead weight (o = 0,
+    // equal rows), so no chunk is empty.
+    const unsigned long long o_full = kSegmentCostRows;
+    const unsigned long long C_full = R + o_full * K;
+    const unsigned long long o = M != 0 && C_full / M >= 2 * (o_full + 1) ? o_full : 0ull;
+    const unsigned long long C = R + o * K;
+    for (uint32_t k = lo; k < hi; ++k) {
+        const uint32_t rows = objs[k].meta & kRowsMask;
+        objs[k].row_start = row;
+        const unsigned long long p = row + o * k;  // P_k
+        const uint32_t first = chunk_of(p + o, C, M);
+        const uint32_t last = chunk_of(p + o + rows - 1, C, M);
+        st[objs[k].item].aux[1] = last - first + 1;
+        // chunks whose first cost falls in [P_k, P_k + o + rows)
+        uint32_t c = chunk_of(p, C, M);
+        c = chunk_row(c, C, M) == p ? c : c + 1;
+        for (; c <= last; ++c) {
+            const unsigned long long x = chunk_row(c, C, M);
+            chunks[c] = ChunkRec{row + (x > p + o ? x - p - o : 0ull), k, 0u};
+        }
+        row += rows;
+    }
+    if (tid == 0) {
+        chunks[M] = ChunkRec{R, K, 0u};
     }
 }
 
@@ -435,29 +442,166 @@ __device__ __forceinline__ bool batch_object_sum(Slot* slot, uint32_t G, uint4 f
     return cta_accumulate(slot, fold, uhi, ulo, lane, G, shi, slo);
 }
 
-// Shared state of the work kernels: the workspace views and the CTA's
-// coordinates.
+// Shared state of the work kernels. R, M and the workspace views sit in a
+// shared-memory context block (kCtxBytes at `ctx`, written by thread 0, read
+// where used through volatile loads), so that none of them is held in
+// registers across a segment's rows.
+constexpr uint32_t kCtxBytes = 40;
 struct BatchCta {
-    BatchHeader* hdr;
-    Slot* st;
-    const TileRec* rec;
-    uint32_t total;
+    BatchHeader* hdr;        // the workspace (a kernel parameter)
+    const uint8_t* ctx;
     int tid;
     int lane;
     int warp;
 };
 
-__device__ __forceinline__ int tile_class(const BatchCta& c, uint32_t tile)
+__device__ __forceinline__ unsigned long long ctx_u64(const BatchCta& c, int off)
 {
-    return static_cast<int>(c.rec[tile].cta >> 24);
+    return *reinterpret_cast<const volatile unsigned long long*>(c.ctx + off);
+}
+__device__ __forceinline__ unsigned long long cta_rows(const BatchCta& c) { return ctx_u64(c, 0); }
+__device__ __forceinline__ uint32_t cta_chunks(const BatchCta& c)
+{
+    return *reinterpret_cast<const volatile uint32_t*>(c.ctx + 8);
+}
+__device__ __forceinline__ const TileObj* cta_objs(const BatchCta& c)
+{
+    return reinterpret_cast<const TileObj*>(ctx_u64(c, 16));
+}
+__device__ __forceinline__ const ChunkRec* cta_chunk_recs(const BatchCta& c)
+{
+    return reinterpret_cast<const ChunkRec*>(ctx_u64(c, 24));
+}
+__device__ __forceinline__ Slot* cta_slots(const BatchCta& c)
+{
+    return reinterpret_cast<Slot*>(ctx_u64(c, 32));
 }
 
-// First queue index of this CTA (all threads); the barriers bracket the
-// shared broadcast.
-__device__ __forceinline__ uint32_t first_tile(volatile uint32_t* next_s, const BatchCta& c, int pass)
+// The caller's next barrier publishes thread 0's context writes.
+__device__ __forceinline__ BatchCta batch_cta(const BatchArgs& a, uint8_t* ctx, int tid)
+{
+    auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
+    if (tid == 0) {
+        *reinterpret_cast<volatile unsigned long long*>(ctx) = hdr->total_rows;
+        *reinterpret_cast<volatile uint32_t*>(ctx + 8) = hdr->chunks;
+        *reinterpret_cast<volatile unsigned long long*>(ctx + 16) =
+            reinterpret_cast<unsigned long long>(a.ws + batch_objs_offset(a.count));
+        *reinterpret_cast<volatile unsigned long long*>(ctx + 24) =
+            reinterpret_cast<unsigned long long>(a.ws + batch_chunks_offset(a.count));
+        *reinterpret_cast<volatile unsigned long long*>(ctx + 32) =
+            reinterpret_cast<unsigned long long>(a.ws + batch_slots_offset());
+    }
+    return BatchCta{hdr, ctx, tid, tid & 31, tid >> 5};
+}
+
+// Position in the row space: chunk `chunk`, tile object k. The rows left in
+// the chunk start at max(first row of the chunk, first row of object k).
+struct Cursor {
+    uint32_t chunk;
+    uint32_t k;
+};
+
+// Opens chunk `chunk`; false once the queue is exhausted.
+__device__ __forceinline__ bool cursor_open(const BatchCta& c, uint32_t chunk, Cursor& cur)
+{
+    if (chunk >= cta_chunks(c)) {
+        return false;
+    }
+    cur.chunk = chunk;
+    cur.k = cta_chunk_recs(c)[chunk].first;
+    return true;
+}
+
+// The segment at the cursor: rows [r0, r1) of tile object k, whose rows are
+// [0, rows) (row r = blocks n - (rows - r) T .. + T); `last` when it ends
+// the chunk.
+struct Segment {
+    uint32_t item;
+    uint32_t rows;
+    uint32_t r0;
+    uint32_t r1;
+    bool last;
+};
+
+__device__ __forceinline__ Segment segment_at(const BatchCta& c, const Cursor& cur)
+{
+    const TileObj o = cta_objs(c)[cur.k];
+    const ChunkRec* cr = cta_chunk_recs(c) + cur.chunk;
+    const unsigned long long a0 = cr[0].row_start;
+    const unsigned long long b = cr[1].row_start;
+    const uint32_t rows = o.meta & kRowsMask;
+    const unsigned long long end = o.row_start + rows;
+    const unsigned long long a = a0 > o.row_start ? a0 : o.row_start;
+    return Segment{o.item, rows, static_cast<uint32_t>(a - o.row_start),
+                   static_cast<uint32_t>((b < end ? b : end) - o.row_start), end >= b};
+}
+
+// Moves past segment sg; true when that ends the chunk (otherwise the next
+// tile object starts where this one ends in the row space).
+__device__ __forceinline__ bool cursor_step(Cursor& cur, const Segment& sg)
+{
+    if (sg.last) {
+        return true;
+    }
+    ++cur.k;
+    return false;
+}
+
+__device__ __forceinline__ int cursor_class(const BatchCta& c, const Cursor& cur)
+{
+    return static_cast<int>(cta_objs(c)[cur.k].meta >> 24);
+}
+
+// Row-warp walk state in shared memory, one slot per row warp: [0] chunk,
+// [1] tile object of the next segment (kChunkEnd after a chunk's last one),
+// [2] hand-off count. All lanes hold the same values, so every lane writes
+// and reads its warp's slot, and none of it stays in registers across a
+// segment's rows. The slot's address is rebuilt from the shared base where
+// used.
+constexpr uint32_t kChunkEnd = 0xffffffffu;
+struct WalkSlot {
+    uint8_t* base;   // shared base + the kernel's walk offset
+};
+
+__device__ __forceinline__ volatile uint32_t* walk_word(const WalkSlot& ws, int i)
+{
+    return reinterpret_cast<volatile uint32_t*>(ws.base + 16 * (threadIdx.x >> 5)) + i;
+}
+__device__ __forceinline__ Cursor walk_cursor(const WalkSlot& ws)
+{
+    return Cursor{*walk_word(ws, 0), *walk_word(ws, 1)};
+}
+// Opens `chunk` into the slot; false once the queue is exhausted.
+__device__ __forceinline__ bool walk_open(const BatchCta& c, uint32_t chunk, const WalkSlot& ws)
+{
+    Cursor cur;
+    if (!cursor_open(c, chunk, cur)) {
+        return false;
+    }
+    *walk_word(ws, 0) = cur.chunk;
+    *walk_word(ws, 1) = cur.k;
+    return true;
+}
+
+// First block of segment sg (negative only when r0 = 0 and the object's first
+// row is partial) and the power d of its GHASH share: (rows - r1) T blocks
+// follow the segment, plus the length block.
+__device__ __forceinline__ int64_t segment_base(const Segment& sg, uint64_t P)
+{
+    const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
+    return n - static_cast<int64_t>(sg.rows - sg.r0) * kHornerThreads;
+}
+__device__ __forceinline__ unsigned long long segment_power(const Segment& sg)
+{
+    return static_cast<unsigned long long>(sg.rows - sg.r1) * kHornerThreads + 2ull;
+}
+
+// First chunk of this CTA (all threads); the barriers bracket the shared
+// broadcast.
+__device__ __forceinline__ uint32_t first_chunk(volatile uint32_t* next_s, const BatchCta& c, int pass)
 {
     if (c.tid == 0) {
-        *next_s = atomicAdd(&c.hdr->next_tile[pass], 1u);
+        *next_s = atomicAdd(&c.hdr->next_chunk[pass], 1u);
     }
     __syncthreads();
     const uint32_t t = *next_s;
@@ -473,9 +617,9 @@ __device__ __forceinline__ uint32_t first_tile(volatile uint32_t* next_s, const 
 // the object's sum and the tag (seal) or verdict (open). Hand-off j uses
 // buffer j & 1; its FULL mbarrier completes when the 16 row warps arrived,
 // its EMPTY mbarrier when the power warp has read the values, so a buffer is
-// rewritten only after it was read. Both sides take the tiles in the same
-// queue order: thread 0 takes the next index after its rows and passes it
-// along with the values.
+// rewritten only after it was read. Both sides walk the same segments: at the
+// end of a chunk thread 0 takes the next chunk index after its rows and
+// passes it along with the values.
 
 // Shared-memory views of the hand-off (kHandoffBytes of buffers at part_off,
 // kHandoffSyncBytes of mbarriers and words at sync_off).
@@ -483,9 +627,10 @@ struct Handoff {
     uint4* part;               // [2][32] fold values V_p
     uint64_t* full;            // [2]
     uint64_t* empty;           // [2]
-    volatile uint32_t* next;   // [2] queue index taken after the buffer's tile
-    volatile uint32_t* first;  // first queue index of the CTA
+    volatile uint32_t* next;   // [2] chunk index taken after the buffer's segment (when it ended a chunk)
+    volatile uint32_t* first;  // first chunk index of the CTA
     volatile uint32_t* abort;  // raised by a wait that gave up
+    uint8_t* ctx;              // kCtxBytes for batch_cta
 };
 
 __device__ __forceinline__ Handoff handoff_at(uint8_t* smem, uint32_t part_off, uint32_t sync_off)
@@ -493,7 +638,8 @@ __device__ __forceinline__ Handoff handoff_at(uint8_t* smem, uint32_t part_off, 
     uint8_t* s = smem + sync_off;
     return Handoff{reinterpret_cast<uint4*>(smem + part_off), reinterpret_cast<uint64_t*>(s),
                    reinterpret_cast<uint64_t*>(s + 16), reinterpret_cast<volatile uint32_t*>(s + 32),
-                   reinterpret_cast<volatile uint32_t*>(s + 40), reinterpret_cast<volatile uint32_t*>(s + 44)};
+                   reinterpret_cast<volatile uint32_t*>(s + 40), reinterpret_cast<volatile uint32_t*>(s + 44),
+                   s + 48};
 }
 
 // Thread 0, before the CTA's first barrier.
@@ -569,30 +715,26 @@ __device__ __forceinline__ bool handoff_failed(const Handoff& h, const BatchCta&
 
 // ------------------------------------------------------------------ seal
 
-// Row warps: tiles of one alignment class, from `tile` while the queue hands
-// out tiles of this class; returns the first tile of another class (or >=
-// total). Per-tile values are loaded where they are used so that only the
-// tile index stays live across the rows.
+// Row warps: segments of one alignment class from the cursor on; returns
+// true when the next segment has another class, false when the queue is
+// exhausted (or a hand-off gave up). Per-segment values are loaded where they
+// are used so that only the cursor stays live across the rows.
 template <int SQ, bool PT>
-__device__ __forceinline__ uint32_t seal_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c,
-                                               const Handoff& h, uint32_t tile, int cls, uint32_t& j)
+__device__ __forceinline__ bool seal_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, const Handoff& h,
+                                           const WalkSlot& ws, int cls)
 {
-    constexpr int64_t T = kHornerThreads;
     const uint4* ft = reinterpret_cast<const uint4*>(smem + kSealBatchFold);
     for (;;) {
         uint4 q;
         {
-            const TileRec tr = c.rec[tile];
-            const uint32_t cta = tr.cta & kTileIndexMask;
-            const BatchItem* it = a.items + tr.item;
-            const uint32_t J = c.st[tr.item].aux[0];
-            const uint32_t G = c.st[tr.item].aux[1];
+            const Cursor cur = walk_cursor(ws);
+            const Segment sg = segment_at(c, cur);
+            *walk_word(ws, 1) = sg.last ? kChunkEnd : cur.k + 1;
+            const BatchItem* it = a.items + sg.item;
             const uint64_t P = it->plen;
-            const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
-            const int64_t span = static_cast<int64_t>(J) * T;
             uint8_t* frame = it->dst;
             const uint32_t ivw[3] = {it->iv[0], it->iv[1], it->iv[2]};
-            if (cta == 0 && c.tid == 0) {
+            if (sg.r0 == 0 && c.tid == 0) {
                 frame[0] = 1;
                 for (int b = 0; b < 12; ++b) {
                     frame[1 + b] = static_cast<uint8_t>(ivw[b >> 2] >> (8 * (b & 3)));
@@ -602,49 +744,50 @@ __device__ __forceinline__ uint32_t seal_class(uint8_t* smem, const BatchArgs& a
             uint32_t store_r;
             store_class(frame + 13, sq, store_r);  // sq == SQ for this class
             (void)sq;
-            const SealTile t{it->src, frame + 13, P, n - static_cast<int64_t>(G - cta) * span,
-                             static_cast<int64_t>(J), {ivw[0] ^ a.rk[0], ivw[1] ^ a.rk[1], ivw[2] ^ a.rk[2]},
-                             store_r};
+            const SealTile t{it->src, frame + 13, P, segment_base(sg, P), static_cast<int64_t>(sg.r1 - sg.r0),
+                             {ivw[0] ^ a.rk[0], ivw[1] ^ a.rk[1], ivw[2] ^ a.rk[2]}, store_r};
             q = seal_rows<SQ, PT>(t, a.rk, a.kt.gh_pow2, c.tid, c.lane);
         }
+        const bool chunk_done = *walk_word(ws, 1) == kChunkEnd;
         uint32_t taken = 0;
-        if (c.tid == 0) {
-            taken = atomicAdd(&c.hdr->next_tile[0], 1u);
+        if (chunk_done && c.tid == 0) {
+            taken = atomicAdd(&c.hdr->next_chunk[0], 1u);
         }
         const uint4 v = warp_fold_pairs<true>(q, ft, c.lane);
+        const uint32_t j = *walk_word(ws, 2);
         uint32_t next;
         if (!row_handoff(h, j, v, taken, c, next)) {
-            return c.total;
+            return false;
         }
-        ++j;
-        if (next >= c.total || tile_class(c, next) != cls) {
-            return next;
+        *walk_word(ws, 2) = j + 1;
+        if (chunk_done && !walk_open(c, next, ws)) {
+            return false;
         }
-        tile = next;
+        if (cursor_class(c, walk_cursor(ws)) != cls) {
+            return true;
+        }
     }
 }
 
-// Power warp of the batched seal, over the same tiles as the row warps:
-// E_K(J0), L*H and the basis of H^d while the tile's rows run, then the fold
-// levels 4..8 (the key's global tables), the object's sum and, once the
-// object's last tile is in, its tag.
+// Power warp of the batched seal, over the same segments as the row warps:
+// E_K(J0), L*H and the basis of H^d while the segment's rows run, then the
+// fold levels 4..8 (the key's global tables), the object's sum and, once the
+// object's last segment is in, its tag.
 __device__ __forceinline__ void seal_power_loop(const BatchArgs& a, const BatchCta& c, const Handoff& h,
-                                                uint32_t tile)
+                                                uint32_t chunk)
 {
-    constexpr unsigned long long T = kHornerThreads;
-    for (uint32_t j = 0; tile < c.total; ++j) {
-        const TileRec tr = c.rec[tile];
-        const uint32_t cta = tr.cta & kTileIndexMask;
-        Slot* slot = c.st + tr.item;
-        const BatchItem* it = a.items + tr.item;
-        const uint32_t J = slot->aux[0];
+    Cursor cur;
+    bool more = cursor_open(c, chunk, cur);
+    for (uint32_t j = 0; more; ++j) {
+        const Segment sg = segment_at(c, cur);
+        Slot* slot = cta_slots(c) + sg.item;
+        const BatchItem* it = a.items + sg.item;
         const uint32_t G = slot->aux[1];
         const uint64_t P = it->plen;
         const uint32_t ivw[3] = {it->iv[0], it->iv[1], it->iv[2]};
-        const unsigned long long d = static_cast<unsigned long long>(G - 1 - cta) * J * T + 2ull;
         uint4 ej0, lh;
         unsigned long long uhi, ulo;
-        seal_power(ivw, a.rk, P, d, a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
+        seal_power(ivw, a.rk, P, segment_power(sg), a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
         uint4 v;
         uint32_t next;
         if (!power_take(h, j, c.lane, v, next)) {
@@ -658,7 +801,9 @@ __device__ __forceinline__ void seal_power_loop(const BatchArgs& a, const BatchC
                 it->dst[13 + P + c.lane] = static_cast<uint8_t>(byte_of(tag, c.lane));
             }
         }
-        tile = next;
+        if (cursor_step(cur, sg)) {
+            more = cursor_open(c, next, cur);
+        }
     }
 }
 
@@ -675,28 +820,27 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
         handoff_init(h);
     }
     pdl_wait();  // the plan kernel's workspace
-    auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
-    const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
-                     reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count)), hdr->total_tiles,
-                     tid, tid & 31, tid >> 5};
-    uint32_t tile = first_tile(h.first, c, 0);
+    const BatchCta c = batch_cta(a, h.ctx, tid);
+    const uint32_t chunk = first_chunk(h.first, c, 0);
     if (c.warp == kPowerWarp) {
-        seal_power_loop(a, c, h, tile);
+        seal_power_loop(a, c, h, chunk);
     } else {
-        uint32_t j = 0;
-        while (tile < c.total) {
-            const int cls = tile_class(c, tile);
+        const WalkSlot ws{smem + kSealBatchWalk};
+        *walk_word(ws, 2) = 0;
+        bool more = walk_open(c, chunk, ws);
+        while (more) {
+            const int cls = cursor_class(c, walk_cursor(ws));
             switch (cls) {
-            case 0: tile = seal_class<0, false>(smem, a, c, h, tile, cls, j); break;
-            case 1: tile = seal_class<0, true>(smem, a, c, h, tile, cls, j); break;
-            case 2: tile = seal_class<1, false>(smem, a, c, h, tile, cls, j); break;
-            case 3: tile = seal_class<1, true>(smem, a, c, h, tile, cls, j); break;
-            case 4: tile = seal_class<2, false>(smem, a, c, h, tile, cls, j); break;
-            case 5: tile = seal_class<2, true>(smem, a, c, h, tile, cls, j); break;
-            case 6: tile = seal_class<3, false>(smem, a, c, h, tile, cls, j); break;
-            case 7: tile = seal_class<3, true>(smem, a, c, h, tile, cls, j); break;
-            case 8: tile = seal_class<4, false>(smem, a, c, h, tile, cls, j); break;
-            default: tile = seal_class<4, true>(smem, a, c, h, tile, cls, j); break;
+            case 0: more = seal_class<0, false>(smem, a, c, h, ws, cls); break;
+            case 1: more = seal_class<0, true>(smem, a, c, h, ws, cls); break;
+            case 2: more = seal_class<1, false>(smem, a, c, h, ws, cls); break;
+            case 3: more = seal_class<1, true>(smem, a, c, h, ws, cls); break;
+            case 4: more = seal_class<2, false>(smem, a, c, h, ws, cls); break;
+            case 5: more = seal_class<2, true>(smem, a, c, h, ws, cls); break;
+            case 6: more = seal_class<3, false>(smem, a, c, h, ws, cls); break;
+            case 7: more = seal_class<3, true>(smem, a, c, h, ws, cls); break;
+            case 8: more = seal_class<4, false>(smem, a, c, h, ws, cls); break;
+            default: more = seal_class<4, true>(smem, a, c, h, ws, cls); break;
             }
         }
     }
@@ -704,9 +848,9 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
         return;
     }
 
-    // Small objects, one warp each, once the tiles are gone: H^32 over the
+    // Small objects, one warp each, once the chunks are gone: H^32 over the
     // chain table (the fold slots already hold H^8, H^1, H^2, H^4).
-    const uint32_t small_count = hdr->small_count;
+    const uint32_t small_count = c.hdr->small_count;
     if (small_count == 0) {
         return;
     }
@@ -716,7 +860,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
     for (;;) {
         uint32_t k = 0;
         if (c.lane == 0) {
-            k = atomicAdd(&hdr->small_next[0], 1u);
+            k = atomicAdd(&c.hdr->small_next[0], 1u);
         }
         k = __shfl_sync(0xffffffffu, k, 0);
         if (k >= small_count) {
@@ -728,72 +872,69 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
 
 // ------------------------------------------------------------------ open
 
-// Row warps of the GHASH pass: tiles whose frames share load class LQ (both
-// plaintext sides); returns the first tile of another load class (or >=
-// total).
+// Row warps of the GHASH pass: segments whose frames share load class LQ
+// (both plaintext sides); same contract as seal_class.
 template <int LQ>
-__device__ __forceinline__ uint32_t open_ghash_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c,
-                                                     const Handoff& h, uint32_t tile, uint32_t& j)
+__device__ __forceinline__ bool open_ghash_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c,
+                                                 const Handoff& h, const WalkSlot& ws)
 {
-    constexpr int64_t T = kHornerThreads;
     const uint4* ft = reinterpret_cast<const uint4*>(smem + kOpenFold);
     for (;;) {
         uint4 q;
         {
-            const TileRec tr = c.rec[tile];
-            const uint32_t cta = tr.cta & kTileIndexMask;
-            const BatchItem* it = a.items + tr.item;
-            const uint32_t J = c.st[tr.item].aux[0];
-            const uint32_t G = c.st[tr.item].aux[1];
+            const Cursor cur = walk_cursor(ws);
+            const Segment sg = segment_at(c, cur);
+            *walk_word(ws, 1) = sg.last ? kChunkEnd : cur.k + 1;
+            const BatchItem* it = a.items + sg.item;
             const uint64_t P = it->plen;
-            const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
-            const int64_t span = static_cast<int64_t>(J) * T;
             const uint8_t* frame = it->src;
             int lq;
             uint32_t load_r;
             load_class(frame + 13, lq, load_r);  // lq == LQ for this class
             (void)lq;
-            const OpenTile t{frame, it->capacity, P, n - static_cast<int64_t>(G - cta) * span,
-                             static_cast<int64_t>(J), load_r};
+            const OpenTile t{frame, it->capacity, P, segment_base(sg, P), static_cast<int64_t>(sg.r1 - sg.r0),
+                             load_r};
             q = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), c.tid, c.lane);
         }
+        const bool chunk_done = *walk_word(ws, 1) == kChunkEnd;
         uint32_t taken = 0;
-        if (c.tid == 0) {
-            taken = atomicAdd(&c.hdr->next_tile[0], 1u);
+        if (chunk_done && c.tid == 0) {
+            taken = atomicAdd(&c.hdr->next_chunk[0], 1u);
         }
         const uint4 v = warp_fold_pairs<false>(q, ft, c.lane);
+        const uint32_t j = *walk_word(ws, 2);
         uint32_t next;
         if (!row_handoff(h, j, v, taken, c, next)) {
-            return c.total;
+            return false;
         }
-        ++j;
-        if (next >= c.total || (tile_class(c, next) >> 1) != LQ) {
-            return next;
+        *walk_word(ws, 2) = j + 1;
+        if (chunk_done && !walk_open(c, next, ws)) {
+            return false;
         }
-        tile = next;
+        if ((cursor_class(c, walk_cursor(ws)) >> 1) != LQ) {
+            return true;
+        }
     }
 }
 
 // Power warp of the GHASH pass: E_K(J0), L*H and the basis of H^d while the
 // rows run, then fold levels 4..8 (shared tables), the object's sum and, once
-// its last tile is in, the verdict (auth_ok and the object's slot).
+// its last segment is in, the verdict (auth_ok and the object's slot).
 __device__ __forceinline__ void open_power_loop(const uint8_t* smem, const BatchArgs& a, const BatchCta& c,
-                                                const Handoff& h, uint32_t tile)
+                                                const Handoff& h, uint32_t chunk)
 {
-    constexpr unsigned long long T = kHornerThreads;
     const uint4* t4 = reinterpret_cast<const uint4*>(smem + kOpenFold) + 4 * 512;
-    for (uint32_t j = 0; tile < c.total; ++j) {
-        const TileRec tr = c.rec[tile];
-        const uint32_t cta = tr.cta & kTileIndexMask;
-        Slot* slot = c.st + tr.item;
-        const BatchItem* it = a.items + tr.item;
-        const uint32_t J = slot->aux[0];
+    Cursor cur;
+    bool more = cursor_open(c, chunk, cur);
+    for (uint32_t j = 0; more; ++j) {
+        const Segment sg = segment_at(c, cur);
+        Slot* slot = cta_slots(c) + sg.item;
+        const BatchItem* it = a.items + sg.item;
         const uint32_t G = slot->aux[1];
         const uint64_t P = it->plen;
-        const unsigned long long d = static_cast<unsigned long long>(G - 1 - cta) * J * T + 2ull;
         uint4 ej0, lh;
         unsigned long long uhi, ulo;
-        open_power(it->src, a.kt.aes_t, a.rk, P, d, a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
+        open_power(it->src, a.kt.aes_t, a.rk, P, segment_power(sg), a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
         uint4 v;
         uint32_t next;
         if (!power_take(h, j, c.lane, v, next)) {
@@ -806,7 +947,9 @@ __device__ __forceinline__ void open_power_loop(const uint8_t* smem, const Batch
             *it->auth_ok = ok;
             slot->aux[2] = static_cast<unsigned int>(ok);
         }
-        tile = next;
+        if (cursor_step(cur, sg)) {
+            more = cursor_open(c, next, cur);
+        }
     }
 }
 
@@ -824,79 +967,76 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
         handoff_init(h);
     }
     pdl_wait();  // the plan kernel's workspace
-    auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
-    const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
-                     reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count)), hdr->total_tiles,
-                     tid, tid & 31, tid >> 5};
-    uint32_t tile = first_tile(h.first, c, 0);
+    const BatchCta c = batch_cta(a, h.ctx, tid);
+    const uint32_t chunk = first_chunk(h.first, c, 0);
     if (c.warp == kPowerWarp) {
-        open_power_loop(smem, a, c, h, tile);
+        open_power_loop(smem, a, c, h, chunk);
     } else {
-        uint32_t j = 0;
-        while (tile < c.total) {
-            switch (tile_class(c, tile) >> 1) {  // the GHASH pass does not touch the plaintext side
-            case 0: tile = open_ghash_class<0>(smem, a, c, h, tile, j); break;
-            case 1: tile = open_ghash_class<1>(smem, a, c, h, tile, j); break;
-            case 2: tile = open_ghash_class<2>(smem, a, c, h, tile, j); break;
-            case 3: tile = open_ghash_class<3>(smem, a, c, h, tile, j); break;
-            default: tile = open_ghash_class<4>(smem, a, c, h, tile, j); break;
+        const WalkSlot ws{smem + kOpenBatchWalk};
+        *walk_word(ws, 2) = 0;
+        bool more = walk_open(c, chunk, ws);
+        while (more) {
+            switch (cursor_class(c, walk_cursor(ws)) >> 1) {  // the GHASH pass does not touch the plaintext side
+            case 0: more = open_ghash_class<0>(smem, a, c, h, ws); break;
+            case 1: more = open_ghash_class<1>(smem, a, c, h, ws); break;
+            case 2: more = open_ghash_class<2>(smem, a, c, h, ws); break;
+            case 3: more = open_ghash_class<3>(smem, a, c, h, ws); break;
+            default: more = open_ghash_class<4>(smem, a, c, h, ws); break;
             }
         }
     }
     handoff_failed(h, c);
 }
 
-// Gated CTR over the same tiles (rows of kCtrThreads = kHornerThreads
-// blocks). Each tile reads its object's verdict, written by
-// open_ghash_batch_kernel earlier on the stream: authentic -> decrypt,
-// otherwise zero the tile's plaintext bytes. Thread 0 takes the next index
-// after this tile's rows (a CTA that reserved tiles ahead would hold them
-// while other CTAs sit idle); it goes through a two-entry shared buffer so
-// one barrier per tile suffices.
+// Gated CTR over the same row space (rows of kCtrThreads = kHornerThreads
+// blocks), chunks from a second queue. Each segment reads its object's
+// verdict, written by open_ghash_batch_kernel earlier on the stream:
+// authentic -> decrypt, otherwise zero the segment's plaintext bytes. Thread
+// 0 takes the next chunk after the rows of a chunk's last segment; it goes
+// through a two-entry shared buffer so one barrier per chunk suffices.
 template <int LQ, bool PT>
-__device__ __forceinline__ uint32_t ctr_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, uint32_t tile,
-                                              int cls, uint32_t& round)
+__device__ __forceinline__ bool ctr_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, Cursor& cur,
+                                          int cls, uint32_t& round)
 {
-    static_assert(kCtrThreads == kHornerThreads, "CTR tiles reuse the GHASH tile rows");
-    constexpr int64_t T = kCtrThreads;
+    static_assert(kCtrThreads == kHornerThreads, "CTR segments reuse the GHASH rows");
     volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kCtrBatchMisc);
-    for (;; ++round) {
-        const TileRec tr = c.rec[tile];
-        const uint32_t cta = tr.cta & kTileIndexMask;
-        const BatchItem* it = a.items + tr.item;
-        const Slot& slot = c.st[tr.item];
-        const uint32_t J = slot.aux[0];
-        const uint32_t G = slot.aux[1];
-        const int ok = static_cast<int>(slot.aux[2]);
-        const uint64_t P = it->plen;
-        const int64_t n = static_cast<int64_t>(P / 16u + ((P & 15u) != 0));
-        const int64_t span = static_cast<int64_t>(J) * T;
-        const uint8_t* frame = it->src;
-        int lq;
-        uint32_t load_r;
-        load_class(frame + 13, lq, load_r);  // lq == LQ for this class
-        (void)lq;
-        CtrTile t{frame, it->capacity, it->dst, P, n - static_cast<int64_t>(G - cta) * span,
-                  static_cast<int64_t>(J), {0u, 0u, 0u}, load_r};
-        if (!ok) {
-            ctr_zero_rows<PT>(t, c.tid);
-        } else {
-            const uint4 iv = load_bytes(frame + 1, 12);
-            t.s012[0] = iv.x ^ a.rk[0];
-            t.s012[1] = iv.y ^ a.rk[1];
-            t.s012[2] = iv.z ^ a.rk[2];
-            ctr_rows<LQ, PT>(t, a.rk, c.tid, c.lane);
+    for (;;) {
+        const Segment sg = segment_at(c, cur);
+        {
+            const BatchItem* it = a.items + sg.item;
+            const int ok = static_cast<int>(cta_slots(c)[sg.item].aux[2]);
+            const uint64_t P = it->plen;
+            const uint8_t* frame = it->src;
+            int lq;
+            uint32_t load_r;
+            load_class(frame + 13, lq, load_r);  // lq == LQ for this class
+            (void)lq;
+            CtrTile t{frame, it->capacity, it->dst, P, segment_base(sg, P), static_cast<int64_t>(sg.r1 - sg.r0),
+                      {0u, 0u, 0u}, load_r};
+            if (!ok) {
+                ctr_zero_rows<PT>(t, c.tid);
+            } else {
+                const uint4 iv = load_bytes(frame + 1, 12);
+                t.s012[0] = iv.x ^ a.rk[0];
+                t.s012[1] = iv.y ^ a.rk[1];
+                t.s012[2] = iv.z ^ a.rk[2];
+                ctr_rows<LQ, PT>(t, a.rk, c.tid, c.lane);
+            }
         }
-        if (c.tid == 0) {
-            next_s[round & 1] = atomicAdd(&c.hdr->next_tile[1], 1u);
-        }
-        __syncthreads();
-        const uint32_t next = next_s[round & 1];
-        if (next >= c.total || tile_class(c, next) != cls) {
+        if (cursor_step(cur, sg)) {
+            if (c.tid == 0) {
+                next_s[round & 1] = atomicAdd(&c.hdr->next_chunk[1], 1u);
+            }
+            __syncthreads();
+            const uint32_t next = next_s[round & 1];
             ++round;
-            return next;
+            if (!cursor_open(c, next, cur)) {
+                return false;
+            }
         }
-        tile = next;
+        if (cursor_class(c, cur) != cls) {
+            return true;
+        }
     }
 }
 
@@ -908,36 +1048,35 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const Ba
     fill_aes_smem(smem, a.kt.aes_t);
     small_fill_open_tables(smem, a.kt.gh_pow2);
     pdl_wait();  // the verdicts of the GHASH pass
-    auto* hdr = reinterpret_cast<BatchHeader*>(a.ws);
-    const BatchCta c{hdr, reinterpret_cast<Slot*>(a.ws + batch_slots_offset()),
-                     reinterpret_cast<const TileRec*>(a.ws + batch_tiles_offset(a.count)), hdr->total_tiles,
-                     tid, tid & 31, tid >> 5};
-    uint32_t tile = first_tile(reinterpret_cast<volatile uint32_t*>(smem + kCtrBatchMisc) + 2, c, 1);
+    const BatchCta c = batch_cta(a, smem + kCtrBatchMisc + 16, tid);
+    const uint32_t chunk = first_chunk(reinterpret_cast<volatile uint32_t*>(smem + kCtrBatchMisc) + 2, c, 1);
+    Cursor cur;
+    bool more = cursor_open(c, chunk, cur);
     uint32_t round = 0;  // parity of the shared buffer entry, continued across classes
-    while (tile < c.total) {
-        const int cls = tile_class(c, tile);
+    while (more) {
+        const int cls = cursor_class(c, cur);
         switch (cls) {
-        case 0: tile = ctr_class<0, false>(smem, a, c, tile, cls, round); break;
-        case 1: tile = ctr_class<0, true>(smem, a, c, tile, cls, round); break;
-        case 2: tile = ctr_class<1, false>(smem, a, c, tile, cls, round); break;
-        case 3: tile = ctr_class<1, true>(smem, a, c, tile, cls, round); break;
-        case 4: tile = ctr_class<2, false>(smem, a, c, tile, cls, round); break;
-        case 5: tile = ctr_class<2, true>(smem, a, c, tile, cls, round); break;
-        case 6: tile = ctr_class<3, false>(smem, a, c, tile, cls, round); break;
-        case 7: tile = ctr_class<3, true>(smem, a, c, tile, cls, round); break;
-        case 8: tile = ctr_class<4, false>(smem, a, c, tile, cls, round); break;
-        default: tile = ctr_class<4, true>(smem, a, c, tile, cls, round); break;
+        case 0: more = ctr_class<0, false>(smem, a, c, cur, cls, round); break;
+        case 1: more = ctr_class<0, true>(smem, a, c, cur, cls, round); break;
+        case 2: more = ctr_class<1, false>(smem, a, c, cur, cls, round); break;
+        case 3: more = ctr_class<1, true>(smem, a, c, cur, cls, round); break;
+        case 4: more = ctr_class<2, false>(smem, a, c, cur, cls, round); break;
+        case 5: more = ctr_class<2, true>(smem, a, c, cur, cls, round); break;
+        case 6: more = ctr_class<3, false>(smem, a, c, cur, cls, round); break;
+        case 7: more = ctr_class<3, true>(smem, a, c, cur, cls, round); break;
+        case 8: more = ctr_class<4, false>(smem, a, c, cur, cls, round); break;
+        default: more = ctr_class<4, true>(smem, a, c, cur, cls, round); break;
         }
     }
 
     // Small objects: one warp opens a whole object (GHASH, tag check, CTR),
     // so its plaintext waits for nothing outside the warp.
-    const uint32_t small_count = hdr->small_count;
+    const uint32_t small_count = c.hdr->small_count;
     const uint32_t* small_list = reinterpret_cast<const uint32_t*>(a.ws + batch_small_offset(a.count));
     for (;;) {
         uint32_t k = 0;
         if (c.lane == 0) {
-            k = atomicAdd(&hdr->small_next[1], 1u);
+            k = atomicAdd(&c.hdr->small_next[1], 1u);
         }
         k = __shfl_sync(0xffffffffu, k, 0);
         if (k >= small_count) {

@@ -6,8 +6,8 @@ Each function restates, line for line, one piece of confkv_b200/csrc:
                interior loop;
   grids        horner_grid and the open-CTR rows_per_cta split
                (gpu_aesgcm.cu), which cut one object into tiles;
-  batch plan   batch_plan_kernel (batch.cuh): tile height J*, per-object
-               (J, G) and the tile queue order.
+  batch plan   batch_plan_kernel (batch.cuh): the row space of the tile
+               objects, its chunks and each chunk's segments.
 The interior loops index memory without bounds checks, so these replays are
 their bounds proofs.
 """
@@ -18,12 +18,12 @@ T = 512              # kHornerThreads == kCtrThreads
 SEAL_PAIR = 2        # rows per interior iteration of seal_rows
 OPEN_R = 2           # kOpenChains: rows per interior iteration of open_ghash_rows
 CTR_PAIR = 2
-BATCH_WAVES = 8      # kBatchWaves
 BATCH_MAX_SMS = 256  # kBatchMaxSms
-PLAN_CANDIDATES = 16  # kPlanCandidates
+CHUNKS_PER_SM = 4    # kChunksPerSm
+MIN_CHUNK_ROWS = 64  # kMinChunkRows
+MAX_CHUNKS = CHUNKS_PER_SM * BATCH_MAX_SMS
 SMALL_MAX_BLOCKS = 1024  # kSmallMaxBlocks
-TILE_OVERHEAD_ROWS = 4.0  # kTileOverheadRows
-BATCH_EXTRA = BATCH_WAVES * BATCH_MAX_SMS
+SEGMENT_COST_ROWS = 5    # kSegmentCostRows
 
 
 def cdiv(a, b):
@@ -105,55 +105,84 @@ def tile_base(n, J, G, c):
     return n - (G - c) * J * T
 
 
-def plan_tile_height(rows, sms, count):
-    """Tile height J* of batch_plan_kernel (rows: per object, 0 = invalid)."""
-    R = sum(rows)
-    max_rows = max(rows) if rows else 0
-    cand = []
-    for c in range(PLAN_CANDIDATES):
-        if c < 8:
-            j = cdiv(R, (c + 1) * sms)
-        else:
-            j = cdiv(max_rows, c - 7)
-        j = min(j, max_rows)
-        cand.append(max(1, j))
-    tiles = [sum((1 if r <= J else cdiv(r, J)) for r in rows if r) for J in cand]
-    best, best_est = -1, 0.0
-    for c in range(PLAN_CANDIDATES):
-        t = tiles[c]
-        if t == 0 or t > count + BATCH_EXTRA:
-            continue
-        est = float(cdiv(t, sms)) * (float(R) / float(t) + TILE_OVERHEAD_ROWS)
-        if best < 0 or est < best_est or (est == best_est and cand[c] > cand[best]):
-            best, best_est = c, est
-    return 1 if best < 0 else cand[best]
+def chunk_count(R, sms):
+    """batch_chunk_count: chunks for R rows on `sms` SMs."""
+    if R == 0:
+        return 0
+    per = max(1, min(CHUNKS_PER_SM, R // (sms * MIN_CHUNK_ROWS)))
+    return min(per * sms, R)
 
 
-def batch_plan(lens, sms, valid=None):
-    """batch_plan_kernel: returns (jstar, [(J, G), or None for an invalid or
-    small object, per object], queue) where the queue lists (object, tile) in
-    device order up to the order inside one bucket (the device fills a bucket
-    with atomics)."""
-    count = len(lens)
-    valid = valid if valid is not None else [True] * count
-    rows = []
-    for P, ok in zip(lens, valid):
-        n = cdiv(P, 16)
-        # objects of at most SMALL_MAX_BLOCKS blocks take the warp-per-object
-        # path and get no tiles
-        rows.append(cdiv(n, T) if ok and n > SMALL_MAX_BLOCKS else 0)
+def chunk_row(c, R, M):
+    return c * R // M
+
+
+def chunk_of(x, R, M):
+    return ((x + 1) * M - 1) // R
+
+
+def tile_rows(P, ok=True):
+    """Rows of a tile object (0 for small and invalid objects)."""
+    n = cdiv(P, 16)
+    return cdiv(n, T) if ok and n > SMALL_MAX_BLOCKS else 0
+
+
+def chunk_plan(lens, sms, valid=None, classes=None):
+    """batch_plan_kernel: the row space (tile objects grouped by alignment
+    class; inside a class the device order follows its atomics, here the
+    descriptor order), its chunk count M, the chunks' first rows (cut at
+    equal cost, a tile object weighing its rows plus SEGMENT_COST_ROWS), the
+    first tile object of each chunk and the segment count of each object (0
+    for small and invalid ones)."""
+    valid = valid if valid is not None else [True] * len(lens)
+    classes = classes if classes is not None else [0] * len(lens)
     sms = min(sms, BATCH_MAX_SMS)
-    jstar = plan_tile_height(rows, sms, count)
-    plan = []
-    buckets = {}
-    for i, (P, r) in enumerate(zip(lens, rows)):
-        if r == 0:
-            plan.append(None)
-            continue
-        J = min(r, jstar)
-        n = cdiv(P, 16)
-        G = max(1, cdiv(n, J * T))
-        plan.append((J, G))
-        buckets.setdefault(J.bit_length() - 1, []).extend((i, c) for c in range(G))
-    queue = [t for b in sorted(buckets, reverse=True) for t in buckets[b]]
-    return jstar, plan, queue
+    objs, row = [], 0
+    order = sorted(range(len(lens)), key=lambda i: (classes[i], i))
+    for i in order:
+        rows = tile_rows(lens[i], valid[i])
+        if rows:
+            objs.append((row, i, rows))
+            row += rows
+    R, K = row, len(objs)
+    M = chunk_count(R, sms)
+    o = SEGMENT_COST_ROWS if M and (R + SEGMENT_COST_ROWS * K) // M >= 2 * (SEGMENT_COST_ROWS + 1) else 0
+    C = R + o * K
+    chunk_first = [None] * M
+    chunk_start = [None] * M + [R]
+    segs = [0] * len(lens)
+    for k, (start, i, rows) in enumerate(objs):
+        p = start + o * k
+        first, last = chunk_of(p + o, C, M), chunk_of(p + o + rows - 1, C, M)
+        segs[i] = last - first + 1
+        c = chunk_of(p, C, M)
+        c = c if chunk_row(c, C, M) == p else c + 1
+        for c in range(c, last + 1):
+            assert chunk_first[c] is None
+            x = chunk_row(c, C, M)
+            chunk_first[c] = k
+            chunk_start[c] = start + max(0, x - p - o)
+    return {"R": R, "M": M, "objs": objs, "chunk_first": chunk_first, "chunk_start": chunk_start,
+            "segments": segs}
+
+
+def chunk_segments(plan, chunk):
+    """Segments of one chunk as the work kernels walk them (Cursor,
+    segment_at, cursor_step): (item, rows, r0, r1) each."""
+    objs = plan["objs"]
+    a0, b = plan["chunk_start"][chunk], plan["chunk_start"][chunk + 1]
+    k = plan["chunk_first"][chunk]
+    out = []
+    while True:
+        start, item, rows = objs[k]
+        end = start + rows
+        a = max(a0, start)
+        out.append((item, rows, a - start, min(b, end) - start))
+        if end >= b:
+            return out
+        k += 1
+
+
+def segment_base(P, rows, r0):
+    """First block of a segment starting at row r0 of an object of `rows` rows."""
+    return cdiv(P, 16) - (rows - r0) * T

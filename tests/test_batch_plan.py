@@ -1,15 +1,16 @@
-"""CPU replay of the batched plan and the tile row schedules (batch.cuh,
-tiles.cuh): the tile count stays inside the workspace's record area, tiles
-partition each object, taller tiles come first in the queue, and every
-tile's interior rows meet their loops' preconditions."""
+"""CPU replay of the batched plan and the row schedules (batch.cuh,
+tiles.cuh): the chunks cut the row space into near-equal pieces that fit the
+workspace, walking every chunk's segments covers each tile object's rows
+exactly once with the segment count its slot expects, and every segment's
+interior rows meet their loops' preconditions."""
 
 import math
 
 import numpy as np
 import pytest
 
-from schedules import (BATCH_EXTRA, SMALL_MAX_BLOCKS, T, batch_plan, cdiv, ctr_tile_rows, open_tile_rows,
-                       pad_rows, seal_tile_rows, tile_base)
+from schedules import (MAX_CHUNKS, SEGMENT_COST_ROWS, SMALL_MAX_BLOCKS, T, cdiv, chunk_plan, chunk_segments, ctr_tile_rows,
+                       open_tile_rows, pad_rows, seal_tile_rows, segment_base, tile_base, tile_rows)
 
 
 def _ragged(count, seed, lo=4096, hi=1 << 20):
@@ -27,58 +28,96 @@ BATCHES = {
     "zeros": [0] * 100,
     "tiny_many": list(range(0, 20000, 7)),
     "max_blocks": [16 * 0xFFFFFFFE, 5],
+    "just_above_small": [SMALL_MAX_BLOCKS * 16 + 1] * 7,
 }
+
+
+def _walk(plan):
+    """All chunks' segments in chunk order."""
+    return [seg for c in range(plan["M"]) for seg in chunk_segments(plan, c)]
 
 
 @pytest.mark.parametrize("name", sorted(BATCHES))
 @pytest.mark.parametrize("sms", [148, 132, 1, 300])
-def test_plan_bound_order_and_partition(name, sms):
+@pytest.mark.parametrize("mixed", [False, True])
+def test_chunks_cover_every_row_once(name, sms, mixed):
     lens = BATCHES[name]
-    jstar, plan, queue = batch_plan(lens, sms)
-    assert len(queue) <= len(lens) + BATCH_EXTRA
-    # taller tiles first
-    js = [plan[i][0] for i, _ in queue]
-    assert all((a.bit_length() >= b.bit_length()) for a, b in zip(js, js[1:]))
-    assert len(set(queue)) == len(queue)
+    classes = [(7 * i) % 10 for i in range(len(lens))] if mixed else None
+    plan = chunk_plan(lens, sms, classes=classes)
+    R, M = plan["R"], plan["M"]
+    assert R == sum(tile_rows(P) for P in lens)
+    assert M <= MAX_CHUNKS and M <= R and (M > 0) == (R > 0)
+    # chunks are non-empty and of near-equal cost: rows plus a charge per
+    # segment, within two charges and one row of each other
+    o = SEGMENT_COST_ROWS
+    starts = plan["chunk_start"]
+    assert all(a < b for a, b in zip(starts, starts[1:]))
+    costs = [sum(r1 - r0 for _, _, r0, r1 in chunk_segments(plan, c)) + o * len(chunk_segments(plan, c))
+             for c in range(M)]
+    if M and (R + o * len(plan["objs"])) // M >= 2 * (o + 1):
+        assert max(costs) - min(costs) <= 2 * o + 1
+    segs = _walk(plan)
+    covered = {}
+    count = {}
+    if mixed:
+        # grouped by class: the class changes at most 9 times along the row space
+        cls = [classes[item] for item, _, _, _ in segs]
+        assert sum(a != b for a, b in zip(cls, cls[1:])) <= 9
+    for item, rows, r0, r1 in segs:
+        assert 0 <= r0 < r1 <= rows == tile_rows(lens[item])
+        covered.setdefault(item, []).append((r0, r1))
+        count[item] = count.get(item, 0) + 1
     for i, P in enumerate(lens):
-        n = cdiv(P, 16)
-        if n <= SMALL_MAX_BLOCKS:
-            assert plan[i] is None and all(q[0] != i for q in queue)   # one warp, no tiles
+        rows = tile_rows(P)
+        if rows == 0:
+            assert i not in covered and plan["segments"][i] == 0   # small or empty: one warp, no segments
             continue
-        J, G = plan[i]
-        assert 1 <= J <= jstar and G >= 1
-        assert sum(1 for q in queue if q[0] == i) == G if len(lens) < 200 else True
-        # tiles cover [0, n) exactly once; only tile 0 may start below 0
-        starts = [tile_base(n, J, G, c) for c in range(G)]
-        assert starts[-1] + J * T == n
-        assert all(b >= 0 for b in starts[1:])
-        assert starts[0] > -J * T or n == 0
-        # a one-tile object uses exactly its rows (no wasted rows)
-        if G == 1:
-            assert J == max(1, cdiv(n, T))
+        spans = covered[i]
+        # in order, contiguous, covering [0, rows)
+        assert spans[0][0] == 0 and spans[-1][1] == rows
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        assert count[i] == plan["segments"][i]
 
 
-def test_plan_tile_height():
-    # 32 x 32 MiB: eight equal waves of 111-row tiles (37 per object)
-    jstar, plan, queue = batch_plan([32 << 20] * 32, 148)
-    assert jstar == 111 and len(queue) == 32 * 37 == 8 * 148
-    # one 32 MiB object: one wave
-    jstar, plan, queue = batch_plan([32 << 20], 148)
-    assert len(queue) <= 148 and jstar == 28
-    # 64 x 1 MiB: every object in two tiles -> 128 tiles, one wave
-    jstar, plan, queue = batch_plan([1 << 20] * 64, 148)
-    assert jstar == 64 and len(queue) == 128
-    # 64 x 2 MiB kv_small objects: two tiles each
-    jstar, plan, queue = batch_plan([2 << 20] * 64, 148)
-    assert jstar == 128 and len(queue) == 128
-    # all invalid / empty
-    assert batch_plan([5, 6], 148, valid=[False, False])[0] == 1
+def test_chunk_counts():
+    # 32 x 32 MiB: four chunks per SM of 221-222 rows
+    plan = chunk_plan([32 << 20] * 32, 148)
+    assert plan["R"] == 32 * 4096 and plan["M"] == 4 * 148
+    # 64 x 2 MiB: one chunk per SM (110-111 rows), objects cut across chunks
+    plan = chunk_plan([2 << 20] * 64, 148)
+    assert plan["M"] == 148 and set(plan["segments"]) == {3, 4}
+    # one 32 MiB object: 148 chunks of 27-28 rows, 148 segments
+    plan = chunk_plan([32 << 20], 148)
+    assert plan["M"] == 148 and plan["segments"][0] == 148
+    # fewer rows than SMs: one row per chunk
+    plan = chunk_plan([20000] * 10, 148)   # 3 rows each
+    assert plan["R"] == 30 and plan["M"] == 30
+    # nothing to tile
+    assert chunk_plan([5, 6], 148, valid=[False, False])["M"] == 0
+    assert chunk_plan([], 148)["M"] == 0
 
 
 def test_plan_skips_invalid():
-    lens = [100, 200, 300]
-    jstar, plan, queue = batch_plan(lens, 148, valid=[True, False, True])
-    assert plan[1] is None and all(q[0] != 1 for q in queue)
+    lens = [1 << 20, 2 << 20, 3 << 20]
+    plan = chunk_plan(lens, 148, valid=[True, False, True])
+    assert plan["segments"][1] == 0 and all(seg[0] != 1 for seg in _walk(plan))
+
+
+@pytest.mark.parametrize("name", ["ragged64", "huge_and_tiny", "kv_llama8b_x32", "just_above_small", "max_blocks"])
+def test_segment_rows_meet_loop_preconditions(name):
+    lens = BATCHES[name]
+    plan = chunk_plan(lens, 148)
+    segs = _walk(plan)
+    if len(segs) > 400:
+        segs = segs[:200] + segs[-200:]
+    for item, rows, r0, r1 in segs:
+        P = lens[item]
+        base = segment_base(P, rows, r0)
+        J = r1 - r0
+        _check_tile(base, J, P, 0, seal_tile_rows)
+        _check_tile(base, J, P, 1, lambda b, r, p: seal_tile_rows(b, r, p, pt_aligned=False), hi_margin=1)
+        _check_tile(base, J, P, 1, open_tile_rows)
+        _check_tile(base, J, P, 1, ctr_tile_rows)
 
 
 def _check_tile(base, rows, P, lo_block, sched, hi_margin=0):
