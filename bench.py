@@ -284,21 +284,15 @@ def run_ours(args, rank, world, local):
         achieved = objs_per_launch * (2 * P + 29) / (launch_ms * 1e-3) / 1e9
         prof = profile_summary(f"{kernel}_kv_llama8b.txt")
         traffic = prof.get("dram_bytes_per_launch")
-        # The path is integer/LSU-bound, not HBM-bound. Two further bounds:
-        # (1) the canonical AES+GHASH integer-op count (1162 two-input ops per
-        #     16-B block: bitsliced AES 758 + CTR xor 4 + Karatsuba GHASH 400)
-        #     at the measured LOP3 issue rate of this GPU (64 lanes / SM /
-        #     clock, microbenchmarked) and the clock sampled during the run;
-        # (2) the measured binding unit, the L1 data-pipe wavefront rate (1 per
-        #     SM per clock) at the kernel's wavefronts per block (ncu summary
-        #     under profiles/).
+        # The path is bound by the L1 data pipe, not by HBM: every block costs
+        # a fixed number of shared-memory wavefronts (AES T-table and GHASH
+        # table lookups) and the pipe retires one per SM per clock. The second
+        # roofline is that rate at the kernel's measured wavefronts per block
+        # (ncu summary under profiles/) and the clock sampled during the run.
         wpb = prof.get("wavefronts_per_block", 9.02)
         sm_hz = (clk["sm_mhz"] if clk else 1965.0) * 1e6
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
         seal_gbs_dev = objs_per_launch * P / (launch_ms * 1e-3) / 1e9
-        blocks_per_s = seal_gbs_dev * 1e9 / 16
-        int_peak = 64 * n_sm * sm_hz
-        int_ach = blocks_per_s * 1162
         lsu_ceiling_gbs = n_sm * sm_hz / wpb * 16 / 1e9
         line = {
             "metric": METRIC,
@@ -328,10 +322,6 @@ def run_ours(args, rank, world, local):
                          else "fallback 6.65 TB/s",
                          "algorithmic_bytes_per_launch": objs_per_launch * (2 * P + 29),
                          "traffic": traffic},
-            "int_roofline": {"bound": "int", "kernel": kernel, "ops_per_block": 1162,
-                             "achieved": round(int_ach / 1e12, 3), "peak": round(int_peak / 1e12, 3),
-                             "unit": "Tops/s", "frac": round(int_ach / int_peak, 3),
-                             "peak_source": "measured LOP3 rate 64 lanes/SM/clk x SMs x sampled SM clock"},
             "lsu_roofline": {"bound": "l1_wavefronts", "kernel": kernel, "wavefronts_per_block": wpb,
                              "ceiling_plaintext_gbs": round(lsu_ceiling_gbs, 1),
                              "achieved_plaintext_gbs": round(seal_gbs_dev, 1),
