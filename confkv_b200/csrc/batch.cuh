@@ -39,7 +39,8 @@ namespace confkv {
 namespace dev {
 
 constexpr int kBatchMaxSms = 256;     // SMs the plan spreads chunks over
-constexpr int kChunksPerSm = 4;       // chunks per SM for tall batches (the queue evens out SMs that start late)
+constexpr int kChunksPerSm = 4;       // chunks per SM for batches of many tile objects
+constexpr int kChunksPerSmFew = 2;    // chunks per SM otherwise
 constexpr uint32_t kMinChunkRows = 64;  // fewer chunks per SM while chunks would be shorter than this
 constexpr uint32_t kMaxChunks = static_cast<uint32_t>(kChunksPerSm * kBatchMaxSms);
 constexpr uint32_t kBatchMaxItems = 1u << 20;
@@ -143,16 +144,22 @@ __host__ __device__ __forceinline__ uint32_t chunk_of(unsigned long long x, unsi
     return static_cast<uint32_t>(((x + 1) * M - 1) / R);
 }
 
-// Chunks for R rows on `sms` SMs: kChunksPerSm per SM, fewer while a chunk
-// would be shorter than kMinChunkRows, at least one per SM, never more than
-// R (so no chunk is empty).
-__host__ __device__ __forceinline__ uint32_t batch_chunk_count(unsigned long long R, uint32_t sms)
+// Chunks for R rows of K tile objects on `sms` SMs. With at least
+// kChunksPerSm tile objects per SM the per-object cost estimate is least
+// exact (mixed sizes and alignments) and more chunks let the queue even out
+// the SMs: kChunksPerSm per SM; otherwise kChunksPerSmFew, since every chunk
+// boundary inside an object adds a segment (fold, hand-off, pipeline
+// restart). Fewer while a chunk would be shorter than kMinChunkRows, at
+// least one per SM, never more than R (so no chunk is empty).
+__host__ __device__ __forceinline__ uint32_t batch_chunk_count(unsigned long long R, uint32_t K, uint32_t sms)
 {
     if (R == 0) {
         return 0;
     }
+    const unsigned long long cap =
+        K >= static_cast<unsigned long long>(kChunksPerSm) * sms ? kChunksPerSm : kChunksPerSmFew;
     unsigned long long per = R / (static_cast<unsigned long long>(sms) * kMinChunkRows);
-    per = per < 1 ? 1 : (per > kChunksPerSm ? kChunksPerSm : per);
+    per = per < 1 ? 1 : (per > cap ? cap : per);
     const unsigned long long m = per * sms;
     return static_cast<uint32_t>(m < R ? m : R);
 }
@@ -240,6 +247,39 @@ __device__ __forceinline__ unsigned long long plan_scan(unsigned long long v, un
     return before + incl - v;
 }
 
+// Block-wide inclusive prefix maximum of one value per thread (kPlanThreads
+// threads, all calling); `warp_max` holds kPlanThreads / 32 values.
+__device__ __forceinline__ uint32_t plan_scan_max(uint32_t v, uint32_t* warp_max)
+{
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) {
+            v = u > v ? u : v;
+        }
+    }
+    if (lane == 31) {
+        warp_max[warp] = v;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = warp_max[lane];
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t u = __shfl_up_sync(0xffffffffu, w, d);
+            if (lane >= d) {
+                w = u > w ? u : w;
+            }
+        }
+        warp_max[lane] = w;
+    }
+    __syncthreads();
+    const uint32_t before = warp > 0 ? warp_max[warp - 1] : 0u;
+    return before > v ? before : v;
+}
+
 // `open` selects the descriptor rules: seal needs capacity >= P + 29; open
 // needs frame length >= P + 29 and an auth_ok pointer. sms = SMs the work
 // kernels run on (at most kBatchMaxSms). The row space holds the tile
@@ -257,6 +297,9 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     __shared__ uint32_t chunks_s;
     __shared__ unsigned int small_hist[kSmallBuckets];
     __shared__ unsigned int small_cursor[kSmallBuckets];
+    __shared__ uint32_t chunk_mark[kPlanThreads];
+    __shared__ uint32_t warp_marks[kPlanThreads / 32];
+    static_assert(kMaxChunks <= kPlanThreads, "one plan thread per chunk");
     BatchHeader* hdr = reinterpret_cast<BatchHeader*>(ws);
     Slot* st = reinterpret_cast<Slot*>(ws + batch_slots_offset());
     TileObj* objs = reinterpret_cast<TileObj*>(ws + batch_objs_offset(count));
@@ -273,6 +316,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         class_rows[tid] = 0;
         class_objs[tid] = 0;
     }
+    chunk_mark[tid] = 0;
     __syncthreads();
     pdl_wait();  // descriptors and workspace may belong to earlier work on the stream
 
@@ -327,7 +371,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
             K += class_objs[c];
             R += class_rows[c];
         }
-        const uint32_t M = batch_chunk_count(R, sms);
+        const uint32_t M = batch_chunk_count(R, K, sms);
         total_rows_s = R;
         tile_objs_s = K;
         chunks_s = M;
@@ -406,6 +450,11 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     const unsigned long long C_full = R + o_full * K;
     const unsigned long long o = M != 0 && C_full / M >= 2 * (o_full + 1) ? o_full : 0ull;
     const unsigned long long C = R + o * K;
+    // x_c = c q + floor(c r / M) with q = C / M, r = C mod M (c r < 2^20:
+    // a 32-bit division), so the per-chunk work needs no 64-bit division.
+    const unsigned long long q = M != 0 ? C / M : 0ull;
+    const uint32_t r = M != 0 ? static_cast<uint32_t>(C - q * M) : 0u;
+    auto chunk_cost = [&](uint32_t c) { return c * q + (c * r) / M; };
     for (uint32_t k = lo; k < hi; ++k) {
         const uint32_t rows = objs[k].meta & kRowsMask;
         objs[k].row_start = row;
@@ -413,14 +462,25 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         const uint32_t first = chunk_of(p + o, C, M);
         const uint32_t last = chunk_of(p + o + rows - 1, C, M);
         st[objs[k].item].aux[1] = last - first + 1;
-        // chunks whose first cost falls in [P_k, P_k + o + rows)
+        // the first chunk whose first cost falls in [P_k, P_k + o + rows), if any
         uint32_t c = chunk_of(p, C, M);
-        c = chunk_row(c, C, M) == p ? c : c + 1;
-        for (; c <= last; ++c) {
-            const unsigned long long x = chunk_row(c, C, M);
-            chunks[c] = ChunkRec{row + (x > p + o ? x - p - o : 0ull), k, 0u};
+        c = chunk_cost(c) == p ? c : c + 1;
+        if (c <= last) {
+            chunk_mark[c] = k + 1;
         }
         row += rows;
+    }
+    __syncthreads();
+    // Chunk c's tile object: the last mark at or before c (a prefix max over
+    // the chunks, one thread each); its first row follows from x_c.
+    const uint32_t mark = static_cast<uint32_t>(tid) < M ? chunk_mark[tid] : 0u;
+    const uint32_t owner = plan_scan_max(mark, warp_marks) - 1;
+    if (static_cast<uint32_t>(tid) < M) {
+        const uint32_t c = static_cast<uint32_t>(tid);
+        const unsigned long long start = objs[owner].row_start;
+        const unsigned long long p = start + o * owner;
+        const unsigned long long x = chunk_cost(c);
+        chunks[c] = ChunkRec{start + (x > p + o ? x - p - o : 0ull), owner, 0u};
     }
     if (tid == 0) {
         chunks[M] = ChunkRec{R, K, 0u};

@@ -20,6 +20,7 @@ OPEN_R = 2           # kOpenChains: rows per interior iteration of open_ghash_ro
 CTR_PAIR = 2
 BATCH_MAX_SMS = 256  # kBatchMaxSms
 CHUNKS_PER_SM = 4    # kChunksPerSm
+CHUNKS_PER_SM_FEW = 2  # kChunksPerSmFew
 MIN_CHUNK_ROWS = 64  # kMinChunkRows
 MAX_CHUNKS = CHUNKS_PER_SM * BATCH_MAX_SMS
 SMALL_MAX_BLOCKS = 1024  # kSmallMaxBlocks
@@ -105,11 +106,12 @@ def tile_base(n, J, G, c):
     return n - (G - c) * J * T
 
 
-def chunk_count(R, sms):
-    """batch_chunk_count: chunks for R rows on `sms` SMs."""
+def chunk_count(R, K, sms):
+    """batch_chunk_count: chunks for R rows of K tile objects on `sms` SMs."""
     if R == 0:
         return 0
-    per = max(1, min(CHUNKS_PER_SM, R // (sms * MIN_CHUNK_ROWS)))
+    cap = CHUNKS_PER_SM if K >= CHUNKS_PER_SM * sms else CHUNKS_PER_SM_FEW
+    per = max(1, min(cap, R // (sms * MIN_CHUNK_ROWS)))
     return min(per * sms, R)
 
 
@@ -145,7 +147,7 @@ def chunk_plan(lens, sms, valid=None, classes=None):
             objs.append((row, i, rows))
             row += rows
     R, K = row, len(objs)
-    M = chunk_count(R, sms)
+    M = chunk_count(R, K, sms)
     o = SEGMENT_COST_ROWS if M and (R + SEGMENT_COST_ROWS * K) // M >= 2 * (SEGMENT_COST_ROWS + 1) else 0
     C = R + o * K
     chunk_first = [None] * M

@@ -80,9 +80,11 @@ def test_chunks_cover_every_row_once(name, sms, mixed):
 
 
 def test_chunk_counts():
-    # 32 x 32 MiB: four chunks per SM of 221-222 rows
+    # 32 x 32 MiB (few objects): two chunks per SM of 442-443 rows
     plan = chunk_plan([32 << 20] * 32, 148)
-    assert plan["R"] == 32 * 4096 and plan["M"] == 4 * 148
+    assert plan["R"] == 32 * 4096 and plan["M"] == 2 * 148
+    # 4096 ragged objects (many): four chunks per SM
+    assert chunk_plan(BATCHES["ragged4096"], 148)["M"] == 4 * 148
     # 64 x 2 MiB: one chunk per SM (110-111 rows), objects cut across chunks
     plan = chunk_plan([2 << 20] * 64, 148)
     assert plan["M"] == 148 and set(plan["segments"]) == {3, 4}
