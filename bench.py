@@ -259,7 +259,7 @@ def run_ours(args, rank, world, local):
     # frames, then open -> D2H auth flags; copies overlapped across objects.
     e2e = {"ms": float("nan"), "gbs": float("nan"), "h2d": 0, "d2h": 0} if args.no_e2e else \
         run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args)
-    (e2e_ms,) = multigpu.reduce_max([e2e["ms"]], device=dev)
+    (e2e_ms, copy_ms) = multigpu.reduce_max([e2e["ms"], e2e.get("copy_ms", float("nan"))], device=dev)
 
     if rank == 0:
         head = apis[0]
@@ -330,7 +330,10 @@ def run_ours(args, rank, world, local):
                     round(2 * nobj * P * world / (e2e_ms * 1e-3) / 1e9, 2),
                     "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                     "what": "pinned host plaintext -> H2D -> seal_async -> D2H frames; open_async -> D2H auth; "
-                            "copies overlapped across objects on three streams"},
+                            "copies overlapped across objects on three streams",
+                    "copy_only": round(2 * nobj * P * world / (copy_ms * 1e-3) / 1e9, 2),
+                    "copy_only_what": "the same copies on the same streams with no kernels (host-link bound "
+                                      "of the step, same byte accounting)"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
@@ -389,27 +392,46 @@ def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
         with torch.cuda.stream(s_d2h):
             host_auth.copy_(d_auth, non_blocking=True)
 
+    def copies_only():
+        # the same copies in the same order and streams, no kernels: the
+        # host-link bound of this step
+        for k in range(n):
+            e_in = torch.cuda.Event()
+            with torch.cuda.stream(s_h2d):
+                d_in[k].copy_(host_in[k], non_blocking=True)
+                e_in.record(s_h2d)
+            s_d2h.wait_event(e_in)
+            with torch.cuda.stream(s_d2h):
+                host_frames[k].copy_(d_frames[k], non_blocking=True)
+        with torch.cuda.stream(s_d2h):
+            host_auth.copy_(d_auth, non_blocking=True)
+
+    def timed_steps(fn, steps):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(dev)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(s_h2d)
+        s_cmp.wait_event(t0)
+        s_d2h.wait_event(t0)
+        for _ in range(steps):
+            fn()
+        e_c, e_d = torch.cuda.Event(), torch.cuda.Event()
+        e_c.record(s_cmp)
+        e_d.record(s_d2h)
+        s_h2d.wait_event(e_c)
+        s_h2d.wait_event(e_d)
+        t1.record(s_h2d)
+        torch.cuda.synchronize(dev)
+        return t0.elapsed_time(t1) / steps
+
     steps = max(2, min(args.steps, 5))
-    for _ in range(2):
-        step()
-    torch.cuda.synchronize(dev)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(s_h2d)
-    s_cmp.wait_event(t0)
-    s_d2h.wait_event(t0)
-    for _ in range(steps):
-        step()
-    e_c, e_d = torch.cuda.Event(), torch.cuda.Event()
-    e_c.record(s_cmp)
-    e_d.record(s_d2h)
-    s_h2d.wait_event(e_c)
-    s_h2d.wait_event(e_d)
-    t1.record(s_h2d)
-    torch.cuda.synchronize(dev)
-    ms = t0.elapsed_time(t1) / steps
+    copy_ms = timed_steps(copies_only, steps)
+    ms = timed_steps(step, steps)
     assert bool((host_auth == 1).all())
-    return {"ms": ms, "gbs": 2 * n * P / (ms * 1e-3) / 1e9, "h2d": n * P, "d2h": n * (stride) + 4 * n}
+    return {"ms": ms, "gbs": 2 * n * P / (ms * 1e-3) / 1e9, "h2d": n * P, "d2h": n * (stride) + 4 * n,
+            "copy_ms": copy_ms}
 
 
 # ------------------------------------------------------- CPU (reference)

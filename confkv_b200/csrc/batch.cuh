@@ -487,10 +487,10 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     }
 }
 
-// Final GHASH sum of a tile's object: a one-tile object multiplies its fold
-// by H^2 directly; otherwise the fold goes through the object's slot and only
-// the last tile gets the sum. Power warp only; returns true where (shi, slo)
-// holds the sum.
+// Final GHASH sum of a segment's object: an object in one segment multiplies
+// its fold by H^2 directly; otherwise each segment's share goes through the
+// object's slot and only the last to arrive gets the sum. Power warp only;
+// returns true where (shi, slo) holds the sum.
 __device__ __forceinline__ bool batch_object_sum(Slot* slot, uint32_t G, uint4 fold, unsigned long long uhi,
                                                  unsigned long long ulo, int lane, unsigned long long& shi,
                                                  unsigned long long& slo)
@@ -671,15 +671,15 @@ __device__ __forceinline__ uint32_t first_chunk(volatile uint32_t* next_s, const
 
 // ------------------------------------------------------------- hand-off
 //
-// Seal and open-GHASH CTAs run their tiles as a pipeline: the 16 row warps
-// compute a tile's rows and the first fold stage, hand 32 values to the power
-// warp and go on with the next tile, while the power warp finishes the fold,
-// the object's sum and the tag (seal) or verdict (open). Hand-off j uses
-// buffer j & 1; its FULL mbarrier completes when the 16 row warps arrived,
-// its EMPTY mbarrier when the power warp has read the values, so a buffer is
-// rewritten only after it was read. Both sides walk the same segments: at the
-// end of a chunk thread 0 takes the next chunk index after its rows and
-// passes it along with the values.
+// Seal and open-GHASH CTAs run their segments as a pipeline: the 16 row warps
+// compute a segment's rows and the first fold stage, hand 32 values to the
+// power warp and go on with the next segment, while the power warp finishes
+// the fold, the object's sum and the tag (seal) or verdict (open). Hand-off
+// j uses buffer j & 1; its FULL mbarrier completes when the 16 row warps
+// arrived, its EMPTY mbarrier when the power warp has read the values, so a
+// buffer is rewritten only after it was read. Both sides walk the same
+// segments: at the end of a chunk thread 0 takes the next chunk index after
+// its rows and passes it along with the values.
 
 // Shared-memory views of the hand-off (kHandoffBytes of buffers at part_off,
 // kHandoffSyncBytes of mbarriers and words at sync_off).
@@ -759,7 +759,7 @@ __device__ __forceinline__ bool power_take(const Handoff& h, uint32_t j, int lan
     return true;
 }
 
-// Work-kernel epilogue of the tile phase (all threads): a CTA whose hand-off
+// Work-kernel epilogue of the chunk phase (all threads): a CTA whose hand-off
 // gave up marks the batch as faulted and reports true.
 __device__ __forceinline__ bool handoff_failed(const Handoff& h, const BatchCta& c)
 {

@@ -8,7 +8,7 @@
 // object's end; lane chains q_l = sum_r C H^(32 (rows-1-r)) (the replicated
 // H^32 table), then a 5-level shuffle fold gives sum_l q_l H^(31-l) =
 // sum_i C_i H^(n-1-i), and GHASH = that * H^2 + L * H. Shared memory (the
-// batched seal and open-CTR kernels switch to it after their tiles):
+// batched seal and open-CTR kernels switch to it after their chunks):
 //   [0, 128K)          AES T-tables, replicated per lane
 //   [128K, 192K)       H^32, replicated 4-bit table
 //   [192K, 224K)       compact 4-bit tables of H^8, H^1, H^2, H^4
@@ -20,9 +20,9 @@
 namespace confkv {
 namespace dev {
 
-// Objects up to 16 KiB. Above that, tiles win: a warp's rows are serial, so
-// a batch of fewer larger objects than warps ends on one warp's long chain
-// (64 KiB objects ran at half the tile path's rate).
+// Objects up to 16 KiB. Above that, the row space wins: a warp's rows are
+// serial, so a batch of fewer larger objects than warps ends on one warp's
+// long chain (64 KiB objects ran at half the rate of 512-thread tiles).
 constexpr uint64_t kSmallMaxBlocks = 1024;
 constexpr uint32_t kSmallGh = kAesBytes;
 constexpr uint32_t kSmallFold = kAesBytes + kGhBytes;
