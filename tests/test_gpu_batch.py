@@ -281,3 +281,63 @@ def test_batch_two_hundred_thousand_tiny_objects(gpu_lib, oracle):
             assert auth[i] == 0 and not seg.any(), i
         else:
             assert auth[i] == 1 and np.array_equal(seg, pts[i]), i
+
+
+def _seal_single(k, d_plain, pt_off, d_frames, fr_off, lens, ivs, s):
+    for i in range(len(lens)):
+        k.seal_async(src_ptr=d_plain.data_ptr() + int(pt_off[i]), plaintext_len=int(lens[i]),
+                     dst_ptr=d_frames.data_ptr() + int(fr_off[i]), dst_capacity=int(lens[i]) + 29,
+                     iv=ivs[i], stream_ptr=s.cuda_stream)
+
+
+@pytest.mark.parametrize("lens", [
+    # one large object cut by many chunk boundaries, tile objects of 3 rows, warp-path
+    # objects and an empty one, at odd offsets
+    [(64 << 20) + 7] + [20 * 1024 + 3] * 6 + [4096, 0, (1 << 20) + 1],
+    # fewer rows than SMs: one-row chunks, so every 3-row object is three segments and
+    # the first one holds a single block (1025 blocks = 3 rows, row 0 partial)
+    [16 * 1024 + 16] * 3,
+    [16 * 1024 + 16, 40 * 1024, 16 * 1024 + 1],
+])
+def test_batch_chunk_boundaries_and_gating(gpu_lib, lens):
+    """Segments of one object run on different CTAs: the frames equal
+    seal_async's, and a tampered object is rejected and zero-filled in every
+    segment while its neighbours in the same chunks open."""
+    key = workloads.make_key(21)
+    lens = np.array(lens, dtype=np.int64)
+    ivs = workloads.make_ivs(21, len(lens))
+    pt_off, pt_total = _packed(lens, align=1, pad=3)
+    fr_off, fr_total = _packed(lens + 29, align=1, pad=5)
+    g = torch.Generator(device="cuda").manual_seed(21)
+    d_plain = torch.randint(0, 256, (pt_total + 16,), dtype=torch.uint8, device="cuda", generator=g)
+    d_batch = torch.zeros(fr_total + 16, dtype=torch.uint8, device="cuda")
+    d_single = torch.zeros(fr_total + 16, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    batch = DeviceBatch(gpu_lib, len(lens))
+    with GpuAes128GcmKey(gpu_lib, key) as k:
+        batch.seal(k, _seal_entries(d_plain, pt_off, d_batch, fr_off, lens, ivs), s)
+        _seal_single(k, d_plain, pt_off, d_single, fr_off, lens, ivs, s)
+        s.synchronize()
+        assert int(batch.fault()) == 0
+        assert not batch.statuses().any()
+        assert torch.equal(d_batch, d_single)
+        # tamper the middle of the largest object's ciphertext and the tag of the last one
+        big = int(np.argmax(lens))
+        mid = int(fr_off[big]) + 13 + int(lens[big]) // 2
+        d_batch[mid] ^= 0x10
+        last = len(lens) - 1
+        d_batch[int(fr_off[last]) + 13 + int(lens[last])] ^= 0x01
+        d_out = torch.full((pt_total + 16,), 0xCC, dtype=torch.uint8, device="cuda")
+        d_auth = torch.full((len(lens),), 7, dtype=torch.int32, device="cuda")
+        batch.open(k, _open_entries(d_batch, fr_off, d_out, pt_off, lens, d_auth, range(len(lens))), s)
+        s.synchronize()
+        assert int(batch.fault()) == 0
+    auth = d_auth.cpu().tolist()
+    for i in range(len(lens)):
+        a, n = int(pt_off[i]), int(lens[i])
+        if i in (big, last):
+            assert auth[i] == 0, i
+            assert not d_out[a:a + n].any(), i
+        else:
+            assert auth[i] == 1, i
+            assert torch.equal(d_out[a:a + n], d_plain[a:a + n]), i
