@@ -36,7 +36,7 @@ import statistics
 
 import torch
 
-from . import multigpu, workloads
+from . import hostmem, multigpu, workloads
 from .batch import DeviceBatch
 from .gpu_aesgcm import GpuAes128GcmKey, GpuAesGcmLibrary
 
@@ -115,6 +115,21 @@ class RankWork:
             with torch.cuda.stream(self.stream):
                 g.replay()
         return replay
+
+    def seal_each_to_host(self):
+        """Per-object seal with each frame written straight into pinned host
+        memory (device-mapped, no copy afterwards). Requires
+        hostmem.device_mapped(self.host_ptr())."""
+        base = self.host_ptr()
+        sp = self.stream.cuda_stream
+        for i, (s, d, n, c, iv) in enumerate(self.seal_entries):
+            self.key.seal_async(src_ptr=s, plaintext_len=n, dst_ptr=base + self.fr_off[i], dst_capacity=c, iv=iv,
+                                stream_ptr=sp)
+
+    def host_ptr(self) -> int:
+        if self.host is None:
+            self.host = torch.empty(self.frames.numel(), dtype=torch.uint8, pin_memory=True)
+        return self.host.data_ptr()
 
     def seal_each_d2h(self, side: torch.cuda.Stream):
         """Per-object seal with each frame copied to pinned host memory on
@@ -202,6 +217,18 @@ def measure(work: RankWork, apis, warmup, iters, world, dev, d2h=False) -> list[
         t = timed(lambda: work.seal_each_d2h(side), work.stream, warmup, iters, world, dev)
         out[0]["seal_d2h_gbs"] = round(total / (t["median_ms"] * 1e-3) / 1e9, 2)
         out[0]["seal_d2h_ms_median"] = round(t["median_ms"], 4)
+        # the same frames written by the seal kernel straight into pinned host
+        # memory (checked to be device-mapped on the host first)
+        if hostmem.device_mapped(work.host_ptr()):
+            torch.cuda.synchronize(dev)
+            work.host.fill_(0)
+            t = timed(work.seal_each_to_host, work.stream, warmup, iters, world, dev)
+            torch.cuda.synchronize(dev)
+            same = all(torch.equal(work.host[a:a + n + 29].to(dev), work.frames[a:a + n + 29])
+                       for a, n in zip(work.fr_off, work.lens))
+            out[0]["seal_to_host_gbs"] = round(total / (t["median_ms"] * 1e-3) / 1e9, 2)
+            out[0]["seal_to_host_ms_median"] = round(t["median_ms"], 4)
+            out[0]["seal_to_host_frames_ok"] = bool(multigpu.all_ok(same, device=dev))
     return out
 
 
