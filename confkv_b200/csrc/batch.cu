@@ -2,6 +2,7 @@
 // are in batch.cuh; this translation unit holds their launch, the
 // descriptor checks made on the host and the workspace size.
 #include <cstddef>
+#include <cstdlib>
 #include <cstring>
 
 #include "batch.cuh"
@@ -32,6 +33,18 @@ cudaError_t confkv::host::configure_batch_kernels()
 }
 
 namespace {
+
+// Test-only: CONFKV_B200_TEST_HANDOFF_STALL=1 makes the batched seal's power
+// warps stop taking hand-offs and shortens the hand-off waits to
+// kInjectedWaitNs, so the row warps' waits run out and the call reports a
+// fault in the workspace instead of hanging (tests/test_gpu_batch.py).
+constexpr unsigned long long kInjectedWaitNs = 50ull * 1000ull * 1000ull;
+
+bool handoff_stall_injected()
+{
+    const char* v = std::getenv("CONFKV_B200_TEST_HANDOFF_STALL");
+    return v != nullptr && v[0] == '1';
+}
 
 // Host checks, then: plan (one CTA) -> seal_batch_kernel, or plan ->
 // open_ghash_batch_kernel -> open_ctr_batch_kernel, all with programmatic
@@ -67,6 +80,8 @@ int batch_launch(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* it
     ba.items = d_items;
     ba.ws = ws;
     ba.count = static_cast<uint32_t>(count);
+    ba.stall = handoff_stall_injected() ? 1u : 0u;
+    ba.wait_ns = ba.stall != 0u ? kInjectedWaitNs : dev::kWaitLimitNs;
     std::memcpy(ba.rk, h->rk, sizeof(ba.rk));
     ba.kt = h->kt;
     const uint32_t grid = static_cast<uint32_t>(h->num_sms);

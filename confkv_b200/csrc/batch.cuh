@@ -54,7 +54,7 @@ constexpr int kSmallBuckets = 11;                   // floor(log2 n) of a small 
 // two buffers of 32 partials, and per buffer a FULL mbarrier (the 16 row
 // warps arrived) and an EMPTY one (the power warp took the values).
 constexpr uint32_t kHandoffBytes = 2 * 32 * 16;
-constexpr uint32_t kHandoffSyncBytes = 96;   // mbarriers, queue words, the CTA context
+constexpr uint32_t kHandoffSyncBytes = 96;   // mbarriers, queue words, the CTA context, the wait limit
 constexpr uint32_t kWalkBytes = (kHornerThreads / 32) * 16;  // one WalkSlot per row warp
 // Batched seal shared memory: AES tables, the chain table H^512 (H^32 for
 // small objects), the row-warp fold tables H^8, H^1, H^2, H^4 (the slots the
@@ -168,6 +168,12 @@ struct BatchArgs {
     BatchItem* items;
     uint8_t* ws;
     uint32_t count;
+    // Test-only stall injection (host switch CONFKV_B200_TEST_HANDOFF_STALL):
+    // nonzero makes the seal power warp stop taking hand-offs, so the row
+    // warps' bounded waits run out after wait_ns and the batch reports a
+    // fault. wait_ns is kWaitLimitNs otherwise.
+    uint32_t stall;
+    unsigned long long wait_ns;
     uint32_t rk[44];
     KeyTables kt;
 };
@@ -691,6 +697,7 @@ struct Handoff {
     volatile uint32_t* first;  // first chunk index of the CTA
     volatile uint32_t* abort;  // raised by a wait that gave up
     uint8_t* ctx;              // kCtxBytes for batch_cta
+    volatile unsigned long long* limit_ns;  // the waits' time limit
 };
 
 __device__ __forceinline__ Handoff handoff_at(uint8_t* smem, uint32_t part_off, uint32_t sync_off)
@@ -699,17 +706,20 @@ __device__ __forceinline__ Handoff handoff_at(uint8_t* smem, uint32_t part_off, 
     return Handoff{reinterpret_cast<uint4*>(smem + part_off), reinterpret_cast<uint64_t*>(s),
                    reinterpret_cast<uint64_t*>(s + 16), reinterpret_cast<volatile uint32_t*>(s + 32),
                    reinterpret_cast<volatile uint32_t*>(s + 40), reinterpret_cast<volatile uint32_t*>(s + 44),
-                   s + 48};
+                   s + 48, reinterpret_cast<volatile unsigned long long*>(s + 88)};
 }
 
+static_assert(48 + kCtxBytes <= 88 && 88 + 8 <= kHandoffSyncBytes, "hand-off shared words overlap");
+
 // Thread 0, before the CTA's first barrier.
-__device__ __forceinline__ void handoff_init(const Handoff& h)
+__device__ __forceinline__ void handoff_init(const Handoff& h, unsigned long long wait_ns)
 {
     mbar_init(h.full, kHornerThreads / 32);
     mbar_init(h.full + 1, kHornerThreads / 32);
     mbar_init(h.empty, 1);
     mbar_init(h.empty + 1, 1);
     *h.abort = 0u;
+    *h.limit_ns = wait_ns;
 }
 
 // Row warps, hand-off j: wait until the power warp has read the buffer's
@@ -722,7 +732,7 @@ __device__ __forceinline__ bool row_handoff(const Handoff& h, uint32_t j, uint4 
 {
     const uint32_t b = j & 1u;
     const uint32_t parity = (j >> 1) & 1u;
-    if (!__all_sync(0xffffffffu, mbar_wait(h.empty + b, parity ^ 1u, h.abort))) {
+    if (!__all_sync(0xffffffffu, mbar_wait(h.empty + b, parity ^ 1u, h.abort, h.limit_ns))) {
         return false;
     }
     if (c.lane < 2) {
@@ -735,7 +745,7 @@ __device__ __forceinline__ bool row_handoff(const Handoff& h, uint32_t j, uint4 
     if (c.lane == 0) {
         mbar_arrive(h.full + b);
     }
-    if (!__all_sync(0xffffffffu, mbar_wait(h.full + b, parity, h.abort))) {
+    if (!__all_sync(0xffffffffu, mbar_wait(h.full + b, parity, h.abort, h.limit_ns))) {
         return false;
     }
     next = h.next[b];
@@ -747,7 +757,7 @@ __device__ __forceinline__ bool row_handoff(const Handoff& h, uint32_t j, uint4 
 __device__ __forceinline__ bool power_take(const Handoff& h, uint32_t j, int lane, uint4& v, uint32_t& next)
 {
     const uint32_t b = j & 1u;
-    if (!__all_sync(0xffffffffu, mbar_wait(h.full + b, (j >> 1) & 1u, h.abort))) {
+    if (!__all_sync(0xffffffffu, mbar_wait(h.full + b, (j >> 1) & 1u, h.abort, h.limit_ns))) {
         return false;
     }
     v = h.part[32 * b + lane];
@@ -837,7 +847,7 @@ __device__ __forceinline__ void seal_power_loop(const BatchArgs& a, const BatchC
                                                 uint32_t chunk)
 {
     Cursor cur;
-    bool more = cursor_open(c, chunk, cur);
+    bool more = cursor_open(c, chunk, cur) && a.stall == 0u;
     for (uint32_t j = 0; more; ++j) {
         const Segment sg = segment_at(c, cur);
         Slot* slot = cta_slots(c) + sg.item;
@@ -877,7 +887,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
     fill_small_fold(smem, a.kt.gh_pow2);
     const Handoff h = handoff_at(smem, kSealBatchHandoff, kSealBatchSync);
     if (tid == 0) {
-        handoff_init(h);
+        handoff_init(h, a.wait_ns);
     }
     pdl_wait();  // the plan kernel's workspace
     const BatchCta c = batch_cta(a, h.ctx, tid);
@@ -1024,7 +1034,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
     }
     const Handoff h = handoff_at(smem, kOpenBatchHandoff, kOpenBatchSync);
     if (tid == 0) {
-        handoff_init(h);
+        handoff_init(h, a.wait_ns);
     }
     pdl_wait();  // the plan kernel's workspace
     const BatchCta c = batch_cta(a, h.ctx, tid);

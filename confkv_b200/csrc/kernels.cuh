@@ -190,11 +190,15 @@ __device__ __forceinline__ unsigned long long global_ns()
 
 // Bounded wait for the phase of `bar` with parity `parity`; false when the
 // limit ran out (the caller's thread raises *abort) or *abort was raised.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort)
+// *limit_ns is the time limit (kWaitLimitNs unless a test shortens it); it is
+// read only once the first test has failed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
+                                          const volatile unsigned long long* limit_ns)
 {
     if (mbar_test(bar, parity)) {
         return true;
     }
+    const unsigned long long limit = *limit_ns;
     const unsigned long long t0 = global_ns();
     for (uint32_t polls = 0; polls < kWaitLimitPolls; ++polls) {
         if (mbar_test(bar, parity)) {
@@ -203,7 +207,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         if (*abort != 0u) {
             return false;
         }
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit) {
             break;
         }
     }

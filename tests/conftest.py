@@ -48,6 +48,8 @@ def cpu_lib():
 
 @pytest.fixture(autouse=True)
 def _no_alloc_fault_env():
-    os.environ.pop("CONFKV_B200_FAIL_ALLOC", None)
+    for name in ("CONFKV_B200_FAIL_ALLOC", "CONFKV_B200_TEST_HANDOFF_STALL"):
+        os.environ.pop(name, None)
     yield
-    os.environ.pop("CONFKV_B200_FAIL_ALLOC", None)
+    for name in ("CONFKV_B200_FAIL_ALLOC", "CONFKV_B200_TEST_HANDOFF_STALL"):
+        os.environ.pop(name, None)

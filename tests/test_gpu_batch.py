@@ -341,3 +341,38 @@ def test_batch_chunk_boundaries_and_gating(gpu_lib, lens):
         else:
             assert auth[i] == 1, i
             assert torch.equal(d_out[a:a + n], d_plain[a:a + n]), i
+
+
+def test_batch_handoff_wait_runs_out_without_hanging(gpu_lib, monkeypatch):
+    """Host-side stall injection (CONFKV_B200_TEST_HANDOFF_STALL=1): the seal
+    power warps take no hand-off, so the row warps' bounded waits run out
+    after 50 ms. The call must return with the batch's fault word set, and the
+    next call in the same context must be correct."""
+    import time
+
+    key = workloads.make_key(41)
+    lens = np.array([20 * 1024] * 2000, dtype=np.int64)   # 3-row tile objects: many segments per CTA
+    ivs = workloads.make_ivs(41, len(lens))
+    pt_off, pt_total = _packed(lens, align=16)
+    fr_off, fr_total = _packed(lens + 29, align=16)
+    g = torch.Generator(device="cuda").manual_seed(41)
+    d_plain = torch.randint(0, 256, (pt_total,), dtype=torch.uint8, device="cuda", generator=g)
+    d_batch = torch.zeros(fr_total, dtype=torch.uint8, device="cuda")
+    d_single = torch.zeros(fr_total, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    batch = DeviceBatch(gpu_lib, len(lens))
+    entries = _seal_entries(d_plain, pt_off, d_batch, fr_off, lens, ivs)
+    with GpuAes128GcmKey(gpu_lib, key) as k:
+        monkeypatch.setenv("CONFKV_B200_TEST_HANDOFF_STALL", "1")
+        t0 = time.monotonic()
+        batch.seal(k, entries, s)
+        s.synchronize()
+        elapsed = time.monotonic() - t0
+        assert int(batch.fault()) != 0
+        assert elapsed < 10.0
+        monkeypatch.delenv("CONFKV_B200_TEST_HANDOFF_STALL")
+        batch.seal(k, entries, s)
+        _seal_single(k, d_plain, pt_off, d_single, fr_off, lens, ivs, s)
+        s.synchronize()
+        assert int(batch.fault()) == 0
+        assert torch.equal(d_batch, d_single)
