@@ -344,7 +344,7 @@ def run_ours(args, rank, world, local):
                     round(2 * nobj * P * world / (e2e_ms * 1e-3) / 1e9, 2),
                     "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                     "what": "pinned host plaintext -> H2D -> seal_async -> D2H frames; open_async -> D2H auth; "
-                            "copies overlapped across objects on three streams",
+                            "copies overlapped across objects (streams: H2D, seal, open, D2H)",
                     "copy_only": round(2 * nobj * P * world / (copy_ms * 1e-3) / 1e9, 2),
                     "copy_only_what": "the same copies on the same streams with no kernels (host-link bound "
                                       "of the step, same byte accounting)"},
@@ -375,36 +375,56 @@ def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
     host_in = torch.empty((n, P), dtype=torch.uint8, pin_memory=True)
     host_in.copy_(plain_u8.cpu())
     host_frames = torch.empty((n, stride), dtype=torch.uint8, pin_memory=True)
-    host_auth = torch.empty((n,), dtype=torch.int32, pin_memory=True)
+    host_auth = torch.empty((2, n), dtype=torch.int32, pin_memory=True)
     d_in = torch.empty_like(plain_u8)
-    d_frames = torch.empty((n, stride), dtype=torch.uint8, device=dev)
+    # frames and verdicts alternate between two buffers by step, so a step's
+    # seals never overwrite frames the previous step's opens still read
+    d_frames = torch.empty((2, n, stride), dtype=torch.uint8, device=dev)
     d_out = torch.empty_like(plain_u8)
-    d_auth = torch.zeros((n,), dtype=torch.int32, device=dev)
-    s_h2d, s_cmp, s_d2h = (torch.cuda.Stream(device=dev) for _ in range(3))
+    d_auth = torch.zeros((2, n), dtype=torch.int32, device=dev)
+    s_h2d, s_cmp, s_open, s_d2h = (torch.cuda.Stream(device=dev) for _ in range(4))
     frame_len = P + 29
+    parity = [0]
+    opened = [None, None]   # event after the opens that last used buffer set b
+    sealed = [None] * n     # event after the last seal of object k (it read d_in[k])
 
     def step():
+        b = parity[0]
+        parity[0] ^= 1
+        frames, auth = d_frames[b], d_auth[b]
+        # the opens that last read this buffer set (two steps back) must be
+        # done; the previous step's opens (other set) may still run
+        if opened[b] is not None:
+            s_cmp.wait_event(opened[b])
         for k in range(n):
             e_in = torch.cuda.Event()
+            if sealed[k] is not None:
+                s_h2d.wait_event(sealed[k])
             with torch.cuda.stream(s_h2d):
                 d_in[k].copy_(host_in[k], non_blocking=True)
                 e_in.record(s_h2d)
             s_cmp.wait_event(e_in)
-            key.seal_async(src_ptr=d_in[k].data_ptr(), plaintext_len=P, dst_ptr=d_frames[k].data_ptr(),
+            key.seal_async(src_ptr=d_in[k].data_ptr(), plaintext_len=P, dst_ptr=frames[k].data_ptr(),
                            dst_capacity=stride, iv=ivs[k], stream_ptr=s_cmp.cuda_stream)
             e_seal = torch.cuda.Event()
             e_seal.record(s_cmp)
+            sealed[k] = e_seal
             s_d2h.wait_event(e_seal)
             with torch.cuda.stream(s_d2h):
-                host_frames[k].copy_(d_frames[k], non_blocking=True)
+                host_frames[k].copy_(frames[k], non_blocking=True)
+        # opens on their own stream: the next step's seals need not wait for them
+        e_sealed = torch.cuda.Event()
+        e_sealed.record(s_cmp)
+        s_open.wait_event(e_sealed)
         for k in range(n):
-            key.open_async(src_ptr=d_frames[k].data_ptr(), frame_len=frame_len, dst_ptr=d_out[k].data_ptr(),
-                           plaintext_len=P, auth_ok_ptr=d_auth[k:k + 1].data_ptr(), stream_ptr=s_cmp.cuda_stream)
+            key.open_async(src_ptr=frames[k].data_ptr(), frame_len=frame_len, dst_ptr=d_out[k].data_ptr(),
+                           plaintext_len=P, auth_ok_ptr=auth[k:k + 1].data_ptr(), stream_ptr=s_open.cuda_stream)
         e_open = torch.cuda.Event()
-        e_open.record(s_cmp)
+        e_open.record(s_open)
+        opened[b] = e_open
         s_d2h.wait_event(e_open)
         with torch.cuda.stream(s_d2h):
-            host_auth.copy_(d_auth, non_blocking=True)
+            host_auth[b].copy_(auth, non_blocking=True)
 
     def copies_only():
         # the same copies in the same order and streams, no kernels: the
@@ -416,9 +436,9 @@ def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
                 e_in.record(s_h2d)
             s_d2h.wait_event(e_in)
             with torch.cuda.stream(s_d2h):
-                host_frames[k].copy_(d_frames[k], non_blocking=True)
+                host_frames[k].copy_(d_frames[0, k], non_blocking=True)
         with torch.cuda.stream(s_d2h):
-            host_auth.copy_(d_auth, non_blocking=True)
+            host_auth[0].copy_(d_auth[0], non_blocking=True)
 
     def timed_steps(fn, steps):
         for _ in range(2):
@@ -427,15 +447,14 @@ def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(s_h2d)
-        s_cmp.wait_event(t0)
-        s_d2h.wait_event(t0)
+        for st in (s_cmp, s_open, s_d2h):
+            st.wait_event(t0)
         for _ in range(steps):
             fn()
-        e_c, e_d = torch.cuda.Event(), torch.cuda.Event()
-        e_c.record(s_cmp)
-        e_d.record(s_d2h)
-        s_h2d.wait_event(e_c)
-        s_h2d.wait_event(e_d)
+        for st in (s_cmp, s_open, s_d2h):
+            e = torch.cuda.Event()
+            e.record(st)
+            s_h2d.wait_event(e)
         t1.record(s_h2d)
         torch.cuda.synchronize(dev)
         return t0.elapsed_time(t1) / steps
@@ -443,7 +462,7 @@ def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
     steps = max(2, min(args.steps, 5))
     copy_ms = timed_steps(copies_only, steps)
     ms = timed_steps(step, steps)
-    assert bool((host_auth == 1).all())
+    assert bool((host_auth == 1).all()), "e2e open rejected a frame"
     return {"ms": ms, "gbs": 2 * n * P / (ms * 1e-3) / 1e9, "h2d": n * P, "d2h": n * (stride) + 4 * n,
             "copy_ms": copy_ms}
 
