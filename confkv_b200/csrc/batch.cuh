@@ -29,8 +29,11 @@
 //   [256, ...)          one Slot per object: acc, ticket, aux = {rows, segments, verdict}
 //   [objs_offset, ...)  TileObj per tile object, then a sentinel
 //   [chunks_offset, ...) ChunkRec per chunk (first row, first tile object), then a sentinel
-//   [small_offset, ...) small objects (item indices), largest first
+//   [small_offset, ...) small objects (item indices): kSmallBuckets regions of
+//                       `count` entries, one per size bucket
 #pragma once
+
+#include <cstddef>
 
 #include "small.cuh"
 #include "tiles.cuh"
@@ -48,7 +51,10 @@ constexpr int kPlanThreads = 1024;
 constexpr uint64_t kBatchMaxBlocks = 0xfffffffeull;
 constexpr uint32_t kCtrBatchMisc = kSmallSmem;      // after the small-object tables
 constexpr uint32_t kCtrBatchSmem = kCtrBatchMisc + 64;
-constexpr int kSmallBuckets = 11;                   // floor(log2 n) of a small object, n <= 1024
+// Small objects are handed out largest first, by size bucket: n <= 128,
+// <= 256, <= 512, <= 1024 blocks (up to 2, 4, 8, 16 KiB). Each bucket has its
+// own list region of `count` entries, filled in the plan's first pass.
+constexpr int kSmallBuckets = 4;
 
 // Hand-off from the row warps to the power warp (two-stage fold, tiles.cuh):
 // two buffers of 32 partials, and per buffer a FULL mbarrier (the 16 row
@@ -88,7 +94,8 @@ struct BatchHeader {
     uint32_t small_count;           // objects of at most kSmallMaxBlocks blocks, one warp each
     uint32_t fault;                 // nonzero: a work kernel's hand-off wait gave up (results invalid)
     uint32_t small_next[2];         // small-object queue heads: [0] seal, [1] open
-    uint32_t pad[6];
+    uint32_t small_bucket[4];       // objects per small-object bucket (kSmallBuckets)
+    uint32_t pad[2];
 };
 static_assert(sizeof(BatchHeader) <= 256, "batch header fits its 256-byte area");
 
@@ -130,7 +137,7 @@ __host__ __device__ constexpr size_t batch_small_offset(size_t count)
 }
 __host__ __device__ constexpr size_t batch_workspace_bytes(size_t count)
 {
-    return batch_small_offset(count) + count * sizeof(uint32_t);
+    return batch_small_offset(count) + kSmallBuckets * count * sizeof(uint32_t);
 }
 
 // First row of chunk c and the chunk holding row x (0 <= x < R), for M
@@ -199,18 +206,6 @@ __device__ __forceinline__ void load_class(const uint8_t* ct, int& lq, uint32_t&
     const uint32_t off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(ct) & 15u);
     lq = off == 0 ? 4 : static_cast<int>(off >> 2);
     r = off & 3u;
-}
-
-__device__ __forceinline__ int item_class(const BatchItem& it, int open)
-{
-    int v;
-    uint32_t r;
-    if (open) {
-        load_class(it.src + 13, v, r);
-        return 2 * v + ((reinterpret_cast<uintptr_t>(it.dst) & 15u) == 0);
-    }
-    store_class(it.dst + 13, v, r);
-    return 2 * v + ((reinterpret_cast<uintptr_t>(it.src) & 15u) == 0);
 }
 
 // ------------------------------------------------------------------ plan
@@ -301,8 +296,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     __shared__ unsigned long long total_rows_s;
     __shared__ uint32_t tile_objs_s;
     __shared__ uint32_t chunks_s;
-    __shared__ unsigned int small_hist[kSmallBuckets];
-    __shared__ unsigned int small_cursor[kSmallBuckets];
+    __shared__ unsigned int small_fill[kSmallBuckets];
     __shared__ uint32_t chunk_mark[kPlanThreads];
     __shared__ uint32_t warp_marks[kPlanThreads / 32];
     static_assert(kMaxChunks <= kPlanThreads, "one plan thread per chunk");
@@ -316,7 +310,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     constexpr uint64_t T = kHornerThreads;
     pdl_release();
     if (tid < kSmallBuckets) {
-        small_hist[tid] = 0;
+        small_fill[tid] = 0;
     }
     if (tid < kClasses) {
         class_rows[tid] = 0;
@@ -328,25 +322,61 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
 
     // Pass 1: validate, rows per tile object (small and invalid objects have
     // none), reset the slot (aux[1] keeps the class until pass 3), the
-    // small-object histogram and the per-class totals (one shared atomic per
-    // class present in a warp).
+    // per-class totals, and the small objects into their bucket's list (one
+    // shared atomic per class or bucket present in a warp).
+    static_assert(offsetof(BatchItem, dst) == 8 && offsetof(BatchItem, plen) == 16 &&
+                      offsetof(BatchItem, capacity) == 24 && offsetof(BatchItem, auth_ok) == 32,
+                  "pass 1 decodes the descriptor's first 48 bytes");
+    // The fields pass 1 reads (the first 48 bytes of a descriptor) are
+    // loaded one iteration ahead, so the loop pays one memory latency in all
+    // rather than one per iteration.
+    auto fetch = [&](uint32_t i, uint4 (&d)[3]) {
+        if (i < count) {
+            const uint4* q = reinterpret_cast<const uint4*>(items + i);
+            d[0] = q[0];
+            d[1] = q[1];
+            d[2] = q[2];
+        }
+    };
+    uint4 cur[3];
+    fetch(static_cast<uint32_t>(tid), cur);
     for (uint32_t base = 0; base < count; base += kPlanThreads) {
         const uint32_t i = base + static_cast<uint32_t>(tid);
-        int key = -1;
+        uint4 nxt[3];
+        fetch(i + kPlanThreads, nxt);
+        int key = -1;   // alignment class of a tile object
+        int skey = -1;  // size bucket of a small object
         uint32_t rows = 0;
         if (i < count) {
-            BatchItem& it = items[i];
-            const uint64_t P = it.plen;
+            // {src, dst}, {plen, capacity}, {auth_ok, iv[0..1]}
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(
+                (static_cast<unsigned long long>(cur[0].y) << 32) | cur[0].x);
+            const uint8_t* dst = reinterpret_cast<const uint8_t*>(
+                (static_cast<unsigned long long>(cur[0].w) << 32) | cur[0].z);
+            const uint64_t P = (static_cast<uint64_t>(cur[1].y) << 32) | cur[1].x;
+            const uint64_t capacity = (static_cast<uint64_t>(cur[1].w) << 32) | cur[1].z;
+            const bool has_auth = (cur[2].x | cur[2].y) != 0u;
             const uint64_t n = P / 16u + ((P & 15u) != 0);
-            bool ok = it.src != nullptr && it.dst != nullptr && n <= kBatchMaxBlocks && it.capacity >= P + 29u;
+            bool ok = src != nullptr && dst != nullptr && n <= kBatchMaxBlocks && capacity >= P + 29u;
             if (open) {
-                ok = ok && it.auth_ok != nullptr;
+                ok = ok && has_auth;
             }
             const bool small = ok && n <= kSmallMaxBlocks;
             rows = ok && !small ? static_cast<uint32_t>((n + T - 1) / T) : 0u;
-            it.status = ok ? 0 : -1;
+            items[i].status = ok ? 0 : -1;
             if (rows != 0) {
-                key = item_class(it, open);
+                int v;
+                uint32_t r;
+                if (open) {
+                    load_class(src + 13, v, r);
+                    key = 2 * v + ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+                } else {
+                    store_class(dst + 13, v, r);
+                    key = 2 * v + ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+                }
+            }
+            if (small) {
+                skey = n <= 128 ? 0 : (n <= 256 ? 1 : (n <= 512 ? 2 : 3));
             }
             Slot& s = st[i];
             s.acc_hi = 0;
@@ -355,17 +385,26 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
             s.aux[0] = rows;
             s.aux[1] = static_cast<uint32_t>(key);
             s.aux[2] = 0;
-            if (small) {
-                const int b = 31 - __clz(static_cast<int>(n | 1u));
-                s.aux[2] = static_cast<uint32_t>(b + 1);
-                atomicAdd(&small_hist[b], 1u);
-            }
         }
         const unsigned peers = __match_any_sync(0xffffffffu, key);
         const unsigned sum = __reduce_add_sync(peers, rows);  // at most 32 x 2^23
         if (key >= 0 && lane == __ffs(peers) - 1) {
             atomicAdd(&class_rows[key], static_cast<unsigned long long>(sum));
             atomicAdd(&class_objs[key], static_cast<unsigned>(__popc(peers)));
+        }
+        const unsigned speers = __match_any_sync(0xffffffffu, skey);
+        if (skey >= 0) {
+            const int leader = __ffs(speers) - 1;
+            unsigned pos = 0;
+            if (lane == leader) {
+                pos = atomicAdd(&small_fill[skey], static_cast<unsigned>(__popc(speers)));
+            }
+            pos = __shfl_sync(speers, pos, leader) + static_cast<unsigned>(__popc(speers & ((1u << lane) - 1u)));
+            small_list[static_cast<size_t>(skey) * count + pos] = i;
+        }
+#pragma unroll
+        for (int w = 0; w < 3; ++w) {
+            cur[w] = nxt[w];
         }
     }
     __syncthreads();
@@ -389,32 +428,44 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         hdr->fault = 0;
         objs[K] = TileObj{R, 0xffffffffu, 0u};
     } else if (tid == 32) {
-        // small objects: largest bucket first
-        unsigned int pos = 0;
-        for (int b = kSmallBuckets - 1; b >= 0; --b) {
-            small_cursor[b] = pos;
-            pos += small_hist[b];
+        unsigned int total = 0;
+        for (int b = 0; b < kSmallBuckets; ++b) {
+            hdr->small_bucket[b] = small_fill[b];
+            total += small_fill[b];
         }
-        hdr->small_count = pos;
+        hdr->small_count = total;
         hdr->small_next[0] = 0;
         hdr->small_next[1] = 0;
     }
     __syncthreads();
+    if (tile_objs_s == 0) {
+        return;  // small objects only: nothing to place
+    }
 
-    // Pass 2: place the tile objects, class by class; the small-object list.
+    // Pass 2: place the tile objects, class by class (each slot's rows and
+    // class loaded one iteration ahead, as in pass 1).
+    auto fetch_slot = [&](uint32_t i, uint32_t& rows, uint32_t& cls) {
+        if (i < count) {
+            rows = st[i].aux[0];
+            cls = st[i].aux[1];
+        }
+    };
+    uint32_t cur_rows = 0, cur_cls = 0;
+    fetch_slot(static_cast<uint32_t>(tid), cur_rows, cur_cls);
     for (uint32_t base = 0; base < count; base += kPlanThreads) {
         const uint32_t i = base + static_cast<uint32_t>(tid);
+        uint32_t next_rows = 0, next_cls = 0;
+        fetch_slot(i + kPlanThreads, next_rows, next_cls);
         int key = -1;
         uint32_t rows = 0;
         if (i < count) {
-            const Slot& s = st[i];
-            rows = s.aux[0];
+            rows = cur_rows;
             if (rows != 0) {
-                key = static_cast<int>(s.aux[1]);
-            } else if (s.aux[2] != 0) {
-                small_list[atomicAdd(&small_cursor[s.aux[2] - 1], 1u)] = i;
+                key = static_cast<int>(cur_cls);
             }
         }
+        cur_rows = next_rows;
+        cur_cls = next_cls;
         const unsigned peers = __match_any_sync(0xffffffffu, key);
         if (key >= 0) {
             const int leader = __ffs(peers) - 1;
@@ -783,6 +834,23 @@ __device__ __forceinline__ bool handoff_failed(const Handoff& h, const BatchCta&
     return true;
 }
 
+// Item index of the small object at queue position k: the buckets are handed
+// out largest first (bucket kSmallBuckets - 1 down to 0), each from its own
+// list region of `count` entries.
+__device__ __forceinline__ uint32_t small_item(const BatchArgs& a, const BatchHeader* hdr, uint32_t k)
+{
+    const uint32_t* lists = reinterpret_cast<const uint32_t*>(a.ws + batch_small_offset(a.count));
+    int b = kSmallBuckets - 1;
+    for (; b > 0; --b) {
+        const uint32_t n = hdr->small_bucket[b];
+        if (k < n) {
+            break;
+        }
+        k -= n;
+    }
+    return lists[static_cast<size_t>(b) * a.count + k];
+}
+
 // ------------------------------------------------------------------ seal
 
 // Row warps: segments of one alignment class from the cursor on; returns
@@ -926,7 +994,6 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
     }
     fill_gh_smem(smem + kSmallGh, a.kt.gh_pow2 + 5 * 512);
     __syncthreads();
-    const uint32_t* small_list = reinterpret_cast<const uint32_t*>(a.ws + batch_small_offset(a.count));
     for (;;) {
         uint32_t k = 0;
         if (c.lane == 0) {
@@ -936,7 +1003,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
         if (k >= small_count) {
             break;
         }
-        seal_object_warp(a.items + small_list[k], a.rk, a.kt.gh_pow2, smem, c.lane);
+        seal_object_warp(a.items + small_item(a, c.hdr, k), a.rk, a.kt.gh_pow2, smem, c.lane);
     }
 }
 
@@ -1142,7 +1209,6 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const Ba
     // Small objects: one warp opens a whole object (GHASH, tag check, CTR),
     // so its plaintext waits for nothing outside the warp.
     const uint32_t small_count = c.hdr->small_count;
-    const uint32_t* small_list = reinterpret_cast<const uint32_t*>(a.ws + batch_small_offset(a.count));
     for (;;) {
         uint32_t k = 0;
         if (c.lane == 0) {
@@ -1152,7 +1218,7 @@ __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const Ba
         if (k >= small_count) {
             break;
         }
-        open_object_warp(a.items + small_list[k], a.rk, a.kt.gh_pow2, smem, c.lane);
+        open_object_warp(a.items + small_item(a, c.hdr, k), a.rk, a.kt.gh_pow2, smem, c.lane);
     }
 }
 

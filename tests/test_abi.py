@@ -132,11 +132,11 @@ def test_batch_workspace_size(cpu_lib):
     ws = cpu_lib.batch_workspace_size
     # header 256 B, one 32-B slot per object (rounded to 256 B), a 16-B
     # tile-object record per object plus a sentinel (rounded to 256 B), a
-    # 16-B record for each of at most 1024 chunks plus a sentinel, a 4-B
-    # small-object list entry per object
+    # 16-B record for each of at most 1024 chunks plus a sentinel, and four
+    # small-object list regions (one per size bucket) of a 4-B entry per object
     r256 = lambda x: (x + 255) // 256 * 256
     for count in (1, 7, 8, 9, 4096, 1 << 20):
-        assert ws(count) == 256 + r256(count * 32) + r256((count + 1) * 16) + 1025 * 16 + count * 4
+        assert ws(count) == 256 + r256(count * 32) + r256((count + 1) * 16) + 1025 * 16 + 4 * count * 4
     assert ws((1 << 20) + 1) == 0
 
 
