@@ -12,12 +12,11 @@
 // is combined through the object's slot, the last segment writing the tag
 // or verdict.
 //
-//   batch_plan_kernel    one CTA: validates every descriptor (status), lays
-//                        out the row space (tile objects grouped by
-//                        alignment class), picks M, counts each object's
-//                        segments and records the tile object holding each
-//                        chunk's first row; small objects go to a list,
-//                        largest first.
+//   batch_plan_kernel    one CTA: validates every descriptor (status), puts
+//                        small objects into size-bucket lists, lays out the
+//                        row space (tile objects grouped by alignment
+//                        class), picks M, counts each object's segments and
+//                        records each chunk's first row and tile object.
 //   seal_batch_kernel    one CTA per SM; each takes chunks from a queue
 //   open_ghash_batch_    (atomic head) and walks their segments. No CTA waits
 //   kernel               for another. After the chunks, small objects, one
