@@ -17,7 +17,7 @@ namespace host {
 
 constexpr size_t kFrameOverhead = 29;
 constexpr uint64_t kMaxBlocks = 0xfffffffeull;
-constexpr int kSlots = 64;
+constexpr int kSlots = 1024;  // per-call accumulation slots of a key handle (a ring)
 constexpr int kMaxDevices = 64;
 
 struct KeyHandle {

@@ -53,8 +53,9 @@ int lmcache_gpu_aes128gcm_key_destroy(lmcache_gpu_aesgcm_key_t key);
 /*
  * Pre-size per-call workspace for objects up to max_plaintext_len bytes
  * (reference gpu_aesgcm_api.h:35-44). The workspace here is a fixed-size
- * per-handle ring that key_create already allocates, so this only validates
- * the handle and the size limit; seal/open never call cudaMalloc.
+ * per-handle ring (1024 accumulation slots) that key_create already
+ * allocates, so this only validates the handle and the size limit;
+ * seal/open never call cudaMalloc.
  */
 int lmcache_gpu_aes128gcm_reserve(lmcache_gpu_aesgcm_key_t key, size_t max_plaintext_len);
 
@@ -65,6 +66,12 @@ int lmcache_gpu_aes128gcm_reserve(lmcache_gpu_aesgcm_key_t key, size_t max_plain
  * cudaStream_t cast to void* (null = legacy default stream).
  * dst_capacity < P + 29 or more than 2^32 - 2 blocks -> ERR_ARGUMENT.
  * rc reports only enqueue errors; the caller synchronises.
+ *
+ * Concurrency (lifts the reference's one-stream-per-handle rule): several
+ * streams and host threads may use one handle at once. Each seal/open call
+ * takes the next entry of the handle's 1024-entry ring of accumulation
+ * slots, so at most 1024 calls may be outstanding across different streams
+ * at a time; calls on one stream are ordered and never collide.
  */
 int lmcache_gpu_aes128gcm_seal_async(lmcache_gpu_aesgcm_key_t key, const void* src,
                                      size_t plaintext_len, void* dst, size_t dst_capacity,
