@@ -1,9 +1,10 @@
 // Batched seal / open: one plan launch and one (seal) or two (open)
 // persistent launches for any number of objects of any sizes and alignments.
 //
-// Objects of more than kSmallMaxBlocks blocks ("tile objects") are cut into
-// rows of kHornerThreads blocks, aligned to the object's end (only row 0 can
-// start before block 0). The batch's rows form one row space, tile objects
+// Objects of more than kSmallMaxBlocks blocks ("tile objects"; mid objects
+// of up to kWarpMaxBlocks blocks only when the batch has too few of them for
+// the warp path) are cut into rows of kHornerThreads blocks, aligned to the
+// object's end (only row 0 can start before block 0). The batch's rows form one row space, tile objects
 // back to back, which is cut into M chunks of equal estimated cost (rows
 // plus a fixed charge per tile object). As in stream-K, a chunk may end
 // inside one object and start inside another, so every SM gets the same
@@ -13,7 +14,8 @@
 // or verdict.
 //
 //   batch_plan_kernel    one CTA: validates every descriptor (status), puts
-//                        small objects into size-bucket lists, lays out the
+//                        small objects into size-bucket lists, routes the
+//                        mid objects to warps or to rows, lays out the
 //                        row space (tile objects grouped by alignment
 //                        class), picks M, counts each object's segments and
 //                        records each chunk's first row and tile object.
@@ -51,9 +53,27 @@ constexpr uint64_t kBatchMaxBlocks = 0xfffffffeull;
 constexpr uint32_t kCtrBatchMisc = kSmallSmem;      // after the small-object tables
 constexpr uint32_t kCtrBatchSmem = kCtrBatchMisc + 64;
 // Small objects are handed out largest first, by size bucket: n <= 128,
-// <= 256, <= 512, <= 1024 blocks (up to 2, 4, 8, 16 KiB). Each bucket has its
-// own list region of `count` entries, filled in the plan's first pass.
-constexpr int kSmallBuckets = 4;
+// <= 256, <= 512, <= 1024 blocks (up to 2, 4, 8, 16 KiB), and bucket 4 for
+// the mid objects (1025 .. kWarpMaxBlocks blocks, up to 32 KiB) when they take
+// the warp path. Each bucket has its own list region of `count` entries,
+// filled in the plan's first pass.
+constexpr int kSmallBuckets = 5;
+// Mid objects take one warp each when the batch's N warp-path objects
+// (small + mid) are enough for the warps to beat the tile path:
+//   N (rows_avg + o) 512 >= alpha max_n sms,
+// rows_avg + o being a mid object's mean cost as a tile object (rows plus
+// the segment charge) and max_n its largest size in blocks. A warp's
+// throughput is about fixed, so warp-path throughput grows with N; a tile
+// object's cost grows with its rows plus o, a warp's time with n. alpha
+// comes from measured crossovers on B200 (32 KiB objects: seal at 11.5, open
+// at 8.4 objects per SM; 20 KiB: about 8 and under 7): 2048 objects of
+// 32 KiB ran 298 / 313 GB/s (seal / open) as warps against 249 / 200 as
+// tiles, 1480 of them 218 / 238 against 254 / 201. With fewer objects, one
+// warp's serial rows (up to 64) would end the call late, and they stay tile
+// objects like the larger ones.
+constexpr uint32_t kMidAlphaSeal = 26;
+constexpr uint32_t kMidAlphaOpen = 19;
+constexpr uint32_t kMidFlag = 0x80000000u;  // aux[0] of a mid object until the plan routes it
 
 // Hand-off from the row warps to the power warp (two-stage fold, tiles.cuh):
 // two buffers of 32 partials, and per buffer a FULL mbarrier (the 16 row
@@ -90,11 +110,11 @@ struct BatchHeader {
     uint32_t chunks;                // M (0 when there are no tile objects)
     uint32_t next_chunk[2];         // queue heads: [0] seal / open GHASH, [1] open CTR
     uint32_t tile_objects;          // K
-    uint32_t small_count;           // objects of at most kSmallMaxBlocks blocks, one warp each
+    uint32_t small_count;           // warp-path objects (small, and mid when routed), one warp each
     uint32_t fault;                 // nonzero: a work kernel's hand-off wait gave up (results invalid)
     uint32_t small_next[2];         // small-object queue heads: [0] seal, [1] open
-    uint32_t small_bucket[4];       // objects per small-object bucket (kSmallBuckets)
-    uint32_t pad[2];
+    uint32_t small_bucket[5];       // objects per small-object bucket (kSmallBuckets)
+    uint32_t pad[1];
 };
 static_assert(sizeof(BatchHeader) <= 256, "batch header fits its 256-byte area");
 
@@ -292,6 +312,10 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     __shared__ unsigned long long class_rows[kClasses];
     __shared__ unsigned int class_objs[kClasses];
     __shared__ unsigned int class_cursor[kClasses];
+    __shared__ unsigned long long mid_rows[kClasses];
+    __shared__ unsigned int mid_objs[kClasses];
+    __shared__ uint32_t route_mid;
+    __shared__ unsigned int mid_max_n;
     __shared__ unsigned long long total_rows_s;
     __shared__ uint32_t tile_objs_s;
     __shared__ uint32_t chunks_s;
@@ -314,6 +338,11 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     if (tid < kClasses) {
         class_rows[tid] = 0;
         class_objs[tid] = 0;
+        mid_rows[tid] = 0;
+        mid_objs[tid] = 0;
+    }
+    if (tid == 0) {
+        mid_max_n = 0;
     }
     chunk_mark[tid] = 0;
     __syncthreads();
@@ -344,8 +373,10 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         uint4 nxt[3];
         fetch(i + kPlanThreads, nxt);
         int key = -1;   // alignment class of a tile object
-        int skey = -1;  // size bucket of a small object
+        int mkey = -1;  // alignment class of a mid object
+        int skey = -1;  // size bucket of a small or mid object
         uint32_t rows = 0;
+        uint32_t mid_n = 0;
         if (i < count) {
             // {src, dst}, {plen, capacity}, {auth_ok, iv[0..1]}
             const uint8_t* src = reinterpret_cast<const uint8_t*>(
@@ -374,22 +405,40 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
                     key = 2 * v + ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
                 }
             }
+            const bool mid = rows != 0 && n <= kWarpMaxBlocks;
             if (small) {
                 skey = n <= 128 ? 0 : (n <= 256 ? 1 : (n <= 512 ? 2 : 3));
+            } else if (mid) {
+                // listed for the warp path and counted apart until the plan
+                // knows how many warp-path objects there are
+                skey = 4;
+                mkey = key;
+                key = -1;
+                mid_n = static_cast<uint32_t>(n);
             }
             Slot& s = st[i];
             s.acc_hi = 0;
             s.acc_lo = 0;
             s.ticket = 0;
-            s.aux[0] = rows;
-            s.aux[1] = static_cast<uint32_t>(key);
+            s.aux[0] = mid ? (rows | kMidFlag) : rows;
+            s.aux[1] = static_cast<uint32_t>(mid ? mkey : key);
             s.aux[2] = 0;
         }
         const unsigned peers = __match_any_sync(0xffffffffu, key);
-        const unsigned sum = __reduce_add_sync(peers, rows);  // at most 32 x 2^23
+        const unsigned sum = __reduce_add_sync(peers, key >= 0 ? rows : 0u);  // at most 32 x 2^23
         if (key >= 0 && lane == __ffs(peers) - 1) {
             atomicAdd(&class_rows[key], static_cast<unsigned long long>(sum));
             atomicAdd(&class_objs[key], static_cast<unsigned>(__popc(peers)));
+        }
+        const unsigned warp_max_n = __reduce_max_sync(0xffffffffu, mid_n);
+        if (lane == 0 && warp_max_n != 0) {
+            atomicMax(&mid_max_n, warp_max_n);
+        }
+        const unsigned mpeers = __match_any_sync(0xffffffffu, mkey);
+        const unsigned msum = __reduce_add_sync(mpeers, mkey >= 0 ? rows : 0u);
+        if (mkey >= 0 && lane == __ffs(mpeers) - 1) {
+            atomicAdd(&mid_rows[mkey], static_cast<unsigned long long>(msum));
+            atomicAdd(&mid_objs[mkey], static_cast<unsigned>(__popc(mpeers)));
         }
         const unsigned speers = __match_any_sync(0xffffffffu, skey);
         if (skey >= 0) {
@@ -408,12 +457,27 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     }
     __syncthreads();
     if (tid == 0) {
+        // mid objects take the warp path when there are enough warp-path
+        // objects to beat their cost as tile objects
+        unsigned long long warp_objs = 0;
+        for (int b = 0; b < kSmallBuckets; ++b) {
+            warp_objs += small_fill[b];
+        }
+        unsigned long long mid_cost = 0;  // sum of (rows + o) over mid objects
+        for (int c = 0; c < kClasses; ++c) {
+            mid_cost += mid_rows[c] + static_cast<unsigned long long>(kSegmentCostRows) * mid_objs[c];
+        }
+        const unsigned long long mids = small_fill[4];
+        const unsigned long long alpha = open ? kMidAlphaOpen : kMidAlphaSeal;
+        const uint32_t route =
+            mids != 0 && warp_objs * mid_cost * kHornerThreads >= alpha * mid_max_n * sms * mids ? 1u : 0u;
+        route_mid = route;
         unsigned long long R = 0;
         uint32_t K = 0;
         for (int c = 0; c < kClasses; ++c) {
             class_cursor[c] = K;
-            K += class_objs[c];
-            R += class_rows[c];
+            K += class_objs[c] + (route ? 0u : mid_objs[c]);
+            R += class_rows[c] + (route ? 0ull : mid_rows[c]);
         }
         const uint32_t M = batch_chunk_count(R, K, sms);
         total_rows_s = R;
@@ -426,17 +490,19 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         hdr->tile_objects = K;
         hdr->fault = 0;
         objs[K] = TileObj{R, 0xffffffffu, 0u};
-    } else if (tid == 32) {
+    }
+    __syncthreads();
+    if (tid == 32) {
         unsigned int total = 0;
         for (int b = 0; b < kSmallBuckets; ++b) {
-            hdr->small_bucket[b] = small_fill[b];
-            total += small_fill[b];
+            const unsigned int nb = b == 4 && !route_mid ? 0u : small_fill[b];
+            hdr->small_bucket[b] = nb;
+            total += nb;
         }
         hdr->small_count = total;
         hdr->small_next[0] = 0;
         hdr->small_next[1] = 0;
     }
-    __syncthreads();
     if (tile_objs_s == 0) {
         return;  // small objects only: nothing to place
     }
@@ -458,7 +524,15 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         int key = -1;
         uint32_t rows = 0;
         if (i < count) {
-            rows = cur_rows;
+            rows = cur_rows & ~kMidFlag;
+            if ((cur_rows & kMidFlag) != 0u) {
+                // a mid object: a tile object unless it took the warp path
+                if (route_mid) {
+                    rows = 0;
+                } else {
+                    st[i].aux[0] = rows;
+                }
+            }
             if (rows != 0) {
                 key = static_cast<int>(cur_cls);
             }

@@ -1,4 +1,5 @@
-// Small objects (at most kSmallMaxBlocks 16-byte blocks) in batched calls:
+// Small objects (at most kSmallMaxBlocks 16-byte blocks, or kWarpMaxBlocks
+// when the batch plan routes mid objects here) in batched calls:
 // one warp seals or opens a whole object, so a small object costs no
 // block-wide fold, no barrier and no atomics, and many of them run side by
 // side on every SM.
@@ -20,10 +21,15 @@
 namespace confkv {
 namespace dev {
 
-// Objects up to 16 KiB. Above that, the row space wins: a warp's rows are
-// serial, so a batch of fewer larger objects than warps ends on one warp's
-// long chain (64 KiB objects ran at half the rate of 512-thread tiles).
+// Objects up to 16 KiB always. A warp's rows are serial, so a batch of fewer
+// larger objects than warps ends on one warp's long chain (64 KiB objects ran
+// at half the rate of 512-thread tiles).
 constexpr uint64_t kSmallMaxBlocks = 1024;
+// Objects of kSmallMaxBlocks + 1 .. kWarpMaxBlocks blocks ("mid" objects,
+// up to 32 KiB) take the same warp path when the batch has enough of them
+// (the batch plan decides, kMidAlphaSeal / kMidAlphaOpen); the warp code
+// handles any length.
+constexpr uint64_t kWarpMaxBlocks = 2048;
 constexpr uint32_t kSmallGh = kAesBytes;
 constexpr uint32_t kSmallFold = kAesBytes + kGhBytes;
 constexpr uint32_t kSmallSmem = kSmallFold + 4 * 8192u;

@@ -6,8 +6,9 @@ Each function restates, line for line, one piece of confkv_b200/csrc:
                interior loop;
   grids        horner_grid and the open-CTR rows_per_cta split
                (gpu_aesgcm.cu), which cut one object into tiles;
-  batch plan   batch_plan_kernel (batch.cuh): the row space of the tile
-               objects, its chunks and each chunk's segments.
+  batch plan   batch_plan_kernel (batch.cuh): which objects take one warp
+               each, the row space of the tile objects, its chunks and each
+               chunk's segments.
 The interior loops index memory without bounds checks, so these replays are
 their bounds proofs.
 """
@@ -24,6 +25,9 @@ CHUNKS_PER_SM_FEW = 2  # kChunksPerSmFew
 MIN_CHUNK_ROWS = 64  # kMinChunkRows
 MAX_CHUNKS = CHUNKS_PER_SM * BATCH_MAX_SMS
 SMALL_MAX_BLOCKS = 1024  # kSmallMaxBlocks
+WARP_MAX_BLOCKS = 2048   # kWarpMaxBlocks
+MID_ALPHA_SEAL = 26      # kMidAlphaSeal
+MID_ALPHA_OPEN = 19      # kMidAlphaOpen
 SEGMENT_COST_ROWS = 5    # kSegmentCostRows
 
 
@@ -123,13 +127,33 @@ def chunk_of(x, R, M):
     return ((x + 1) * M - 1) // R
 
 
-def tile_rows(P, ok=True):
-    """Rows of a tile object (0 for small and invalid objects)."""
+def tile_rows(P, ok=True, mid_routed=False):
+    """Rows of a tile object (0 for small and invalid objects, and for mid
+    objects when the batch sends them down the warp path)."""
     n = cdiv(P, 16)
-    return cdiv(n, T) if ok and n > SMALL_MAX_BLOCKS else 0
+    if not ok or n <= SMALL_MAX_BLOCKS or (mid_routed and n <= WARP_MAX_BLOCKS):
+        return 0
+    return cdiv(n, T)
 
 
-def chunk_plan(lens, sms, valid=None, classes=None):
+def mid_routed(lens, sms, valid=None, open_=False):
+    """The plan's routing rule: mid objects (SMALL_MAX_BLOCKS + 1 ..
+    WARP_MAX_BLOCKS blocks) take one warp each when there are any and the
+    batch's N warp-path objects (small plus mid) satisfy
+    N * sum(rows + o) * T >= alpha * max_n * sms * mids over the mid
+    objects; `sms` is the plan's SM count (at most BATCH_MAX_SMS)."""
+    valid = valid if valid is not None else [True] * len(lens)
+    blocks = [cdiv(P, 16) for P, ok in zip(lens, valid) if ok]
+    mid = [n for n in blocks if SMALL_MAX_BLOCKS < n <= WARP_MAX_BLOCKS]
+    if not mid:
+        return False
+    warp = sum(1 for n in blocks if n <= WARP_MAX_BLOCKS)
+    cost = sum(cdiv(n, T) + SEGMENT_COST_ROWS for n in mid)
+    alpha = MID_ALPHA_OPEN if open_ else MID_ALPHA_SEAL
+    return warp * cost * T >= alpha * max(mid) * sms * len(mid)
+
+
+def chunk_plan(lens, sms, valid=None, classes=None, open_=False):
     """batch_plan_kernel: the row space (tile objects grouped by alignment
     class; inside a class the device order follows its atomics, here the
     descriptor order), its chunk count M, the chunks' first rows (cut at
@@ -139,10 +163,11 @@ def chunk_plan(lens, sms, valid=None, classes=None):
     valid = valid if valid is not None else [True] * len(lens)
     classes = classes if classes is not None else [0] * len(lens)
     sms = min(sms, BATCH_MAX_SMS)
+    routed = mid_routed(lens, sms, valid, open_)
     objs, row = [], 0
     order = sorted(range(len(lens)), key=lambda i: (classes[i], i))
     for i in order:
-        rows = tile_rows(lens[i], valid[i])
+        rows = tile_rows(lens[i], valid[i], routed)
         if rows:
             objs.append((row, i, rows))
             row += rows
@@ -165,7 +190,7 @@ def chunk_plan(lens, sms, valid=None, classes=None):
             chunk_first[c] = k
             chunk_start[c] = start + max(0, x - p - o)
     return {"R": R, "M": M, "objs": objs, "chunk_first": chunk_first, "chunk_start": chunk_start,
-            "segments": segs}
+            "segments": segs, "mid_routed": routed}
 
 
 def chunk_segments(plan, chunk):

@@ -136,7 +136,7 @@ def test_batch_workspace_size(cpu_lib):
     # small-object list regions (one per size bucket) of a 4-B entry per object
     r256 = lambda x: (x + 255) // 256 * 256
     for count in (1, 7, 8, 9, 4096, 1 << 20):
-        assert ws(count) == 256 + r256(count * 32) + r256((count + 1) * 16) + 1025 * 16 + 4 * count * 4
+        assert ws(count) == 256 + r256(count * 32) + r256((count + 1) * 16) + 1025 * 16 + 5 * count * 4
     assert ws((1 << 20) + 1) == 0
 
 

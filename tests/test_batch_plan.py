@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 from schedules import (MAX_CHUNKS, SEGMENT_COST_ROWS, SMALL_MAX_BLOCKS, T, cdiv, chunk_plan, chunk_segments, ctr_tile_rows,
-                       open_tile_rows, pad_rows, seal_tile_rows, segment_base, tile_base, tile_rows)
+                       mid_routed, open_tile_rows, pad_rows, seal_tile_rows, segment_base, tile_base, tile_rows)
 
 
 def _ragged(count, seed, lo=4096, hi=1 << 20):
@@ -29,6 +29,9 @@ BATCHES = {
     "tiny_many": list(range(0, 20000, 7)),
     "max_blocks": [16 * 0xFFFFFFFE, 5],
     "just_above_small": [SMALL_MAX_BLOCKS * 16 + 1] * 7,
+    # mid objects (16-32 KiB): few stay tile objects, many take one warp each
+    "mid_few": [32768, 24576, 16385, 32767, 4096] * 40,
+    "mid_many": [32768, 20480, 16400, 2048] * 400,
 }
 
 
@@ -40,12 +43,15 @@ def _walk(plan):
 @pytest.mark.parametrize("name", sorted(BATCHES))
 @pytest.mark.parametrize("sms", [148, 132, 1, 300])
 @pytest.mark.parametrize("mixed", [False, True])
-def test_chunks_cover_every_row_once(name, sms, mixed):
+@pytest.mark.parametrize("open_", [False, True])
+def test_chunks_cover_every_row_once(name, sms, mixed, open_):
     lens = BATCHES[name]
     classes = [(7 * i) % 10 for i in range(len(lens))] if mixed else None
-    plan = chunk_plan(lens, sms, classes=classes)
+    plan = chunk_plan(lens, sms, classes=classes, open_=open_)
     R, M = plan["R"], plan["M"]
-    assert R == sum(tile_rows(P) for P in lens)
+    routed = plan["mid_routed"]
+    assert routed == mid_routed(lens, min(sms, 256), open_=open_)
+    assert R == sum(tile_rows(P, True, routed) for P in lens)
     assert M <= MAX_CHUNKS and M <= R and (M > 0) == (R > 0)
     # chunks are non-empty and of near-equal cost: rows plus a charge per
     # segment, within two charges and one row of each other
@@ -64,11 +70,11 @@ def test_chunks_cover_every_row_once(name, sms, mixed):
         cls = [classes[item] for item, _, _, _ in segs]
         assert sum(a != b for a, b in zip(cls, cls[1:])) <= 9
     for item, rows, r0, r1 in segs:
-        assert 0 <= r0 < r1 <= rows == tile_rows(lens[item])
+        assert 0 <= r0 < r1 <= rows == tile_rows(lens[item], True, routed)
         covered.setdefault(item, []).append((r0, r1))
         count[item] = count.get(item, 0) + 1
     for i, P in enumerate(lens):
-        rows = tile_rows(P)
+        rows = tile_rows(P, True, routed)
         if rows == 0:
             assert i not in covered and plan["segments"][i] == 0   # small or empty: one warp, no segments
             continue
@@ -97,6 +103,34 @@ def test_chunk_counts():
     # nothing to tile
     assert chunk_plan([5, 6], 148, valid=[False, False])["M"] == 0
     assert chunk_plan([], 148)["M"] == 0
+
+
+def test_mid_objects_take_the_warp_path_only_in_number():
+    sms = 148
+    # 2048 objects of 32 KiB: 13.8 per SM, one warp each
+    plan = chunk_plan([32768] * 2048, sms)
+    assert plan["mid_routed"] and plan["R"] == 0 and plan["M"] == 0
+    # crossovers of 32 KiB objects: seal from 26 * 2048 / (9 * 512) = 11.6
+    # objects per SM, open from 19 * 2048 / (9 * 512) = 8.4
+    assert not mid_routed([32768] * 1710, sms) and mid_routed([32768] * 1711, sms)
+    assert not mid_routed([32768] * 1249, sms, open_=True) and mid_routed([32768] * 1250, sms, open_=True)
+    plan = chunk_plan([32768] * 1480, sms)
+    assert not plan["mid_routed"] and plan["R"] == 4 * 1480
+    assert chunk_plan([32768] * 1480, sms, open_=True)["mid_routed"]
+    # 20 KiB objects (3 rows as tiles, 40 as a warp): seal from 8.1 per SM
+    assert not mid_routed([20480] * 1202, sms) and mid_routed([20480] * 1203, sms)
+    # small objects count toward N; larger objects stay tiles
+    lens = [32768] * 10 + [4096] * 1702 + [1 << 20] * 3
+    plan = chunk_plan(lens, sms)
+    assert plan["mid_routed"] and plan["R"] == 3 * 128
+    # without mid objects there is nothing to route
+    assert not chunk_plan([4096] * 5000, sms)["mid_routed"]
+    # invalid descriptors do not count; a mixed batch can route open only
+    assert not mid_routed([32768] * 1711, sms, valid=[True] * 1710 + [False])
+    mixed = [32768, 20480, 16400, 2048] * 400
+    assert not mid_routed(mixed, sms) and mid_routed(mixed, sms, open_=True)
+    assert tile_rows(32768) == 4 and tile_rows(32768, True, True) == 0
+    assert tile_rows(32784, True, True) == 5   # 2049 blocks: above the warp path
 
 
 def test_plan_skips_invalid():

@@ -238,6 +238,63 @@ def test_batch_many_small_objects(gpu_lib, oracle):
             assert np.array_equal(frames[fr_off[i]:fr_off[i] + lens[i] + 29], expected[i]), (i, lens[i])
 
 
+@pytest.mark.parametrize("per_sm", [0, 10, 16])
+def test_batch_mid_objects_both_routes(gpu_lib, oracle, per_sm):
+    """Objects of 1025..2048 blocks (16-32 KiB) take one warp each when the
+    batch has enough of them, else they are tile objects: 300 objects stay
+    tiles, 10 per SM take warps in open only, 16 per SM in both directions
+    (the plan's rule, replayed by tests/schedules.py). Both routes give
+    OpenSSL's frames and open's gating. Sizes cover both ends of the range
+    and the first size above it, every alignment class; one object in 50 is
+    tampered."""
+    from schedules import mid_routed
+
+    sms = min(torch.cuda.get_device_properties(0).multi_processor_count, 256)
+    count = per_sm * sms + 7 if per_sm else 300
+    rng = np.random.default_rng(88 + per_sm)
+    key = rng.bytes(16)
+    edges = [16 * 1024 + 1, 16 * 1025, 16 * 2048 - 1, 16 * 2048, 16 * 2048 + 1, 16 * 2049, 4096, 0]
+    lens = np.concatenate([edges, rng.integers(16 * 1024 + 1, 16 * 2048 + 1, size=count - len(edges))]).astype(np.int64)
+    routes = (mid_routed(lens.tolist(), sms), mid_routed(lens.tolist(), sms, open_=True))
+    assert routes == {0: (False, False), 10: (False, True), 16: (True, True)}[per_sm]
+    ivs = [rng.bytes(12) for _ in lens]
+    pts = [rng.integers(0, 256, size=int(n), dtype=np.uint8) for n in lens]
+    pt_off, pt_total = _packed(lens, pad=3)
+    fr_off, fr_total = _packed(lens + 29, pad=5)
+    d_plain = torch.zeros(pt_total + 16, dtype=torch.uint8, device="cuda")
+    d_plain[:pt_total].copy_(torch.from_numpy(np.concatenate(
+        [np.concatenate([p, np.zeros(3, np.uint8)]) for p in pts])))
+    d_frames = torch.full((fr_total + 16,), 0xAB, dtype=torch.uint8, device="cuda")
+    d_out = torch.full((pt_total + 16,), 0xCC, dtype=torch.uint8, device="cuda")
+    d_auth = torch.full((len(lens),), 7, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    batch = DeviceBatch(gpu_lib, len(lens))
+    with GpuAes128GcmKey(gpu_lib, key) as k:
+        batch.seal(k, _seal_entries(d_plain, pt_off, d_frames, fr_off, lens, ivs), s)
+        s.synchronize()
+        assert int(batch.fault()) == 0 and not batch.statuses().any()
+        frames = d_frames.cpu().numpy()
+        expected = oracle.evp_seal_many(key, ivs, pts)
+        for i in range(len(lens)):
+            assert np.array_equal(frames[fr_off[i]:fr_off[i] + lens[i] + 29], expected[i]), (i, lens[i])
+        bad = set(range(3, len(lens), 50))
+        for i in bad:
+            frames[fr_off[i] + 13 + int(rng.integers(0, lens[i] + 16))] ^= 0x10
+        d_frames.copy_(torch.from_numpy(frames))
+        batch.open(k, _open_entries(d_frames, fr_off, d_out, pt_off, lens, d_auth, range(len(lens))), s)
+        s.synchronize()
+        assert int(batch.fault()) == 0
+    auth = d_auth.cpu().numpy()
+    out = d_out.cpu().numpy()
+    for i in range(len(lens)):
+        seg = out[pt_off[i]:pt_off[i] + lens[i]]
+        if i in bad:
+            assert auth[i] == 0 and not seg.any(), i
+        else:
+            assert auth[i] == 1 and np.array_equal(seg, pts[i]), i
+        assert (out[pt_off[i] + lens[i]:pt_off[i] + lens[i] + 3] == 0xCC).all(), i
+
+
 def test_batch_two_hundred_thousand_tiny_objects(gpu_lib, oracle):
     """200,000 objects of 0..256 bytes in one seal and one open call (the
     warp-per-object path, a plan over hundreds of objects per thread); every
@@ -351,7 +408,7 @@ def test_batch_handoff_wait_runs_out_without_hanging(gpu_lib, monkeypatch):
     import time
 
     key = workloads.make_key(41)
-    lens = np.array([20 * 1024] * 2000, dtype=np.int64)   # 3-row tile objects: many segments per CTA
+    lens = np.array([40 * 1024] * 1200, dtype=np.int64)   # 5-row tile objects: many segments per CTA
     ivs = workloads.make_ivs(41, len(lens))
     pt_off, pt_total = _packed(lens, align=16)
     fr_off, fr_total = _packed(lens + 29, align=16)
