@@ -258,7 +258,7 @@ def run_ours(args, rank, world, local):
     # e2e through the public API: pinned host plaintext -> H2D -> seal -> D2H
     # frames, then open -> D2H auth flags; copies overlapped across objects.
     e2e = {"ms": float("nan"), "gbs": float("nan"), "h2d": 0, "d2h": 0} if args.no_e2e else \
-        run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args)
+        run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args, barrier)
     (e2e_ms, copy_ms) = multigpu.reduce_max([e2e["ms"], e2e.get("copy_ms", float("nan"))], device=dev)
 
     if rank == 0:
@@ -369,8 +369,10 @@ def run_ours(args, rank, world, local):
         torch.distributed.destroy_process_group()
 
 
-def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
-    """Same step through the public API with host buffers and copies timed."""
+def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args, barrier):
+    """Same step through the public API with host buffers and copies timed.
+    Every rank runs each timed phase at the same time (barrier before each):
+    the ranks share the host's memory and links."""
     n = plain_u8.shape[0]
     host_in = torch.empty((n, P), dtype=torch.uint8, pin_memory=True)
     host_in.copy_(plain_u8.cpu())
@@ -412,18 +414,17 @@ def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
             s_d2h.wait_event(e_seal)
             with torch.cuda.stream(s_d2h):
                 host_frames[k].copy_(frames[k], non_blocking=True)
-        # opens on their own stream: the next step's seals need not wait for them
-        e_sealed = torch.cuda.Event()
-        e_sealed.record(s_cmp)
-        s_open.wait_event(e_sealed)
-        for k in range(n):
+            # each open follows its seal on its own stream, so the next
+            # object's seal and the frame copies never wait for it
+            s_open.wait_event(e_seal)
             key.open_async(src_ptr=frames[k].data_ptr(), frame_len=frame_len, dst_ptr=d_out[k].data_ptr(),
                            plaintext_len=P, auth_ok_ptr=auth[k:k + 1].data_ptr(), stream_ptr=s_open.cuda_stream)
         e_open = torch.cuda.Event()
         e_open.record(s_open)
         opened[b] = e_open
-        s_d2h.wait_event(e_open)
-        with torch.cuda.stream(s_d2h):
+        # the verdicts go back on the open stream: the frame stream (the
+        # host link's busy direction) does not wait for the opens
+        with torch.cuda.stream(s_open):
             host_auth[b].copy_(auth, non_blocking=True)
 
     def copies_only():
@@ -443,7 +444,7 @@ def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args):
     def timed_steps(fn, steps):
         for _ in range(2):
             fn()
-        torch.cuda.synchronize(dev)
+        barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(s_h2d)
