@@ -149,6 +149,27 @@ class RankWork:
         e.record(side)
         self.stream.wait_event(e)
 
+    def open_each_from_host(self, side: torch.cuda.Stream):
+        """Per-object open of frames held in pinned host memory (the load path
+        from host storage): each frame is copied in on `side` and opened on the
+        work stream as soon as it has arrived, so copies overlap the opens of
+        earlier objects. The copies start after the work stream's earlier
+        work, whose opens may still read the frame buffer."""
+        if self.host is None:
+            raise RuntimeError("no host frames: seal_each_d2h or seal_each_to_host first")
+        e = torch.cuda.Event()
+        e.record(self.stream)
+        side.wait_event(e)
+        sp = self.stream.cuda_stream
+        for i, (f, d, n, fl, a) in enumerate(self.open_entries):
+            o = self.fr_off[i]
+            with torch.cuda.stream(side):
+                self.frames[o:o + n + 29].copy_(self.host[o:o + n + 29], non_blocking=True)
+            e = torch.cuda.Event()
+            e.record(side)
+            self.stream.wait_event(e)
+            self.key.open_async(src_ptr=f, frame_len=fl, dst_ptr=d, plaintext_len=n, auth_ok_ptr=a, stream_ptr=sp)
+
     def reset_outputs(self):
         self.out.zero_()
         self.auth.zero_()
@@ -229,6 +250,14 @@ def measure(work: RankWork, apis, warmup, iters, world, dev, d2h=False) -> list[
             out[0]["seal_to_host_gbs"] = round(total / (t["median_ms"] * 1e-3) / 1e9, 2)
             out[0]["seal_to_host_ms_median"] = round(t["median_ms"], 4)
             out[0]["seal_to_host_frames_ok"] = bool(multigpu.all_ok(same, device=dev))
+        # the load path: frames from pinned host memory -> H2D -> gated open
+        torch.cuda.synchronize(dev)
+        work.reset_outputs()
+        t = timed(lambda: work.open_each_from_host(side), work.stream, warmup, iters, world, dev)
+        torch.cuda.synchronize(dev)
+        out[0]["open_h2d_gbs"] = round(total / (t["median_ms"] * 1e-3) / 1e9, 2)
+        out[0]["open_h2d_ms_median"] = round(t["median_ms"], 4)
+        out[0]["open_h2d_round_trip_ok"] = bool(multigpu.all_ok(work.round_trip_ok(), device=dev))
     return out
 
 

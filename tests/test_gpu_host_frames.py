@@ -1,10 +1,12 @@
-"""Seal straight into pinned host memory.
+"""Frames in pinned host memory: the store and load paths.
 
 Pinned host memory (cudaHostAlloc, torch `pin_memory=True`) is mapped into the
 device's address space at the same address, so seal_async and
 seal_batch_async can write frames directly into it: the persistent-store path
 without a separate device-to-host copy. The frames must equal the OpenSSL EVP
-frames; the host-side check (`hostmem.device_mapped`) must hold first.
+frames; the host-side check (`hostmem.device_mapped`) must hold first. The
+load path copies frames from pinned host memory in on a side stream and opens
+each one as soon as it has arrived; tampered frames are rejected and zeroed.
 """
 
 import numpy as np
@@ -13,6 +15,7 @@ import torch
 
 from confkv_b200 import hostmem, workloads
 from confkv_b200.batch import DeviceBatch
+from confkv_b200.configs import RankWork, random_plain
 from confkv_b200.gpu_aesgcm import GpuAes128GcmKey
 
 pytestmark = pytest.mark.gpu
@@ -86,3 +89,41 @@ def test_seal_batch_into_pinned_host(gpu_lib, oracle):
 def test_device_mapped_rejects_pageable_memory():
     a = np.zeros(4096, dtype=np.uint8)
     assert not hostmem.device_mapped(a.ctypes.data)
+
+
+def test_open_frames_from_pinned_host(gpu_lib, oracle):
+    """RankWork.open_each_from_host: OpenSSL frames placed in pinned host
+    memory open on the GPU after their H2D copies; one tampered frame in
+    three is rejected with a zeroed output, the rest round-trip."""
+    dev = torch.device("cuda", 0)
+    key = workloads.make_key(33)
+    lens = [n for n in SIZES for _ in range(3)]
+    ivs = workloads.make_ivs(33, len(lens))
+    plain, offs = random_plain(lens, seed=33, dev=dev)
+    s = torch.cuda.Stream()
+    with GpuAes128GcmKey(gpu_lib, key) as k:
+        w = RankWork(gpu_lib, k, lens, plain, offs, s, ivs)   # runs one batched seal + open on s
+        s.synchronize()
+        host_plain = plain.cpu().numpy()
+        expected = oracle.evp_seal_many(key, ivs, [host_plain[o:o + n] for o, n in zip(offs, lens)])
+        w.host_ptr()
+        bad = set(range(2, len(lens), 3))
+        for i, (o, n) in enumerate(zip(w.fr_off, lens)):
+            f = expected[i].copy()
+            if i in bad:
+                f[13 + (7 * i) % (n + 16)] ^= 0x04
+            w.host[o:o + n + 29].copy_(torch.from_numpy(f))
+        side = torch.cuda.Stream()
+        w.out.fill_(0xCC)
+        w.auth.fill_(7)
+        torch.cuda.synchronize()
+        w.open_each_from_host(side)
+        w.open_each_from_host(side)   # a second pass over the same buffers
+        s.synchronize()
+        auth = w.auth.cpu().numpy()
+        out = w.out.cpu().numpy()
+        for i, (o, n) in enumerate(zip(offs, lens)):
+            if i in bad:
+                assert auth[i] == 0 and not out[o:o + n].any(), (i, n)
+            else:
+                assert auth[i] == 1 and np.array_equal(out[o:o + n], host_plain[o:o + n]), (i, n)
