@@ -442,6 +442,65 @@ __device__ __forceinline__ void aes_ctr2_cached(uint32_t x[4], uint32_t y[4], ui
     }
 }
 
+// Counter-mode round caching for one warp's rows: lane l of row r takes
+// counter c0 + 32 r + l, so counter bytes 12..14 change only on a carry out of
+// byte 15. Within an epoch (ctr >> 8) round 1 has a single varying lookup
+// (column 0, T3 of state byte 15) and round 2 one varying lookup per column
+// (all from column 0): 5 lookups instead of 32.
+struct WarpCtrCache {
+    uint32_t epoch;  // ctr >> 8 the cache was built for
+    uint32_t k0;     // round-1 column 0 without T3[state byte 15]
+    uint32_t l[4];   // round-2 columns without their column-0 term
+};
+
+// Builds the cache for the epoch of ctr (its byte 15 is not used).
+template <uint32_t TAB>
+__device__ __forceinline__ void warp_ctr_cache_build(WarpCtrCache& cc, uint32_t ctr, const uint32_t s012[3],
+                                                     const uint32_t* rk, const uint32_t lb[4])
+{
+    const uint32_t s0 = s012[0], s1 = s012[1], s2 = s012[2];
+    const uint32_t s3 = bswap32(ctr) ^ rk[3];
+    const uint32_t n1 = tlook<TAB>(s1, lb[0], 0) ^ tlook<TAB>(s2, lb[1], 1) ^ tlook<TAB>(s3, lb[2], 2) ^
+                        tlook<TAB>(s0, lb[3], 3) ^ rk[5];
+    const uint32_t n2 = tlook<TAB>(s2, lb[0], 0) ^ tlook<TAB>(s3, lb[1], 1) ^ tlook<TAB>(s0, lb[2], 2) ^
+                        tlook<TAB>(s1, lb[3], 3) ^ rk[6];
+    const uint32_t n3 = tlook<TAB>(s3, lb[0], 0) ^ tlook<TAB>(s0, lb[1], 1) ^ tlook<TAB>(s1, lb[2], 2) ^
+                        tlook<TAB>(s2, lb[3], 3) ^ rk[7];
+    cc.k0 = tlook<TAB>(s0, lb[0], 0) ^ tlook<TAB>(s1, lb[1], 1) ^ tlook<TAB>(s2, lb[2], 2) ^ rk[4];
+    cc.l[0] = tlook<TAB>(n1, lb[1], 1) ^ tlook<TAB>(n2, lb[2], 2) ^ tlook<TAB>(n3, lb[3], 3) ^ rk[8];
+    cc.l[1] = tlook<TAB>(n1, lb[0], 0) ^ tlook<TAB>(n2, lb[1], 1) ^ tlook<TAB>(n3, lb[2], 2) ^ rk[9];
+    cc.l[2] = tlook<TAB>(n2, lb[0], 0) ^ tlook<TAB>(n3, lb[1], 1) ^ tlook<TAB>(n1, lb[3], 3) ^ rk[10];
+    cc.l[3] = tlook<TAB>(n3, lb[0], 0) ^ tlook<TAB>(n1, lb[2], 2) ^ tlook<TAB>(n2, lb[3], 3) ^ rk[11];
+    cc.epoch = ctr >> 8;
+}
+
+// Keystream block E_K(IV || BE32(ctr)) for one warp row (every lane calls it
+// with its own counter; the counters of a row are consecutive). When every
+// lane's counter is in the cached epoch: rounds 1-2 from the cache. Otherwise
+// the whole warp runs the full cipher and rebuilds the cache for the next
+// row's counters (ctr + 32), so a row crossing an epoch boundary costs one
+// slow row and no divergence.
+template <uint32_t TAB>
+__device__ __forceinline__ void warp_ctr_keystream(uint32_t x[4], uint32_t ctr, WarpCtrCache& cc,
+                                                   const uint32_t s012[3], const uint32_t* rk, const uint32_t lb[4])
+{
+    if (__all_sync(0xffffffffu, (ctr >> 8) == cc.epoch)) {
+        const uint32_t n0 = cc.k0 ^ tlook<TAB>(bswap32(ctr) ^ rk[3], lb[3], 3);
+        x[0] = cc.l[0] ^ tlook<TAB>(n0, lb[0], 0);
+        x[1] = cc.l[1] ^ tlook<TAB>(n0, lb[3], 3);
+        x[2] = cc.l[2] ^ tlook<TAB>(n0, lb[2], 2);
+        x[3] = cc.l[3] ^ tlook<TAB>(n0, lb[1], 1);
+        aes_rounds_from<TAB, 3>(x, rk, lb);
+    } else {
+        x[0] = s012[0];
+        x[1] = s012[1];
+        x[2] = s012[2];
+        x[3] = bswap32(ctr) ^ rk[3];
+        aes_rounds_from<TAB, 1>(x, rk, lb);
+        warp_ctr_cache_build<TAB>(cc, ctr + 32u, s012, rk, lb);
+    }
+}
+
 // Same cipher reading the compact T-tables from global memory (one-off blocks).
 __device__ inline uint4 aes_encrypt_gmem(const uint32_t* T, const uint32_t* rk, uint4 in)
 {

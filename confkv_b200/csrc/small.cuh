@@ -125,18 +125,20 @@ __device__ __forceinline__ void seal_object_warp(const BatchItem* it, const uint
     const int64_t lo = so == 0 ? 0 : 1;
     const int64_t hi = g.n_full - (so == 0 ? 0 : 1);
     uint4 q = make_uint4(0, 0, 0, 0);
+    WarpCtrCache cc{0xffffffffu, 0u, {0u, 0u, 0u, 0u}};
 #pragma unroll 1
     for (int64_t r = 0; r < g.rows; ++r) {
         const int64_t i0 = g.base + 32 * r;
         const int64_t i = i0 + lane;
-        uint32_t x[4] = {s012[0], s012[1], s012[2], bswap32(static_cast<uint32_t>(i) + 2u) ^ rk[3]};
+        const uint32_t ctr = static_cast<uint32_t>(i) + 2u;
+        uint32_t x[4];
         uint4 c;
         if (i0 >= lo && i0 + 32 <= hi) {
             const uint8_t* sp = src + static_cast<uint64_t>(i) * 16u;
             const uint4 p = so == 0 ? __ldg(reinterpret_cast<const uint4*>(sp))
                                     : window16(__ldg(reinterpret_cast<const uint4*>(sp - so)),
                                                __ldg(reinterpret_cast<const uint4*>(sp - so + 16)), sq, sfs);
-            aes_rounds_smem<0>(x, rk, lb);
+            warp_ctr_keystream<0>(x, ctr, cc, s012, rk, lb);
             c = make_uint4(p.x ^ x[0], p.y ^ x[1], p.z ^ x[2], p.w ^ x[3]);
             if (co == 0) {
                 *reinterpret_cast<uint4*>(ct + static_cast<uint64_t>(i) * 16u) = c;
@@ -146,7 +148,7 @@ __device__ __forceinline__ void seal_object_warp(const BatchItem* it, const uint
         } else {
             const int nb = block_bytes(i, g.P);
             const uint4 p = load_pt_block<false>(src, i, g.P);
-            aes_rounds_smem<0>(x, rk, lb);
+            warp_ctr_keystream<0>(x, ctr, cc, s012, rk, lb);
             c = mask_bytes(make_uint4(p.x ^ x[0], p.y ^ x[1], p.z ^ x[2], p.w ^ x[3]), nb);
             if (co == 0) {
                 if (nb == 16) {
@@ -224,6 +226,7 @@ __device__ __forceinline__ void open_object_warp(const BatchItem* it, const uint
     const uint32_t ds = 16u - d_off;
     const uint32_t dq = (ds >> 2) & 3u;
     const uint32_t dfs = funnel_sel(ds & 3u);
+    WarpCtrCache cc{0xffffffffu, 0u, {0u, 0u, 0u, 0u}};
 #pragma unroll 1
     for (int64_t r = 0; r < g.rows; ++r) {
         const int64_t i0 = g.base + 32 * r;
@@ -238,8 +241,8 @@ __device__ __forceinline__ void open_object_warp(const BatchItem* it, const uint
             }
             continue;
         }
-        uint32_t x[4] = {s012[0], s012[1], s012[2], bswap32(static_cast<uint32_t>(i) + 2u) ^ rk[3]};
-        aes_rounds_smem<0>(x, rk, lb);
+        uint32_t x[4];
+        warp_ctr_keystream<0>(x, static_cast<uint32_t>(i) + 2u, cc, s012, rk, lb);
         if (i0 >= 1 && i0 + 32 <= g.n_full) {
             const uint4 c = ct_fast(i);
             const uint4 p = make_uint4(c.x ^ x[0], c.y ^ x[1], c.z ^ x[2], c.w ^ x[3]);
