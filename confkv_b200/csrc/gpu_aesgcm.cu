@@ -125,15 +125,22 @@ __global__ void seal_empty_kernel(const SealArgs a)
 
 // ---------------------------------------------------- open: GHASH + verify
 //
-// Same tiles and fold as seal_kernel over the ciphertext at frame + 13, with
-// kOpenChains chains per thread. The power warp computes E_K(J0) and L*H up
-// front; the last CTA compares the expected tag with the frame's (16 bytes,
-// OR-accumulated) and checks the version byte, then writes *auth_ok.
+// Same tiles as seal_kernel over the ciphertext at frame + 13, with
+// kOpenChains chains per thread. Every fold table is in shared memory, so
+// the two-stage fold of the batched kernels (tiles.cuh) needs one barrier:
+// each row warp folds its partials with levels 0..3 and hands two values to
+// the power warp, which folds them with levels 4..8. (Seal keeps the block
+// fold: its levels 4..8 would read the key's global tables, five dependent
+// L2 round trips that cost 2 MiB objects 14 %.) The power warp computes
+// E_K(J0) and L*H up front; the last CTA compares the expected tag with the
+// frame's (16 bytes, OR-accumulated) and checks the version byte, then
+// writes *auth_ok.
 template <int LQ>
 __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenArgs a)
 {
     extern __shared__ __align__(16) uint8_t smem[];
-    uint4* part = reinterpret_cast<uint4*>(smem + kOpenPart);
+    uint4* part = reinterpret_cast<uint4*>(smem + kOpenPart);  // the row warps' fold values V_0..V_31
+    const uint4* fold_tabs = reinterpret_cast<const uint4*>(smem + kOpenFold);
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -162,15 +169,18 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
         const OpenTile t{a.frame, a.frame_len, P,
                          static_cast<int64_t>(a.nblocks) - static_cast<int64_t>(a.grid - blockIdx.x) * span,
                          static_cast<int64_t>(a.iters), a.load_r};
-        part[tid] = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), tid, lane);
+        const uint4 q = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), tid, lane);
+        const uint4 v = warp_fold_pairs<false>(q, fold_tabs, lane);
+        if (lane < 2) {
+            part[2 * warp + lane] = v;
+        }
     }
     __syncthreads();
 
-    fold_partials<kFoldLevels>(part, reinterpret_cast<const uint4*>(smem + kOpenFold), a.kt.gh_pow2);
-
     if (warp == kPowerWarp) {
+        const uint4 fold = power_fold(part[lane], fold_tabs + 4 * 512, lane);
         unsigned long long shi, slo;
-        if (cta_accumulate(a.slot, part[0], uhi, ulo, lane, a.grid, shi, slo) && lane == 0) {
+        if (cta_accumulate(a.slot, fold, uhi, ulo, lane, a.grid, shi, slo) && lane == 0) {
             *a.auth_ok = open_verdict(a.frame, P, shi, slo, lh, ej0);
         }
     }

@@ -211,7 +211,8 @@ __device__ __forceinline__ void seal_fold(uint8_t* smem, uint4* part, const uint
 //
 // The persistent batched kernels fold a tile's kHornerThreads partials Q_t in
 // two stages, so the row warps hand their tile over and start the next one
-// without waiting for the tile's epilogue:
+// without waiting for the tile's epilogue (the per-object open-GHASH kernel
+// folds the same way, with one barrier):
 //   row warps   warp w folds its 32 partials with levels 0..3 into
 //               V_p = sum_{t in [16p, 16p+16)} Q_t H^(16p+15-t), p = 2w, 2w+1
 //               (warp_fold_pairs);
