@@ -29,7 +29,6 @@ import os
 import statistics
 import subprocess
 import sys
-import time
 from pathlib import Path
 
 
@@ -94,54 +93,6 @@ def profile_summary(name: str) -> dict:
                 except ValueError:
                     pass
     return out
-
-
-class ClockSampler:
-    """nvidia-smi clock/throttle sampling during the timed region."""
-
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
-
-    def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
-
-    def stop(self) -> dict | None:
-        if self.proc is None:
-            return None
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = max(mx, float(r[2]))
-                for nm, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(nm)
-            except (ValueError, IndexError):
-                continue
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
 
 
 # ----------------------------------------------------------------- ours
@@ -242,6 +193,7 @@ def run_ours(args, rank, world, local):
         return seal_ms, open_ms, ok
 
     from confkv_b200 import multigpu
+    from confkv_b200.clocks import ClockSampler
 
     apis = ["batched", "per_object"] if args.api == "both" else [args.api]
     clocks = ClockSampler(local)

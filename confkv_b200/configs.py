@@ -38,6 +38,7 @@ import torch
 
 from . import hostmem, multigpu, workloads
 from .batch import DeviceBatch
+from .clocks import ClockSampler
 from .gpu_aesgcm import GpuAes128GcmKey, GpuAesGcmLibrary
 
 ALIGN = 256
@@ -223,11 +224,14 @@ def measure(work: RankWork, apis, warmup, iters, world, dev, d2h=False) -> list[
             seal_fn, open_fn = work.seal_batched, work.open_batched
         work.reset_outputs()
         barrier(world, dev)
+        clocks = ClockSampler(dev.index if dev.index is not None else 0)
+        clocks.start()
         rs = timed(seal_fn, work.stream, warmup, iters, world, dev)
         ro = timed(open_fn, work.stream, warmup, iters, world, dev)
+        clk = clocks.stop()
         barrier(world, dev)
         ok = multigpu.all_ok(work.round_trip_ok(), device=dev)
-        r = {"api": api, "bytes_all_ranks": total, "round_trip_ok": ok}
+        r = {"api": api, "bytes_all_ranks": total, "round_trip_ok": ok, "clocks": clk}
         for name, t in (("seal", rs), ("open", ro)):
             r[f"{name}_gbs"] = round(total / (t["median_ms"] * 1e-3) / 1e9, 2)
             r[f"{name}_ms_median"] = round(t["median_ms"], 4)
