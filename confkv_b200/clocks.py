@@ -20,7 +20,6 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines: list[str] = []
 
     def start(self):
         try:
@@ -40,19 +39,30 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = max(mx, float(r[2]))
-                for nm, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(nm)
-            except (ValueError, IndexError):
-                continue
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return summarize(out)
+
+
+REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+
+def summarize(text: str) -> dict | None:
+    """Summary of `nvidia-smi --query-gpu=<ClockSampler.FIELDS> --format=csv,noheader,nounits`
+    output: median SM clock, the highest max clock seen, and every throttle
+    reason that was Active in any sample. Lines that do not parse (a line cut
+    off when the sampler was stopped) are skipped; None when no line parses."""
+    sm, mx, reasons = [], 0.0, set()
+    for line in text.strip().splitlines():
+        r = [f.strip() for f in line.split(",")]
+        try:
+            clk, top = float(r[1]), float(r[2])
+            flags = r[5:9]
+        except (ValueError, IndexError):
+            continue
+        if len(flags) != len(REASONS):
+            continue
+        sm.append(clk)
+        mx = max(mx, top)
+        reasons.update(nm for nm, v in zip(REASONS, flags) if v.lower() == "active")
+    if not sm:
+        return None
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
