@@ -1169,9 +1169,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
     const int tid = threadIdx.x;
     pdl_release();
     fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
-    for (int i = tid; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);
-    }
+    fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kOpenFold), a.kt.gh_pow2);
     const Handoff h = handoff_at(smem, kOpenBatchHandoff, kOpenBatchSync);
     if (tid == 0) {
         handoff_init(h, a.wait_ns);

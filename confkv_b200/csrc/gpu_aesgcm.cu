@@ -59,9 +59,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
     pdl_release();
     fill_aes_smem(smem + kSealAes, a.kt.aes_t);
     fill_gh_smem(smem + kSealGh, a.kt.gh_pow2 + kSealChainLog2 * 512);
-    for (int i = threadIdx.x; i < kSealFoldSmemLevels * 512; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + kSealFold)[i] = __ldg(a.kt.gh_pow2 + i);
-    }
+    fill_smem<kSealFoldSmemLevels * 512>(reinterpret_cast<uint4*>(smem + kSealFold), a.kt.gh_pow2);
     pdl_wait();
     if (blockIdx.x == 0 && tid == 0) {
         a.frame[0] = 1;
@@ -148,9 +146,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
 
     pdl_release();
     fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
-    for (int i = threadIdx.x; i < (kFoldLevels + 1) * 512; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + kOpenFold)[i] = __ldg(a.kt.gh_pow2 + i);  // H^(2^l), l <= kHornerLog2
-    }
+    fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kOpenFold), a.kt.gh_pow2);  // H^(2^l), l <= 9
     pdl_wait();
     __syncthreads();
 

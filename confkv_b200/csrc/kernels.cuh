@@ -529,16 +529,53 @@ __device__ inline uint4 aes_encrypt_gmem(const uint32_t* T, const uint32_t* rk, 
 }
 
 // Fill the 128 KiB replicated T-table region from the compact global tables.
+// Table fills run in every CTA's prologue, before any row can start. Each
+// thread issues all of its global loads before its first shared store, so the
+// fill costs one memory round trip rather than one per entry. Every kernel
+// that fills has blockDim.x >= kFillMinThreads.
+constexpr int kFillMinThreads = 512;
+
 __device__ __forceinline__ void fill_aes_smem(uint8_t* tab, const uint32_t* T)
 {
-    for (int i = threadIdx.x; i < 8192; i += blockDim.x) {
-        const int k = i >> 11;
-        const int x = (i >> 3) & 255;
-        const int q = i & 7;
-        const uint32_t t = __ldg(T + k * 256 + x);
-        const uint32_t off = (static_cast<uint32_t>(k >> 1) << 16) | (static_cast<uint32_t>(x) << 8) |
-                             (static_cast<uint32_t>(k & 1) << 7) | (static_cast<uint32_t>(q) << 4);
-        *reinterpret_cast<uint4*>(tab + off) = make_uint4(t, t, t, t);
+    constexpr int kN = 8192;
+    constexpr int kPer = (kN + kFillMinThreads - 1) / kFillMinThreads;
+    uint32_t t[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int i = static_cast<int>(threadIdx.x + k * blockDim.x);
+        t[k] = i < kN ? __ldg(T + (i >> 11) * 256 + ((i >> 3) & 255)) : 0u;
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int i = static_cast<int>(threadIdx.x + k * blockDim.x);
+        if (i < kN) {
+            const int tk = i >> 11;
+            const int x = (i >> 3) & 255;
+            const int q = i & 7;
+            const uint32_t off = (static_cast<uint32_t>(tk >> 1) << 16) | (static_cast<uint32_t>(x) << 8) |
+                                 (static_cast<uint32_t>(tk & 1) << 7) | (static_cast<uint32_t>(q) << 4);
+            *reinterpret_cast<uint4*>(tab + off) = make_uint4(t[k], t[k], t[k], t[k]);
+        }
+    }
+}
+
+// Copies N 16-byte entries from global to shared memory (prologue fills).
+template <int N>
+__device__ __forceinline__ void fill_smem(uint4* dst, const uint4* src)
+{
+    constexpr int kPer = (N + kFillMinThreads - 1) / kFillMinThreads;
+    uint4 v[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int i = static_cast<int>(threadIdx.x + k * blockDim.x);
+        v[k] = i < N ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int i = static_cast<int>(threadIdx.x + k * blockDim.x);
+        if (i < N) {
+            dst[i] = v[k];
+        }
     }
 }
 
@@ -556,12 +593,22 @@ __device__ __forceinline__ void aes_lane_bases(uint32_t lb[4], int lane)
 // Fill the 64 KiB replicated GHASH region from a compact 4-bit table.
 __device__ __forceinline__ void fill_gh_smem(uint8_t* gh, const uint4* compact)
 {
-    for (int i = threadIdx.x; i < 4096; i += blockDim.x) {
+    constexpr int kN = 4096;
+    constexpr int kPer = (kN + kFillMinThreads - 1) / kFillMinThreads;
+    uint4 e[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int i = static_cast<int>(threadIdx.x + k * blockDim.x);
         const int row = i >> 4;
-        const int h = (i >> 3) & 1;
-        const int j = row >> 4;
-        const int v = row & 15;
-        *reinterpret_cast<uint4*>(gh + i * 16) = __ldg(compact + (2 * j + h) * 16 + v);
+        e[k] = i < kN ? __ldg(compact + (2 * (row >> 4) + ((i >> 3) & 1)) * 16 + (row & 15))
+                      : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int i = static_cast<int>(threadIdx.x + k * blockDim.x);
+        if (i < kN) {
+            *reinterpret_cast<uint4*>(gh + i * 16) = e[k];
+        }
     }
 }
 

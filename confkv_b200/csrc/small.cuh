@@ -45,11 +45,8 @@ __device__ __forceinline__ const uint4* small_fold_table(const uint8_t* smem, co
 __device__ __forceinline__ void fill_small_fold(uint8_t* smem, const uint4* pow2)
 {
     uint4* ft = reinterpret_cast<uint4*>(smem + kSmallFold);
-    for (int i = threadIdx.x; i < 4 * 512; i += blockDim.x) {
-        const int k = i >> 9;  // slot k holds H^8, H^1, H^2, H^4
-        const int level = k == 0 ? 3 : k - 1;
-        ft[i] = __ldg(pow2 + level * 512 + (i & 511));
-    }
+    fill_smem<512>(ft, pow2 + 3 * 512);       // slot 0: H^8
+    fill_smem<3 * 512>(ft + 512, pow2);       // slots 1..3: H^1, H^2, H^4
 }
 
 // Fills all small-object tables above the AES region (open-CTR kernel).
