@@ -1,7 +1,7 @@
 /*
  * Native multi-threaded driver for the reference's OpenSSL backend
  * (lmcache_aes128gcm_seal / lmcache_aes128gcm_open from _ref/libcpu_seal.so).
- * TEST AND BASELINE INFRASTRUCTURE ONLY: bench.py's reference leg calls it to
+ * Test and CPU-reference-timing infrastructure only: bench.py's reference leg calls it to
  * time the CPU path on all host cores without a Python interpreter between
  * calls (small objects take microseconds, so a Python loop would time the
  * interpreter, not OpenSSL).
