@@ -21,7 +21,7 @@ OPEN_R = 2           # kOpenChains: rows per interior iteration of open_ghash_ro
 CTR_PAIR = 2
 BATCH_MAX_SMS = 256  # kBatchMaxSms
 CHUNKS_PER_SM = 4    # kChunksPerSm
-CHUNKS_PER_SM_FEW = 2  # kChunksPerSmFew
+CHUNKS_PER_SM_FEW = 1  # kChunksPerSmFew
 MIN_CHUNK_ROWS = 64  # kMinChunkRows
 MAX_CHUNKS = CHUNKS_PER_SM * BATCH_MAX_SMS
 SMALL_MAX_BLOCKS = 1024  # kSmallMaxBlocks

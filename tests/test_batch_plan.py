@@ -86,9 +86,9 @@ def test_chunks_cover_every_row_once(name, sms, mixed, open_):
 
 
 def test_chunk_counts():
-    # 32 x 32 MiB (few objects): two chunks per SM of 442-443 rows
+    # 32 x 32 MiB (few objects): one chunk per SM of 885-886 rows
     plan = chunk_plan([32 << 20] * 32, 148)
-    assert plan["R"] == 32 * 4096 and plan["M"] == 2 * 148
+    assert plan["R"] == 32 * 4096 and plan["M"] == 148
     # 4096 ragged objects (many): four chunks per SM
     assert chunk_plan(BATCHES["ragged4096"], 148)["M"] == 4 * 148
     # 64 x 2 MiB: one chunk per SM (110-111 rows), objects cut across chunks
