@@ -238,6 +238,20 @@ def test_batch_many_small_objects(gpu_lib, oracle):
             assert np.array_equal(frames[fr_off[i]:fr_off[i] + lens[i] + 29], expected[i]), (i, lens[i])
 
 
+def _plan_counts(batch):
+    """(tile objects, warp-path objects) of the last call, as the device plan
+    recorded them in the workspace header (BatchHeader: tile_objects at byte
+    20, small_count at byte 24)."""
+    h = batch.workspace[:32].cpu().numpy().view(np.uint32)
+    return int(h[5]), int(h[6])
+
+
+def _expected_counts(lens, routed):
+    blocks = [-(-int(n) // 16) for n in lens]
+    warp = sum(1 for n in blocks if n <= 1024 or (routed and n <= 2048))
+    return len(lens) - warp, warp
+
+
 @pytest.mark.parametrize("per_sm", [0, 10, 16])
 def test_batch_mid_objects_both_routes(gpu_lib, oracle, per_sm):
     """Objects of 1025..2048 blocks (16-32 KiB) take one warp each when the
@@ -273,6 +287,7 @@ def test_batch_mid_objects_both_routes(gpu_lib, oracle, per_sm):
         batch.seal(k, _seal_entries(d_plain, pt_off, d_frames, fr_off, lens, ivs), s)
         s.synchronize()
         assert int(batch.fault()) == 0 and not batch.statuses().any()
+        assert _plan_counts(batch) == _expected_counts(lens, routes[0])
         frames = d_frames.cpu().numpy()
         expected = oracle.evp_seal_many(key, ivs, pts)
         for i in range(len(lens)):
@@ -284,6 +299,7 @@ def test_batch_mid_objects_both_routes(gpu_lib, oracle, per_sm):
         batch.open(k, _open_entries(d_frames, fr_off, d_out, pt_off, lens, d_auth, range(len(lens))), s)
         s.synchronize()
         assert int(batch.fault()) == 0
+        assert _plan_counts(batch) == _expected_counts(lens, routes[1])
     auth = d_auth.cpu().numpy()
     out = d_out.cpu().numpy()
     for i in range(len(lens)):
