@@ -37,9 +37,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "AES-GCM seal/open GB/s (32 MiB KV objects) at 1/2/4/8 B200 vs OpenSSL host"
 UNIT = "GB/s"
-SHAPE = (2, 32, 256, 8, 128)
-OBJECTS = 32  # objects per GPU per step in the benchmarked workload
-SEED = 2
+SHAPE = (2, 32, 256, 8, 128)  # workloads.BENCH_SHAPE
+OBJECTS = 32  # objects per GPU per step in the benchmarked workload (workloads.BENCH_OBJECTS)
 WORKLOAD = "llama3_8b_kv_chunk_32MiB_x32_seal_then_open"
 
 
@@ -118,17 +117,14 @@ def run_ours(args, rank, world, local):
         torch.distributed.barrier()
     lib = GpuAesGcmLibrary()
 
-    P = workloads.nbytes_of(SHAPE)
-    frame_len = P + 29
-    stride = (frame_len + 255) // 256 * 256
-    key_bytes = workloads.make_key(SEED)
     nobj = args.objects
-    ivs = workloads.make_ivs(SEED * 100 + rank, nobj)
+    case = workloads.bench_case(rank, nobj, device=dev)  # this rank's objects, resident in HBM
+    P = case.object_bytes
+    frame_len = P + 29
+    stride = case.frame_stride
+    key_bytes, ivs, plain_u8 = case.key, case.ivs, case.plain
     key = GpuAes128GcmKey(lib, key_bytes, device=local)
     key.reserve(P)
-
-    plain = workloads.bf16_batch(SHAPE, nobj, seed=SEED * 100 + rank, device=dev)  # [n, ...] bf16
-    plain_u8 = plain.view(torch.uint8).reshape(nobj, P)
     frames = torch.empty((nobj, stride), dtype=torch.uint8, device=dev)
     opened = torch.empty((nobj, P), dtype=torch.uint8, device=dev)
     auth = torch.zeros((nobj,), dtype=torch.int32, device=dev)
@@ -195,7 +191,9 @@ def run_ours(args, rank, world, local):
     from confkv_b200 import multigpu
     from confkv_b200.clocks import ClockSampler
 
-    apis = ["batched", "per_object"] if args.api == "both" else [args.api]
+    # the headline call style is measured last, so `frames` holds its last
+    # timed step's output for the OpenSSL comparison below
+    apis = ["per_object", "batched"] if args.api == "both" else [args.api]
     clocks = ClockSampler(local)
     clocks.start()
     results = {}
@@ -206,6 +204,9 @@ def run_ours(args, rank, world, local):
                                                sum(open_ms)], device=dev)
         results[api] = (tot, ssum, osum, multigpu.all_ok(ok, device=dev))
     clk = clocks.stop()
+    frames_check = frames_match_openssl(frames, plain_u8, ivs, key_bytes, P)
+    frames_check["match"] = multigpu.all_ok(bool(frames_check["match"]), device=dev)
+    frames_check["api"] = apis[-1]
 
     # e2e through the public API: pinned host plaintext -> H2D -> seal -> D2H
     # frames, then open -> D2H auth flags; copies overlapped across objects.
@@ -214,7 +215,7 @@ def run_ours(args, rank, world, local):
     (e2e_ms, copy_ms) = multigpu.reduce_max([e2e["ms"], e2e.get("copy_ms", float("nan"))], device=dev)
 
     if rank == 0:
-        head = apis[0]
+        head = apis[-1]
         total_ms, seal_sum, open_sum, ok = results[head]
         bytes_per_step = 2 * nobj * P * world  # sealed + opened plaintext, all ranks
 
@@ -266,15 +267,14 @@ def run_ours(args, rank, world, local):
             "vs_baseline": None,
             "dtype": "u8",
             "data": "synthetic: bf16 N(0,1) KV chunks from fixed seeds, resident in HBM",
-            "config": {"workload": WORKLOAD, "objects_per_gpu": nobj, "object_shape": list(SHAPE),
-                       "object_bytes": P, "step": f"seal {nobj} objects then open {nobj} frames with tag check",
-                       "api": ("one seal_batch_async + one open_batch_async call per step" if head == "batched"
-                               else "one seal_async + one open_async call per object"),
-                       "l2": "inputs larger than L2 (1 GiB plaintext per GPU)",
-                       "parallelism": f"independent objects per GPU x{world}, no collective"},
+            "config": bench_config(nobj, P, world),
+            "api": ("one seal_batch_async + one open_batch_async call per step" if head == "batched"
+                    else "one seal_async + one open_async call per object"),
             "seal_gbs": round(gbs(seal_sum, nobj * P * world), 2),
             "open_gbs": round(gbs(open_sum, nobj * P * world), 2),
             "round_trip_ok": ok,
+            "frames_match_openssl": frames_check["match"],
+            "frames_check": frames_check,
             "roofline": {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -312,13 +312,44 @@ def run_ours(args, rank, world, local):
                                   "round_trip_ok": okp, "gpu_launches": 3 * nobj * args.steps,
                                   "api": "one seal_async + one open_async call per object (reference C-ABI)"}
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(args)
+            line["cpu_baseline"] = cpu_baseline(args, plain_u8, key_bytes)
         print(json.dumps(line), flush=True)
 
     key.close()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def bench_config(nobj: int, P: int, world: int) -> dict:
+    """The workload, identical in both arms' JSON lines."""
+    return {"workload": WORKLOAD, "objects_per_gpu": nobj, "object_shape": list(SHAPE), "object_bytes": P,
+            "step": f"seal {nobj} objects then open {nobj} frames with tag check (per GPU)",
+            "l2": "inputs larger than L2 (1 GiB plaintext per GPU)",
+            "parallelism": f"independent objects per GPU x{world}, no collective"}
+
+
+def frames_match_openssl(frames, plain_u8, ivs, key: bytes, P: int) -> dict:
+    """SHA-256 of each object's frame as the GPU wrote it against that of the
+    frame OpenSSL writes for the same key, IV and plaintext (pyca
+    `cryptography` AESGCM, stock LMCache's call: 0x01 + IV +
+    encrypt(IV, P, None)). Runs after the timed steps."""
+    import hashlib
+
+    try:
+        from cryptography.hazmat.primitives.ciphers.aead import AESGCM
+    except ImportError as exc:
+        return {"match": False, "error": f"pyca cryptography unavailable: {exc}"}
+    aes = AESGCM(key)
+    host_plain = plain_u8.cpu().numpy()
+    host_frames = frames[:, :P + 29].cpu().numpy()
+    bad = []
+    for k in range(host_plain.shape[0]):
+        want = hashlib.sha256(b"\x01" + ivs[k] + aes.encrypt(ivs[k], host_plain[k].tobytes(), None)).digest()
+        if hashlib.sha256(host_frames[k].tobytes()).digest() != want:
+            bad.append(k)
+    return {"match": not bad, "objects": int(host_plain.shape[0]), "mismatched": bad,
+            "how": "sha256 of each GPU frame vs pyca AESGCM (OpenSSL) frame for the same key, IV, plaintext"}
 
 
 def run_e2e(torch, key, plain_u8, ivs, P, stride, dev, args, barrier):
@@ -434,7 +465,43 @@ def load_ref_lib():
     dp = ctypes.POINTER(ctypes.c_double)
     lib.cpu_threads_sweep.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_long, dp, dp]
     lib.cpu_threads_sweep.restype = ctypes.c_int
+    vpp = ctypes.POINTER(ctypes.c_void_p)
+    lib.cpu_threads_objects.argtypes = [ctypes.c_void_p, vpp, vpp, vpp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int,
+                                        dp, dp]
+    lib.cpu_threads_objects.restype = ctypes.c_int
     return lib
+
+
+class HostObjects:
+    """Distinct objects in host memory, each with its own frame and output
+    buffer, for the reference backend's native thread driver."""
+
+    def __init__(self, objs):
+        import numpy as np
+
+        self.objs = np.ascontiguousarray(objs)            # [count, P] uint8
+        count, P = self.objs.shape
+        self.P, self.count = int(P), int(count)
+        self.frames = np.empty((count, P + 29), dtype=np.uint8)
+        self.outs = np.empty((count, P), dtype=np.uint8)
+        arr = ctypes.c_void_p * count
+        self._src = arr(*[self.objs[k].ctypes.data for k in range(count)])
+        self._fr = arr(*[self.frames[k].ctypes.data for k in range(count)])
+        self._out = arr(*[self.outs[k].ctypes.data for k in range(count)])
+        # touch every page before anything is timed
+        self.frames.fill(0)
+        self.outs.fill(0)
+
+    def run(self, lib, key: bytes, threads: int) -> tuple[float, float]:
+        """Seal every object, then open every frame (reference
+        lmcache_aes128gcm_seal/open, object k on thread k mod threads);
+        returns the wall seconds of the seal leg and of the open leg."""
+        ts, to = ctypes.c_double(), ctypes.c_double()
+        kb = (ctypes.c_uint8 * 16).from_buffer_copy(key)
+        rc = lib.cpu_threads_objects(kb, self._src, self._fr, self._out, self.P, self.count, threads,
+                                     ctypes.byref(ts), ctypes.byref(to))
+        assert rc == 0, "reference backend failed or a round trip differed"
+        return ts.value, to.value
 
 
 def openssl_threads_run(lib, key: bytes, per: int, threads: int, P: int) -> tuple[float, float]:
@@ -448,22 +515,23 @@ def openssl_threads_run(lib, key: bytes, per: int, threads: int, P: int) -> tupl
     return ts.value, to.value
 
 
-def cpu_baseline(args) -> dict:
+def cpu_baseline(args, plain_u8, key: bytes) -> dict:
+    """The reference OpenSSL backend on all host threads, sealing then
+    opening this rank's objects (copied to host memory), once: a bounded
+    sample of the step (1 GiB each way at the default 32 objects)."""
     lib = load_ref_lib()
     if lib is None:
         return {"unavailable": "oracle/_ref/libcpu_threads.so missing"}
-    from confkv_b200 import workloads
-
-    P = workloads.nbytes_of(SHAPE)
     threads = len(os.sched_getaffinity(0))
-    per = args.cpu_sample_objects or max(1, 64 // threads)
-    key = workloads.make_key(SEED)
-    openssl_threads_run(lib, key, 1, threads, P)  # warm-up: page-in buffers
-    ts, to = openssl_threads_run(lib, key, per, threads, P)
-    gbs = 2 * per * threads * P / (ts + to) / 1e9
+    count = plain_u8.shape[0] if not args.cpu_sample_objects else min(args.cpu_sample_objects, plain_u8.shape[0])
+    host = HostObjects(plain_u8[:count].cpu().numpy())
+    host.run(lib, key, threads)  # warm-up: caches, page tables
+    ts, to = host.run(lib, key, threads)
+    gbs = 2 * host.count * host.P / (ts + to) / 1e9
     return {"value": round(gbs, 2), "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": f"{per} x 32 MiB object(s) sealed then opened per thread, {threads} native threads, "
-                      f"reference lmcache_aes128gcm_seal/open (OpenSSL EVP)"}
+            "sample": f"the step's {host.count} objects of {host.P} B (bf16 KV, same bytes as the GPU run) sealed "
+                      f"then opened once on {threads} native threads, reference lmcache_aes128gcm_seal/open "
+                      f"(OpenSSL EVP)"}
 
 
 def cpu_sweep_sizes(lib, key: bytes, threads: int) -> None:
@@ -484,35 +552,48 @@ def cpu_sweep_sizes(lib, key: bytes, threads: int) -> None:
 
 
 def run_reference(args, rank, world):
+    """The reference's OpenSSL CPU backend on this host's cores, over the
+    same objects the GPU run seals: every rank's 32 bf16 KV objects (the whole
+    job of `world` GPUs), each in its own host buffer, sealed then opened per
+    step. Objects are drawn with torch's CUDA generator like the GPU run's
+    (then copied to host memory) when a GPU is present."""
     if rank != 0:
         return
     lib = load_ref_lib()
     if lib is None:
         print(json.dumps({"impl": "reference", "unavailable": "reference OpenSSL backend could not be built"}))
         return
+    import numpy as np
+    import torch
+
     from confkv_b200 import workloads
 
-    P = workloads.nbytes_of(SHAPE)
+    draw = "cuda" if torch.cuda.is_available() else "cpu"
+    cases = [workloads.bench_case(r, args.objects, device=draw) for r in range(world)]
+    objs = np.concatenate([c.plain.cpu().numpy() for c in cases])
+    del cases
+    if draw == "cuda":
+        torch.cuda.empty_cache()
+    key = workloads.make_key(workloads.BENCH_SEED)
+    host = HostObjects(objs)
+    del objs
     threads = len(os.sched_getaffinity(0))
-    key = workloads.make_key(SEED)
-    # each step: the 32 objects x world ranks, spread over all host threads
-    total_objects = OBJECTS * world
-    per = max(1, -(-total_objects // threads))
     for _ in range(args.warmup):
-        openssl_threads_run(lib, key, per, threads, P)
-    times = [sum(openssl_threads_run(lib, key, per, threads, P)) for _ in range(args.steps)]
-    objs_done = per * threads
+        host.run(lib, key, threads)
+    times = [sum(host.run(lib, key, threads)) for _ in range(args.steps)]
     ms = statistics.mean(times) * 1e3
-    value = 2 * objs_done * P / (ms * 1e-3) / 1e9
+    value = 2 * host.count * host.P / (ms * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u8", "data": "synthetic: random bytes, 32 MiB host buffers",
-        "config": {"workload": WORKLOAD, "objects_per_step": objs_done, "object_bytes": P,
-                   "step": "seal then open each object on native host threads"},
+        "vs_baseline": None, "dtype": "u8",
+        "data": f"synthetic: the GPU run's bf16 N(0,1) KV objects (drawn on {draw}), one host buffer each",
+        "config": bench_config(args.objects, host.P, world),
         "impl": "reference",
+        "api": "reference lmcache_aes128gcm_seal / lmcache_aes128gcm_open, one call per object, native threads",
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": f"{objs_done} x 32 MiB objects per step over {threads} native threads"},
+                         "sample": f"all {host.count} objects of the step ({world} GPU(s) x {args.objects}) "
+                                   f"sealed then opened, object k on thread k mod {threads}"},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

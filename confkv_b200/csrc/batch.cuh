@@ -395,6 +395,10 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
             const bool small = ok && n <= kSmallMaxBlocks;
             rows = ok && !small ? static_cast<uint32_t>((n + T - 1) / T) : 0u;
             items[i].status = ok ? 0 : -1;
+            if (open && !ok && has_auth) {
+                // a rejected open never leaves an earlier call's verdict behind
+                *reinterpret_cast<int*>((static_cast<unsigned long long>(cur[2].y) << 32) | cur[2].x) = 0;
+            }
             if (rows != 0) {
                 int v;
                 uint32_t r;

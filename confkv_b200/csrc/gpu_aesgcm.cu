@@ -642,37 +642,96 @@ extern "C" int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, co
 // needs beyond its input and output -- the key's GHASH tables, the AES
 // T-tables and the call's accumulation slot -- in one file-scope __device__
 // array that every GPU loading this library holds until process exit.
+//
+// Which key's tables the array holds is decided on the device, in stream
+// order: every call launches noalloc_prepare_kernel with H = E_K(0^128),
+// which compares H with the record kept beside each table and rebuilds only
+// the tables built for another key; the seal kernel follows it on the stream.
+// The host keeps no key material between calls.
 namespace {
 
 constexpr int kNoAllocPow2Tables = 28;  // H^(2^k), k < 28: exponents of objects up to 1 GiB
 constexpr size_t kNoAllocAesBytes = 4 * 256 * sizeof(uint32_t);
 constexpr size_t kNoAllocTableBytes =
     kNoAllocAesBytes + static_cast<size_t>(kNoAllocPow2Tables) * confkv::kGhashTableBytes;
-constexpr size_t kNoAllocSlotOffset = (kNoAllocTableBytes + 255) / 256 * 256;
+constexpr size_t kNoAllocRecordOffset = kNoAllocTableBytes;  // 32 B per table: {H, valid word}
+constexpr size_t kNoAllocSlotOffset = (kNoAllocRecordOffset + 32 * kNoAllocPow2Tables + 255) / 256 * 256;
 constexpr size_t kNoAllocScratchBytes = kNoAllocSlotOffset + 256;
 constexpr uint64_t kNoAllocMaxPlaintext = 1ull << 30;
+constexpr uint32_t kNoAllocRecordValid = 0x48746162u;
 
 static_assert(dev::kSealChainLog2 < kNoAllocPow2Tables, "chain multiplier table must be in the scratch");
 
-// The shared scratch array (228 KiB + 256 B per device).
+// The shared scratch array (229,376 B + 1,024 B of table records and slot per device).
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// One warp per GHASH table t (H^(2^t)), one CTA. A warp whose record names
+// `h` leaves its table alone; otherwise it forms H^(2^t) by t squarings,
+// rebuilds the 4-bit table (lane L holds U_L = H^(2^t) x^(4L) and writes the
+// 16 entries of nibble position L ^ 1, see ghash_table in host_crypto.cpp)
+// and then rewrites the record. Warp 0 also clears the accumulation slot.
+__global__ void __launch_bounds__(32 * kNoAllocPow2Tables) noalloc_prepare_kernel(uint8_t* scratch, const uint4 h)
+{
+    const int lane = static_cast<int>(threadIdx.x & 31u);
+    const int t = static_cast<int>(threadIdx.x >> 5);
+    if (threadIdx.x == 0) {
+        auto* slot = reinterpret_cast<dev::Slot*>(scratch + kNoAllocSlotOffset);
+        slot->acc_hi = 0;
+        slot->acc_lo = 0;
+        slot->ticket = 0;
+    }
+    uint4* rec = reinterpret_cast<uint4*>(scratch + kNoAllocRecordOffset + 32 * static_cast<size_t>(t));
+    const uint4 have = rec[0];
+    if (rec[1].x == kNoAllocRecordValid && have.x == h.x && have.y == h.y && have.z == h.z && have.w == h.w) {
+        return;
+    }
+    uint4 m = h;
+    for (int k = 0; k < t; ++k) {
+        unsigned long long uhi, ulo, rhi, rlo;
+        dev::warp_lane_basis(m, lane, uhi, ulo);
+        dev::warp_generic_mul(m, uhi, ulo, lane, rhi, rlo);
+        m = dev::be_to_raw(rhi, rlo);
+    }
+    unsigned long long bh[4], bl[4];  // B_c = U_L x^(3-c): the product for nibble bit c
+    dev::warp_lane_basis(m, lane, bh[3], bl[3]);
+    for (int c = 2; c >= 0; --c) {
+        bh[c] = bh[c + 1];
+        bl[c] = bl[c + 1];
+        dev::gf_mul_x(bh[c], bl[c]);
+    }
+    uint4* tab = reinterpret_cast<uint4*>(scratch + kNoAllocAesBytes + static_cast<size_t>(t) * confkv::kGhashTableBytes) +
+                 16 * (lane ^ 1);
+    for (int v = 0; v < 16; ++v) {
+        unsigned long long eh = 0, el = 0;
+        for (int c = 0; c < 4; ++c) {
+            if ((v >> c) & 1) {
+                eh ^= bh[c];
+                el ^= bl[c];
+            }
+        }
+        tab[v] = dev::be_to_raw(eh, el);
+    }
+    __syncwarp();
+    if (lane == 0) {
+        rec[0] = h;
+        rec[1] = make_uint4(kNoAllocRecordValid, 0u, 0u, 0u);
+    }
+}
 
 struct NoAllocDevice {
     std::once_flag once;
     int status = LMCACHE_GPU_AESGCM_OK;
     uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
     int num_sms = 0;
-    bool have_key = false;
-    uint8_t key[16] = {0};
+    std::mutex mu;               // keeps a call's prepare and seal launches adjacent on a stream
 };
 
 NoAllocDevice g_noalloc_dev[kMaxDevices];
-std::mutex g_noalloc_mu;                       // guards the staging buffer and key caches
-uint8_t g_noalloc_staging[kNoAllocTableBytes];  // host image of the scratch tables
 
 // Once per device, with that device current: resolve the array's device
-// address, opt the seal kernels into their shared memory and check the
-// shared-memory layout with the probe kernel writing into the array.
+// address, opt the seal kernels into their shared memory, copy in the
+// key-independent AES T-tables and check the shared-memory layout with the
+// probe kernel writing into the array. Synchronous; allocates nothing.
 int noalloc_setup(int device, NoAllocDevice& st)
 {
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&st.scratch), g_noalloc_scratch) != cudaSuccess ||
@@ -702,6 +761,11 @@ int noalloc_setup(int device, NoAllocDevice& st)
     if (e != cudaSuccess) {
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
     }
+    uint32_t aes_t[4][256];
+    confkv::aes_t_tables(aes_t);
+    if (cudaMemcpy(st.scratch, aes_t, kNoAllocAesBytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
     unsigned int* probe = reinterpret_cast<unsigned int*>(st.scratch + kNoAllocSlotOffset + 128);
     dev::smem_base_probe_kernel<<<1, 32, 1024>>>(probe);
     unsigned int base = 0;
@@ -710,6 +774,16 @@ int noalloc_setup(int device, NoAllocDevice& st)
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
     }
     return base == dev::kDynSmemBase ? LMCACHE_GPU_AESGCM_OK : LMCACHE_GPU_AESGCM_ERR_INTERNAL;
+}
+
+// Plain (not programmatic) launch: the kernel starts only after everything
+// before it on the stream, the prepare kernel's table writes included, has
+// completed.
+template <int SQ, bool A>
+cudaError_t launch_seal_plain(const dev::SealArgs& args, cudaStream_t s)
+{
+    dev::seal_kernel<SQ, A><<<args.grid, dev::kSealThreads, dev::kSealSmem, s>>>(args);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -753,44 +827,22 @@ extern "C" int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key
     args.kt.gh_pow2 = reinterpret_cast<const uint4*>(st.scratch + kNoAllocAesBytes);
     args.slot = reinterpret_cast<dev::Slot*>(st.scratch + kNoAllocSlotOffset);
 
-    {
-        // Upload the key's tables unless this device already holds them. The
-        // copy is ordered on `stream`; from pageable memory it returns once
-        // the source has been consumed, so the staging buffer is free again.
-        std::lock_guard<std::mutex> lock(g_noalloc_mu);
-        if (!st.have_key || std::memcmp(st.key, key, 16) != 0) {
-            uint8_t zero[16] = {0};
-            uint8_t hbytes[16];
-            confkv::aes128_encrypt_block(args.rk, zero, hbytes);
-            confkv::aes_t_tables(reinterpret_cast<uint32_t(*)[256]>(g_noalloc_staging));
-            confkv::Gf128 p = confkv::gf_load(hbytes);
-            for (int k = 0; k < kNoAllocPow2Tables; ++k) {
-                confkv::ghash_table(p, g_noalloc_staging + kNoAllocAesBytes +
-                                           static_cast<size_t>(k) * confkv::kGhashTableBytes);
-                p = confkv::gf_mul(p, p);
-            }
-            if (cudaMemcpyAsync(st.scratch, g_noalloc_staging, kNoAllocTableBytes, cudaMemcpyHostToDevice, s) !=
-                cudaSuccess) {
-                st.have_key = false;
-                return LMCACHE_GPU_AESGCM_ERR_CUDA;
-            }
-            std::memcpy(st.key, key, 16);
-            st.have_key = true;
-        }
-    }
-
     cudaError_t e;
     if (n == 0) {
+        // header + E_K(J0): reads only the key-independent T-tables
         args.grid = 1;
         dev::seal_empty_kernel<<<1, 32, 0, s>>>(args);
         e = cudaGetLastError();
         std::memset(args.rk, 0, sizeof(args.rk));
         return cuda_rc(e);
     }
-    // The slot must start at zero; it keeps whatever the previous call left.
-    if (cudaMemsetAsync(args.slot, 0, sizeof(dev::Slot), s) != cudaSuccess) {
-        return LMCACHE_GPU_AESGCM_ERR_CUDA;
-    }
+    uint8_t zero[16] = {0};
+    uint8_t hbytes[16];
+    confkv::aes128_encrypt_block(args.rk, zero, hbytes);
+    uint4 h;
+    std::memcpy(&h, hbytes, 16);
+    std::memset(hbytes, 0, sizeof(hbytes));
+
     horner_grid(n, st.num_sms, args.iters, args.grid);
     const uintptr_t ct = reinterpret_cast<uintptr_t>(dst) + 13u;
     const uint32_t off = static_cast<uint32_t>(ct & 15u);
@@ -801,23 +853,34 @@ extern "C" int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key
         sq = static_cast<int>(sh >> 2);
         args.store_r = sh & 3u;
     }
-    if (pt_aligned) {
-        switch (sq) {
-        case 0: e = launch_seal_t<0, true>(args, s); break;
-        case 1: e = launch_seal_t<1, true>(args, s); break;
-        case 2: e = launch_seal_t<2, true>(args, s); break;
-        case 3: e = launch_seal_t<3, true>(args, s); break;
-        default: e = launch_seal_t<4, true>(args, s); break;
-        }
-    } else {
-        switch (sq) {
-        case 0: e = launch_seal_t<0, false>(args, s); break;
-        case 1: e = launch_seal_t<1, false>(args, s); break;
-        case 2: e = launch_seal_t<2, false>(args, s); break;
-        case 3: e = launch_seal_t<3, false>(args, s); break;
-        default: e = launch_seal_t<4, false>(args, s); break;
+    {
+        // Two host threads sharing a stream must not interleave their
+        // prepare and seal launches (the second prepare would swap the tables
+        // under the first seal).
+        std::lock_guard<std::mutex> lock(st.mu);
+        noalloc_prepare_kernel<<<1, 32 * kNoAllocPow2Tables, 0, s>>>(st.scratch, h);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) {
+            if (pt_aligned) {
+                switch (sq) {
+                case 0: e = launch_seal_plain<0, true>(args, s); break;
+                case 1: e = launch_seal_plain<1, true>(args, s); break;
+                case 2: e = launch_seal_plain<2, true>(args, s); break;
+                case 3: e = launch_seal_plain<3, true>(args, s); break;
+                default: e = launch_seal_plain<4, true>(args, s); break;
+                }
+            } else {
+                switch (sq) {
+                case 0: e = launch_seal_plain<0, false>(args, s); break;
+                case 1: e = launch_seal_plain<1, false>(args, s); break;
+                case 2: e = launch_seal_plain<2, false>(args, s); break;
+                case 3: e = launch_seal_plain<3, false>(args, s); break;
+                default: e = launch_seal_plain<4, false>(args, s); break;
+                }
+            }
         }
     }
+    std::memset(&h, 0, sizeof(h));
     std::memset(args.rk, 0, sizeof(args.rk));
     return cuda_rc(e);
 }

@@ -63,6 +63,38 @@ def bf16_batch(shape, count: int, seed: int, device="cpu"):
     return torch.randn((count, *shape), generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
 
 
+# The benchmarked workload (Llama-3-8B KV chunks): per rank, 32 objects
+# [2, 32, 256, 8, 128] bf16 (32 MiB each) under one key, each with its own IV;
+# frames laid out at a 256-byte stride (the ciphertext at frame + 13).
+BENCH_SHAPE = SHAPES["kv_llama8b"]
+BENCH_OBJECTS = 32
+BENCH_SEED = 2
+
+
+@dataclass
+class BenchCase:
+    key: bytes
+    ivs: list                  # 12-byte IVs, one per object
+    plain: object              # torch uint8 [count, P] on the device it was drawn on
+    object_bytes: int
+    frame_stride: int
+
+
+def bench_case(rank: int = 0, count: int = BENCH_OBJECTS, device="cuda") -> BenchCase:
+    """The inputs rank `rank` seals in the benchmark: the key is shared by all
+    ranks, the objects and IVs are the rank's own. The objects are drawn with
+    torch's generator on `device` (CUDA draws differ from CPU draws for the
+    same seed), so a host-side consumer that wants the GPU run's bytes draws
+    them on a GPU and copies them to the host."""
+    import torch
+
+    P = nbytes_of(BENCH_SHAPE)
+    plain = bf16_batch(BENCH_SHAPE, count, seed=BENCH_SEED * 100 + rank, device=device).view(torch.uint8)
+    plain = plain.reshape(count, P)
+    return BenchCase(key=make_key(BENCH_SEED), ivs=make_ivs(BENCH_SEED * 100 + rank, count), plain=plain,
+                     object_bytes=P, frame_stride=(P + 29 + 255) // 256 * 256)
+
+
 @dataclass
 class RaggedCase:
     lengths: np.ndarray        # plaintext bytes per object

@@ -97,18 +97,25 @@ int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, const void* s
  * take cudaMalloc's implicit device synchronisation). It takes the raw
  * 16-byte key instead of a handle, runs on `device`, and writes the same
  * frame as lmcache_gpu_aes128gcm_seal_async. Its only working memory is one
- * file-scope __device__ array of 233,728 bytes that every GPU loading this
+ * file-scope __device__ array of 234,752 bytes that every GPU loading this
  * library holds until the process exits; it calls no cudaMalloc or cudaFree.
  *
  * - plaintext_len above 1 GiB (2^30 bytes) -> ERR_ARGUMENT (the array holds
  *   GHASH tables for objects up to that size); other argument rules as seal.
  * - The first call on a device sets up that device (resolves the array's
- *   address, opts the kernels into their shared memory, checks the layout);
- *   make that first call before any stream capture.
- * - All calls share the array: it keeps the last call's key tables (a new
- *   key uploads new ones, in stream order) and the accumulation slot, which
- *   each call clears. Calls whose work overlaps on the GPU race on it;
- *   issue them on one stream or wait for the previous call.
+ *   address, opts the kernels into their shared memory, copies in the AES
+ *   tables, checks the layout) and waits for it; make that first call before
+ *   any stream capture.
+ * - All calls share the array. Each call enqueues a small kernel ahead of
+ *   the seal that compares the key's H = E_K(0^128) with the one the array's
+ *   GHASH tables were built for and rebuilds them on a mismatch, and clears
+ *   the accumulation slot, all in stream order. The host keeps no key
+ *   material between calls; the array keeps the last key's GHASH tables (and
+ *   that H) until another key replaces them or the process exits.
+ * - Calls from several host threads on one stream are safe (each call's two
+ *   launches stay adjacent). Calls whose work overlaps on the GPU (other
+ *   streams, unordered) race on the array; issue them on one stream or wait
+ *   for the previous call.
  */
 int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key_len, const void* src,
                                        size_t plaintext_len, void* dst, size_t dst_capacity,
@@ -125,8 +132,10 @@ int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key_len, const
  *
  * items: DEVICE array of `count` descriptors, 16-byte aligned. The device
  *   checks each descriptor by the rules of seal_async / open_async and writes
- *   its `status`: 0, or ERR_ARGUMENT, in which case that object is skipped
- *   (nothing of it is written, its auth_ok included).
+ *   its `status`: 0, or ERR_ARGUMENT, in which case that object is skipped:
+ *   nothing of it is written, except that a rejected open descriptor with a
+ *   non-null auth_ok gets *auth_ok = 0 (so a reused verdict buffer never
+ *   keeps an earlier call's 1 next to an unwritten dst).
  * workspace: DEVICE buffer, 16-byte aligned, at least
  *   lmcache_gpu_aes128gcm_batch_workspace_size(count) bytes, any contents; the
  *   call owns it until its work on `stream` completes (one call at a time).

@@ -208,7 +208,8 @@ def test_batch_invalid_descriptors_are_skipped(gpu_lib):
         s.synchronize()
         assert int(batch.fault()) == 0
         assert batch.statuses().cpu().tolist() == [0, -1, -1, 0]
-    assert d_auth.cpu().tolist() == [1, 7, 7, 1]
+    # the rejected descriptor with an auth_ok pointer gets 0, not the stale 7
+    assert d_auth.cpu().tolist() == [1, 7, 0, 1]
     out = d_out.cpu().numpy()
     assert (out[n:3 * n] == 0xCC).all()
     pl = d_plain[:n].cpu().numpy()
