@@ -21,7 +21,7 @@ LIB_NAME = "libgpu_aesgcm.so"
 LIB_PATH = PKG / LIB_NAME
 
 SOURCES = [CSRC / "gpu_aesgcm.cu", CSRC / "batch.cu", CSRC / "host_crypto.cpp"]
-HEADERS = [CSRC / "kernels.cuh", CSRC / "tiles.cuh", CSRC / "batch.cuh", CSRC / "small.cuh", CSRC / "host_common.h",
+HEADERS = [CSRC / "kernels.cuh", CSRC / "clmul.cuh", CSRC / "tiles.cuh", CSRC / "batch.cuh", CSRC / "small.cuh", CSRC / "host_common.h",
            CSRC / "host_crypto.h", INCLUDE / "gpu_aesgcm_api.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -42,6 +42,24 @@ def needs_build() -> bool:
 def _compile_cmd(src: Path, obj: Path, verbose: bool) -> list[str]:
     return [nvcc(), "-O3", "-std=c++17", "-lineinfo", "-c", "-Xcompiler=-fPIC", *ARCH_FLAGS,
             "-I", str(INCLUDE), "-I", str(CSRC), *(["-Xptxas", "-v"] if verbose else []), str(src), "-o", str(obj)]
+
+
+PIPE_RATES_SRC = CSRC / "pipe_rates.cu"
+PIPE_RATES_LIB = PKG / "libpipe_rates.so"
+
+
+def build_pipe_rates(force: bool = False) -> Path:
+    """The issue-rate microbenchmark (csrc/pipe_rates.cu) as its own shared
+    library: a measurement tool, not part of the seal/open C-ABI."""
+    if not force and PIPE_RATES_LIB.exists() and PIPE_RATES_LIB.stat().st_mtime >= PIPE_RATES_SRC.stat().st_mtime:
+        return PIPE_RATES_LIB
+    cmd = [nvcc(), "-O3", "-std=c++17", "-lineinfo", "--shared", "-Xcompiler=-fPIC", *ARCH_FLAGS,
+           str(PIPE_RATES_SRC), "-o", str(PIPE_RATES_LIB) + ".tmp"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"pipe_rates build failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(str(PIPE_RATES_LIB) + ".tmp", PIPE_RATES_LIB)
+    return PIPE_RATES_LIB
 
 
 def build(verbose: bool = False, force: bool = False) -> Path:
@@ -74,3 +92,4 @@ def build(verbose: bool = False, force: bool = False) -> Path:
 
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv, force=True))
+    print(build_pipe_rates(force=True))

@@ -84,6 +84,7 @@ int batch_launch(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* it
     ba.wait_ns = ba.stall != 0u ? kInjectedWaitNs : dev::kWaitLimitNs;
     std::memcpy(ba.rk, h->rk, sizeof(ba.rk));
     ba.kt = h->kt;
+    ba.open_cm = h->open_cm;
     const uint32_t grid = static_cast<uint32_t>(h->num_sms);
     int rc;
     if (!open) {

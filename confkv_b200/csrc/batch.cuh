@@ -203,6 +203,7 @@ struct BatchArgs {
     unsigned long long wait_ns;
     uint32_t rk[44];
     KeyTables kt;
+    ClmulConst open_cm;  // the batched open's chain multiplier H^(4 T) for its integer-pipe chains
 };
 
 // Ciphertext store class of a frame: sq = word part of 16 - (ct & 15)
@@ -1109,7 +1110,8 @@ __device__ __forceinline__ bool open_ghash_class(uint8_t* smem, const BatchArgs&
             (void)lq;
             const OpenTile t{frame, it->capacity, P, segment_base(sg, P), static_cast<int64_t>(sg.r1 - sg.r0),
                              load_r};
-            q = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), c.tid, c.lane);
+            q = open_ghash_rows<LQ, kOpenBatchChains, kOpenBatchAluChains, kOpenBatchStepRows>(
+                t, reinterpret_cast<const uint4*>(smem + kOpenHt), &a.open_cm, c.tid, c.lane);
         }
         const bool chunk_done = *walk_word(ws, 1) == kChunkEnd;
         uint32_t taken = 0;
@@ -1173,7 +1175,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const
     extern __shared__ __align__(16) uint8_t smem[];
     const int tid = threadIdx.x;
     pdl_release();
-    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
+    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenBatchChainLog2 * 512);
     fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kOpenFold), a.kt.gh_pow2);
     const Handoff h = handoff_at(smem, kOpenBatchHandoff, kOpenBatchSync);
     if (tid == 0) {

@@ -165,7 +165,8 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
         const OpenTile t{a.frame, a.frame_len, P,
                          static_cast<int64_t>(a.nblocks) - static_cast<int64_t>(a.grid - blockIdx.x) * span,
                          static_cast<int64_t>(a.iters), a.load_r};
-        const uint4 q = open_ghash_rows<LQ>(t, reinterpret_cast<const uint4*>(smem + kOpenHt), tid, lane);
+        const uint4 q = open_ghash_rows<LQ, kOpenChains, 0, kOpenChains>(t, reinterpret_cast<const uint4*>(smem + kOpenHt),
+                                                                        nullptr, tid, lane);
         const uint4 v = warp_fold_pairs<false>(q, fold_tabs, lane);
         if (lane < 2) {
             part[2 * warp + lane] = v;
@@ -424,6 +425,14 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
     Gf128 p = H;
     for (int k = 0; k < confkv::kPow2Tables; ++k) {
         confkv::ghash_table(p, host + off_pow2 + kTab * k);
+        if (k == dev::kOpenBatchChainLog2) {
+            // the batched open's chain multiplier, for its integer-pipe chains
+            uint8_t pb[16];
+            uint32_t pw[4];
+            confkv::gf_store(pb, p);
+            std::memcpy(pw, pb, 16);
+            h->open_cm = confkv::clmul_prepare(pw);
+        }
         p = confkv::gf_mul(p, p);
     }
 

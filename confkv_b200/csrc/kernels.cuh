@@ -10,6 +10,8 @@
 
 #include <cstdint>
 
+#include "clmul.cuh"
+
 namespace confkv {
 namespace dev {
 
@@ -18,8 +20,23 @@ constexpr int kHornerLog2 = 9;                      // log2(kHornerThreads)
 constexpr int kFoldLevels = kHornerLog2;
 constexpr int kSealChains = 1;                      // GHASH chains per thread in seal
 constexpr int kSealChainLog2 = kHornerLog2;         // chain multiplier H^kHornerThreads
-constexpr int kOpenChains = 2;                      // GHASH chains per thread in open
+constexpr int kOpenChains = 2;                      // GHASH chains per thread in the per-object open
 constexpr int kOpenChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * kHornerThreads)
+// The batched open's GHASH pass runs four chains per thread (multiplier
+// H^(4 T)); the last kOpenBatchAluChains of them multiply on the integer
+// pipes (clmul.cuh) instead of the shared-memory tables, so the two share
+// the GHASH work. A table multiply costs 4 shared-memory wavefronts per
+// block and ~110 ALU instructions, an integer-pipe multiply ~310 ALU and
+// ~150 FMA-pipe instructions: with one chain in four on the integer pipes
+// neither unit exceeds the shared-memory pipe's rate (measured on B200, 32 x
+// 32 MiB: 502 -> 549 GB/s; one in two, or two in four, ran slower than tables
+// alone). The per-object open keeps two table chains: its tiles are a few
+// dozen rows, where four chains cost more in the edge rows and the combine
+// than they gain.
+constexpr int kOpenBatchChains = 4;
+constexpr int kOpenBatchChainLog2 = kHornerLog2 + 2;
+constexpr int kOpenBatchAluChains = 1;
+constexpr int kOpenBatchStepRows = 1;               // interior rows read (and prefetched) at a time
 constexpr int kPowerWarp = kHornerThreads / 32;     // warp index of the power warp
 constexpr int kSealThreads = kHornerThreads + 32;
 constexpr int kCtrThreads = 512;

@@ -267,14 +267,20 @@ struct OpenTile {
 };
 
 // Row warps of an open-GHASH tile: the thread's GHASH share over the
-// ciphertext at frame + 13 with kOpenChains chains (multiplier H^(2T) in the
-// replicated table at kOpenGh), combined with the compact H^T table `ht`.
-// Interior rows hold blocks 1 <= i < P/16, so both aligned chunks of every
-// block lie inside the frame and no checks are needed.
-template <int LQ>
-__device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4* ht, int tid, int lane)
+// ciphertext at frame + 13 with R chains (multiplier M = H^(R T)), combined
+// with the compact H^T table `ht`. In the interior rows chains
+// k < R - NALU multiply with the replicated table of M at kOpenGh
+// (shared-memory pipe) and the others with clmul (integer pipes, M's
+// operands `cm` read from the kernel parameters), keeping their value in
+// clmul's integer domain until the interior rows end; S interior rows are
+// read at a time, the next S prefetched. Edge rows use the table for every
+// chain. Interior rows hold blocks 1 <= i < P/16, so both aligned chunks of
+// every block lie inside the frame and no checks are needed.
+template <int LQ, int R, int NALU, int S>
+__device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4* ht, const ClmulConst* cm, int tid,
+                                                 int lane)
 {
-    constexpr int R = kOpenChains;
+    constexpr int kTabChains = R - NALU;
     const uint32_t lb_lo = static_cast<uint32_t>(lane & 7) << 4;
     const uint32_t lb_hi = 0x80u | lb_lo;
     const uint32_t fsel = funnel_sel(t.load_r);
@@ -309,39 +315,69 @@ __device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4*
         generic_row(r);
     }
     if (ngroups > 0) {
+        // Rows are read S at a time, the next step's rows prefetched into
+        // registers during the current step's multiplies; a group of R rows
+        // is R / S steps, unrolled so that every chain index is a
+        // compile-time constant.
+        static_assert(R % S == 0, "steps must tile a group of rows");
         const uint64_t i0 = static_cast<uint64_t>(base + r_a * T + tid);
         const uint8_t* cp = t.frame + 13 + i0 * 16u;
         if (LQ != 4) {
             cp = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(cp) & ~static_cast<uintptr_t>(15));
         }
-        uint4 pd[R], pe[R];
+        uint4 pd[S], pe[S];
 #pragma unroll
-        for (int k = 0; k < R; ++k) {
+        for (int k = 0; k < S; ++k) {
             pd[k] = *reinterpret_cast<const uint4*>(cp + k * kRowBytes);
             pe[k] = LQ != 4 ? *reinterpret_cast<const uint4*>(cp + k * kRowBytes + 16) : make_uint4(0, 0, 0, 0);
         }
+        uint32_t xi[NALU > 0 ? NALU : 1][4];  // integer-domain values of the integer-pipe chains
+#pragma unroll
+        for (int k = kTabChains; k < R; ++k) {
+            const uint32_t q[4] = {ch.q[k].x, ch.q[k].y, ch.q[k].z, ch.q[k].w};
+            clmul_from_raw(q, xi[k - kTabChains]);
+        }
 #pragma unroll 1
         for (int64_t g = 0; g < ngroups; ++g) {
-            uint4 cd[R], ce[R];
 #pragma unroll
-            for (int k = 0; k < R; ++k) {
-                cd[k] = pd[k];
-                ce[k] = pe[k];
-            }
-            if (g + 1 < ngroups) {
-                const uint8_t* nx = cp + R * kRowBytes;
+            for (int h = 0; h < R / S; ++h) {
+                uint4 cd[S], ce[S];
 #pragma unroll
-                for (int k = 0; k < R; ++k) {
-                    pd[k] = *reinterpret_cast<const uint4*>(nx + k * kRowBytes);
-                    pe[k] = LQ != 4 ? *reinterpret_cast<const uint4*>(nx + k * kRowBytes + 16) : make_uint4(0, 0, 0, 0);
+                for (int k = 0; k < S; ++k) {
+                    cd[k] = pd[k];
+                    ce[k] = pe[k];
                 }
-            }
+                if (h + 1 < R / S || g + 1 < ngroups) {
+                    const uint8_t* nx = cp + S * kRowBytes;
 #pragma unroll
-            for (int k = 0; k < R; ++k) {
-                const CtRaw raw{cd[k], ce[k], true};
-                ch.q[k] = xor4(gh_mul_rep<kOpenGh>(ch.q[k], lb_lo, lb_hi), ct_finish<LQ>(raw, t.frame, 0, P, fsel));
+                    for (int k = 0; k < S; ++k) {
+                        pd[k] = *reinterpret_cast<const uint4*>(nx + k * kRowBytes);
+                        pe[k] = LQ != 4 ? *reinterpret_cast<const uint4*>(nx + k * kRowBytes + 16)
+                                        : make_uint4(0, 0, 0, 0);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < S; ++k) {
+                    const int chain = h * S + k;
+                    const CtRaw raw{cd[k], ce[k], true};
+                    const uint4 c = ct_finish<LQ>(raw, t.frame, 0, P, fsel);
+                    if (chain < kTabChains) {
+                        ch.q[chain] = xor4(gh_mul_rep<kOpenGh>(ch.q[chain], lb_lo, lb_hi), c);
+                    } else {
+                        const uint32_t craw[4] = {c.x, c.y, c.z, c.w};
+                        uint32_t ci[4];
+                        clmul_from_raw(craw, ci);
+                        clmul_horner(xi[chain - kTabChains], *cm, ci);
+                    }
+                }
+                cp += S * kRowBytes;
             }
-            cp += R * kRowBytes;
+        }
+#pragma unroll
+        for (int k = kTabChains; k < R; ++k) {
+            uint32_t q[4];
+            clmul_to_raw(xi[k - kTabChains], q);
+            ch.q[k] = make_uint4(q[0], q[1], q[2], q[3]);
         }
         r = r_a + R * ngroups;
     }

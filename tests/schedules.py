@@ -17,7 +17,8 @@ from __future__ import annotations
 
 T = 512              # kHornerThreads == kCtrThreads
 SEAL_PAIR = 2        # rows per interior iteration of seal_rows
-OPEN_R = 2           # kOpenChains: rows per interior iteration of open_ghash_rows
+OPEN_R = 2           # kOpenChains: rows per interior group of the per-object open_ghash_rows
+OPEN_BATCH_R = 4     # kOpenBatchChains: the same for the batched open's GHASH pass
 CTR_PAIR = 2
 BATCH_MAX_SMS = 256  # kBatchMaxSms
 CHUNKS_PER_SM = 4    # kChunksPerSm
@@ -73,14 +74,14 @@ def seal_tile_rows(base, rows, P, pt_aligned=True):
     return _split(pad_rows(base), r_a, SEAL_PAIR * ngroups, rows)
 
 
-def open_tile_rows(base, rows, P):
-    """(generic rows, interior rows) of open_ghash_rows for a tile."""
+def open_tile_rows(base, rows, P, R=OPEN_R):
+    """(generic rows, interior rows) of open_ghash_rows with R chains for a tile."""
     n_full = P // 16
     r_lo = 0 if base >= 1 else _trunc_div(1 - base + T - 1, T)
     r_hi = min(_trunc_div(n_full - base, T), rows)
-    r_a = min(_trunc_div(r_lo + OPEN_R - 1, OPEN_R) * OPEN_R, r_hi)
-    ngroups = _trunc_div(r_hi - r_a, OPEN_R) if r_hi > r_a else 0
-    return _split(pad_rows(base), r_a, OPEN_R * ngroups, rows)
+    r_a = min(_trunc_div(r_lo + R - 1, R) * R, r_hi)
+    ngroups = _trunc_div(r_hi - r_a, R) if r_hi > r_a else 0
+    return _split(pad_rows(base), r_a, R * ngroups, rows)
 
 
 def ctr_tile_rows(base, rows, P):

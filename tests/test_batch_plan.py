@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 from schedules import (MAX_CHUNKS, SEGMENT_COST_ROWS, SMALL_MAX_BLOCKS, T, cdiv, chunk_plan, chunk_segments, ctr_tile_rows,
-                       mid_routed, open_tile_rows, pad_rows, seal_tile_rows, segment_base, tile_base, tile_rows)
+                       mid_routed, OPEN_BATCH_R, open_tile_rows, pad_rows, seal_tile_rows, segment_base, tile_base, tile_rows)
 
 
 def _ragged(count, seed, lo=4096, hi=1 << 20):
@@ -152,7 +152,7 @@ def test_segment_rows_meet_loop_preconditions(name):
         J = r1 - r0
         _check_tile(base, J, P, 0, seal_tile_rows)
         _check_tile(base, J, P, 1, lambda b, r, p: seal_tile_rows(b, r, p, pt_aligned=False), hi_margin=1)
-        _check_tile(base, J, P, 1, open_tile_rows)
+        _check_tile(base, J, P, 1, lambda b, r, p: open_tile_rows(b, r, p, R=OPEN_BATCH_R))
         _check_tile(base, J, P, 1, ctr_tile_rows)
 
 
@@ -185,4 +185,5 @@ def test_tile_rows_every_tile(P, J):
         # lie inside the object
         _check_tile(base, J, P, 1, lambda b, r, p: seal_tile_rows(b, r, p, pt_aligned=False), hi_margin=1)
         _check_tile(base, J, P, 1, open_tile_rows)
+        _check_tile(base, J, P, 1, lambda b, r, p: open_tile_rows(b, r, p, R=OPEN_BATCH_R))
         _check_tile(base, J, P, 1, ctr_tile_rows)
