@@ -19,10 +19,14 @@ static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, iv) == offsetof(dev::Batch
 static_assert(offsetof(lmcache_gpu_aesgcm_batch_item, status) == offsetof(dev::BatchItem, status),
               "descriptor layout");
 static_assert(offsetof(dev::BatchHeader, fault) == LMCACHE_GPU_AESGCM_BATCH_FAULT_OFFSET, "fault word offset");
+static_assert(offsetof(dev::BatchHeader, seal_two_pass) == 60, "the GPU tests read the seal design at byte 60");
 
 cudaError_t confkv::host::configure_batch_kernels()
 {
     cudaError_t e = allow_smem(dev::seal_batch_kernel, dev::kSealBatchSmem);
+    if (e == cudaSuccess) {
+        e = allow_smem(dev::seal_ghash_batch_kernel, dev::kOpenBatchSmem);
+    }
     if (e == cudaSuccess) {
         e = allow_smem(dev::open_ghash_batch_kernel, dev::kOpenBatchSmem);
     }
@@ -88,7 +92,13 @@ int batch_launch(lmcache_gpu_aesgcm_key_t key, lmcache_gpu_aesgcm_batch_item* it
     const uint32_t grid = static_cast<uint32_t>(h->num_sms);
     int rc;
     if (!open) {
-        rc = cuda_rc(launch_pdl(dev::seal_batch_kernel, grid, dev::kSealThreads, dev::kSealBatchSmem, s, ba));
+        // the plan picks fused or two passes; seal_ghash_batch_kernel returns
+        // at once after a fused seal
+        if (launch_pdl(dev::seal_batch_kernel, grid, dev::kSealThreads, dev::kSealBatchSmem, s, ba) != cudaSuccess) {
+            rc = LMCACHE_GPU_AESGCM_ERR_CUDA;
+        } else {
+            rc = cuda_rc(launch_pdl(dev::seal_ghash_batch_kernel, grid, dev::kSealThreads, dev::kOpenBatchSmem, s, ba));
+        }
     } else if (launch_pdl(dev::open_ghash_batch_kernel, grid, dev::kSealThreads, dev::kOpenBatchSmem, s, ba) !=
                cudaSuccess) {
         rc = LMCACHE_GPU_AESGCM_ERR_CUDA;

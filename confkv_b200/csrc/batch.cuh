@@ -114,7 +114,7 @@ struct BatchHeader {
     uint32_t fault;                 // nonzero: a work kernel's hand-off wait gave up (results invalid)
     uint32_t small_next[2];         // small-object queue heads: [0] seal, [1] open
     uint32_t small_bucket[5];       // objects per small-object bucket (kSmallBuckets)
-    uint32_t pad[1];
+    uint32_t seal_two_pass;         // seal: 1 = CTR pass, then GHASH pass (seal_two_pass_wins); 0 = one fused pass
 };
 static_assert(sizeof(BatchHeader) <= 256, "batch header fits its 256-byte area");
 
@@ -189,6 +189,27 @@ __host__ __device__ __forceinline__ uint32_t batch_chunk_count(unsigned long lon
     per = per < 1 ? 1 : (per > cap ? cap : per);
     const unsigned long long m = per * sms;
     return static_cast<uint32_t>(m < R ? m : R);
+}
+
+// The batched seal runs in one of two ways. Fused: seal_batch_kernel's row
+// warps encrypt and hash each segment in one pass (AES and GHASH tables share
+// the shared-memory pipe). Two passes: seal_batch_kernel only encrypts, then
+// seal_ghash_batch_kernel reads the ciphertext back and hashes it on four
+// chains, one of them on the integer pipes (the batched open's GHASH pass),
+// which leaves the shared-memory pipe less loaded per block. Every segment
+// then pays its start-up and fold twice, and the second pass its own launch
+// tail, so two passes win only on batches with many rows per SM and long
+// tile objects. Measured on B200 (seal GB/s, fused -> two passes): 32 x
+// 32 MiB 494 -> 536, 64 x 10 MiB 490 -> 525, 128 x 2 MiB 467 -> 485, one
+// 1 GiB object 495 -> 540, 4 x 64 MiB 474 -> 497; but 64 x 2 MiB 442 -> 431,
+// 32 x 4 MiB 450 -> 438, 48 x 3 MiB 449 -> 446, 64 x 1 MiB 398 -> 374 and the
+// 4096-object ragged batch (23 rows per tile object) 368 -> 344.
+constexpr unsigned long long kTwoPassMinRowsPerSm = 192;
+constexpr unsigned long long kTwoPassMinRowsPerObject = 256;
+
+__host__ __device__ __forceinline__ bool seal_two_pass_wins(unsigned long long R, uint32_t K, uint32_t sms)
+{
+    return K != 0 && R >= kTwoPassMinRowsPerSm * sms && R >= kTwoPassMinRowsPerObject * K;
 }
 
 struct BatchArgs {
@@ -495,6 +516,7 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         hdr->next_chunk[1] = 0;
         hdr->tile_objects = K;
         hdr->fault = 0;
+        hdr->seal_two_pass = !open && seal_two_pass_wins(R, K, sms) ? 1u : 0u;
         objs[K] = TileObj{R, 0xffffffffu, 0u};
     }
     __syncthreads();
@@ -986,6 +1008,77 @@ __device__ __forceinline__ bool seal_class(uint8_t* smem, const BatchArgs& a, co
     }
 }
 
+// CTR pass of a two-pass seal (seal_batch_kernel's row warps only): each
+// segment's rows are encrypted into its frame (seal_rows without the GHASH
+// chain), the segment at row 0 also writes the header. Chunks come from
+// queue 0; the row warps share the next chunk index through shared memory
+// (the unused hand-off buffers) behind named barrier 1, which the power warp
+// does not take part in.
+template <int SQ, bool PT>
+__device__ __forceinline__ bool seal_ctr_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, Cursor& cur,
+                                               int cls, uint32_t& round)
+{
+    volatile uint32_t* next_s = reinterpret_cast<volatile uint32_t*>(smem + kSealBatchHandoff);
+    for (;;) {
+        const Segment sg = segment_at(c, cur);
+        {
+            const BatchItem* it = a.items + sg.item;
+            const uint64_t P = it->plen;
+            uint8_t* frame = it->dst;
+            const uint32_t ivw[3] = {it->iv[0], it->iv[1], it->iv[2]};
+            if (sg.r0 == 0 && c.tid == 0) {
+                frame[0] = 1;
+                for (int b = 0; b < 12; ++b) {
+                    frame[1 + b] = static_cast<uint8_t>(ivw[b >> 2] >> (8 * (b & 3)));
+                }
+            }
+            int sq;
+            uint32_t store_r;
+            store_class(frame + 13, sq, store_r);  // sq == SQ for this class
+            (void)sq;
+            const SealTile t{it->src, frame + 13, P, segment_base(sg, P), static_cast<int64_t>(sg.r1 - sg.r0),
+                             {ivw[0] ^ a.rk[0], ivw[1] ^ a.rk[1], ivw[2] ^ a.rk[2]}, store_r};
+            seal_rows<SQ, PT, false>(t, a.rk, a.kt.gh_pow2, c.tid, c.lane);
+        }
+        if (cursor_step(cur, sg)) {
+            if (c.tid == 0) {
+                next_s[round & 1] = atomicAdd(&c.hdr->next_chunk[0], 1u);
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kHornerThreads) : "memory");
+            const uint32_t next = next_s[round & 1];
+            ++round;
+            if (!cursor_open(c, next, cur)) {
+                return false;
+            }
+        }
+        if (cursor_class(c, cur) != cls) {
+            return true;
+        }
+    }
+}
+
+__device__ __forceinline__ void seal_ctr_walk(uint8_t* smem, const BatchArgs& a, const BatchCta& c, uint32_t chunk)
+{
+    Cursor cur;
+    bool more = cursor_open(c, chunk, cur);
+    uint32_t round = 0;  // parity of the shared next-chunk entry
+    while (more) {
+        const int cls = cursor_class(c, cur);
+        switch (cls) {
+        case 0: more = seal_ctr_class<0, false>(smem, a, c, cur, cls, round); break;
+        case 1: more = seal_ctr_class<0, true>(smem, a, c, cur, cls, round); break;
+        case 2: more = seal_ctr_class<1, false>(smem, a, c, cur, cls, round); break;
+        case 3: more = seal_ctr_class<1, true>(smem, a, c, cur, cls, round); break;
+        case 4: more = seal_ctr_class<2, false>(smem, a, c, cur, cls, round); break;
+        case 5: more = seal_ctr_class<2, true>(smem, a, c, cur, cls, round); break;
+        case 6: more = seal_ctr_class<3, false>(smem, a, c, cur, cls, round); break;
+        case 7: more = seal_ctr_class<3, true>(smem, a, c, cur, cls, round); break;
+        case 8: more = seal_ctr_class<4, false>(smem, a, c, cur, cls, round); break;
+        default: more = seal_ctr_class<4, true>(smem, a, c, cur, cls, round); break;
+        }
+    }
+}
+
 // Power warp of the batched seal, over the same segments as the row warps:
 // E_K(J0), L*H and the basis of H^d while the segment's rows run, then the
 // fold levels 4..8 (the key's global tables), the object's sum and, once the
@@ -1039,7 +1132,14 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
     pdl_wait();  // the plan kernel's workspace
     const BatchCta c = batch_cta(a, h.ctx, tid);
     const uint32_t chunk = first_chunk(h.first, c, 0);
-    if (c.warp == kPowerWarp) {
+    if (c.hdr->seal_two_pass != 0u) {
+        // CTR pass of a two-pass seal: the row warps encrypt the chunks
+        // (seal_ghash_batch_kernel hashes them next); the power warp waits
+        // for the small objects
+        if (c.warp != kPowerWarp) {
+            seal_ctr_walk(smem, a, c, chunk);
+        }
+    } else if (c.warp == kPowerWarp) {
         seal_power_loop(a, c, h, chunk);
     } else {
         const WalkSlot ws{smem + kSealBatchWalk};
@@ -1088,11 +1188,37 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const Batch
 
 // ------------------------------------------------------------------ open
 
-// Row warps of the GHASH pass: segments whose frames share load class LQ
-// (both plaintext sides); same contract as seal_class.
-template <int LQ>
-__device__ __forceinline__ bool open_ghash_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c,
-                                                 const Handoff& h, const WalkSlot& ws)
+// GHASH pass of the batched open (SEAL = false: frames are the descriptors'
+// sources, the power warp checks tags) and of the batched seal (SEAL = true:
+// frames are the destinations, written by seal_ctr_batch_kernel earlier on
+// the stream, and the power warp writes their tags). The ciphertext load
+// class LQ of a segment: open takes it from the plan's alignment class; a
+// seal object's class codes its store funnel, so the seal pass derives LQ
+// from the frame address.
+template <bool SEAL>
+__device__ __forceinline__ const uint8_t* ghash_frame(const BatchItem* it)
+{
+    return SEAL ? it->dst : it->src;
+}
+
+template <bool SEAL>
+__device__ __forceinline__ int ghash_load_class(const BatchArgs& a, const BatchCta& c, const Cursor& cur)
+{
+    if constexpr (SEAL) {
+        int lq;
+        uint32_t r;
+        load_class(ghash_frame<true>(a.items + cta_objs(c)[cur.k].item) + 13, lq, r);
+        return lq;
+    } else {
+        return cursor_class(c, cur) >> 1;
+    }
+}
+
+// Row warps of the GHASH pass: segments whose frames share load class LQ;
+// same contract as seal_class.
+template <bool SEAL, int LQ>
+__device__ __forceinline__ bool ghash_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, const Handoff& h,
+                                            const WalkSlot& ws, int pass)
 {
     const uint4* ft = reinterpret_cast<const uint4*>(smem + kOpenFold);
     for (;;) {
@@ -1103,7 +1229,7 @@ __device__ __forceinline__ bool open_ghash_class(uint8_t* smem, const BatchArgs&
             *walk_word(ws, 1) = sg.last ? kChunkEnd : cur.k + 1;
             const BatchItem* it = a.items + sg.item;
             const uint64_t P = it->plen;
-            const uint8_t* frame = it->src;
+            const uint8_t* frame = ghash_frame<SEAL>(it);
             int lq;
             uint32_t load_r;
             load_class(frame + 13, lq, load_r);  // lq == LQ for this class
@@ -1116,7 +1242,7 @@ __device__ __forceinline__ bool open_ghash_class(uint8_t* smem, const BatchArgs&
         const bool chunk_done = *walk_word(ws, 1) == kChunkEnd;
         uint32_t taken = 0;
         if (chunk_done && c.tid == 0) {
-            taken = atomicAdd(&c.hdr->next_chunk[0], 1u);
+            taken = atomicAdd(&c.hdr->next_chunk[pass], 1u);
         }
         const uint4 v = warp_fold_pairs<false>(q, ft, c.lane);
         const uint32_t j = *walk_word(ws, 2);
@@ -1128,30 +1254,33 @@ __device__ __forceinline__ bool open_ghash_class(uint8_t* smem, const BatchArgs&
         if (chunk_done && !walk_open(c, next, ws)) {
             return false;
         }
-        if ((cursor_class(c, walk_cursor(ws)) >> 1) != LQ) {
+        if (ghash_load_class<SEAL>(a, c, walk_cursor(ws)) != LQ) {
             return true;
         }
     }
 }
 
-// Power warp of the GHASH pass: E_K(J0), L*H and the basis of H^d while the
-// rows run, then fold levels 4..8 (shared tables), the object's sum and, once
-// its last segment is in, the verdict (auth_ok and the object's slot).
-__device__ __forceinline__ void open_power_loop(const uint8_t* smem, const BatchArgs& a, const BatchCta& c,
-                                                const Handoff& h, uint32_t chunk)
+// Power warp of the GHASH pass: E_K(J0) (IV from the frame), L*H and the
+// basis of H^d while the rows run, then fold levels 4..8 (shared tables), the
+// object's sum and, once its last segment is in, the tag (seal) or the
+// verdict (open: auth_ok and the object's slot).
+template <bool SEAL>
+__device__ __forceinline__ void ghash_power_loop(const uint8_t* smem, const BatchArgs& a, const BatchCta& c,
+                                                 const Handoff& h, uint32_t chunk)
 {
     const uint4* t4 = reinterpret_cast<const uint4*>(smem + kOpenFold) + 4 * 512;
     Cursor cur;
-    bool more = cursor_open(c, chunk, cur);
+    bool more = cursor_open(c, chunk, cur) && (!SEAL || a.stall == 0u);
     for (uint32_t j = 0; more; ++j) {
         const Segment sg = segment_at(c, cur);
         Slot* slot = cta_slots(c) + sg.item;
         const BatchItem* it = a.items + sg.item;
         const uint32_t G = slot->aux[1];
         const uint64_t P = it->plen;
+        const uint8_t* frame = ghash_frame<SEAL>(it);
         uint4 ej0, lh;
         unsigned long long uhi, ulo;
-        open_power(it->src, a.kt.aes_t, a.rk, P, segment_power(sg), a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
+        open_power(frame, a.kt.aes_t, a.rk, P, segment_power(sg), a.kt.gh_pow2, c.lane, ej0, lh, uhi, ulo);
         uint4 v;
         uint32_t next;
         if (!power_take(h, j, c.lane, v, next)) {
@@ -1159,10 +1288,17 @@ __device__ __forceinline__ void open_power_loop(const uint8_t* smem, const Batch
         }
         const uint4 fold = power_fold(v, t4, c.lane);
         unsigned long long shi, slo;
-        if (batch_object_sum(slot, G, fold, uhi, ulo, c.lane, shi, slo) && c.lane == 0) {
-            const int ok = open_verdict(it->src, P, shi, slo, lh, ej0);
-            *it->auth_ok = ok;
-            slot->aux[2] = static_cast<unsigned int>(ok);
+        if (batch_object_sum(slot, G, fold, uhi, ulo, c.lane, shi, slo)) {
+            if constexpr (SEAL) {
+                const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
+                if (c.lane < 16) {
+                    it->dst[13 + P + c.lane] = static_cast<uint8_t>(byte_of(tag, c.lane));
+                }
+            } else if (c.lane == 0) {
+                const int ok = open_verdict(frame, P, shi, slo, lh, ej0);
+                *it->auth_ok = ok;
+                slot->aux[2] = static_cast<unsigned int>(ok);
+            }
         }
         if (cursor_step(cur, sg)) {
             more = cursor_open(c, next, cur);
@@ -1170,37 +1306,62 @@ __device__ __forceinline__ void open_power_loop(const uint8_t* smem, const Batch
     }
 }
 
-__global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const BatchArgs a)
+// The GHASH pass's CTA: the single-object open layout (H^(4T) chain table,
+// fold tables H^1..H^512, compact H^512) plus the hand-off; `pass` = the
+// chunk queue this pass takes (open: the first pass, seal: the second).
+template <bool SEAL>
+__device__ __forceinline__ void ghash_batch_cta(const BatchArgs& a, int pass)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     const int tid = threadIdx.x;
     pdl_release();
+    if constexpr (SEAL) {
+        // the plan may have chosen the fused seal, whose kernel wrote the
+        // tags already: read its choice before any table fill, so that a
+        // pass with nothing to do ends at once
+        pdl_wait();
+        if (reinterpret_cast<const volatile BatchHeader*>(a.ws)->seal_two_pass == 0u) {
+            return;
+        }
+    }
     fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenBatchChainLog2 * 512);
     fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kOpenFold), a.kt.gh_pow2);
     const Handoff h = handoff_at(smem, kOpenBatchHandoff, kOpenBatchSync);
     if (tid == 0) {
         handoff_init(h, a.wait_ns);
     }
-    pdl_wait();  // the plan kernel's workspace
+    if constexpr (!SEAL) {
+        pdl_wait();  // the plan's workspace
+    }
     const BatchCta c = batch_cta(a, h.ctx, tid);
-    const uint32_t chunk = first_chunk(h.first, c, 0);
+    const uint32_t chunk = first_chunk(h.first, c, pass);
     if (c.warp == kPowerWarp) {
-        open_power_loop(smem, a, c, h, chunk);
+        ghash_power_loop<SEAL>(smem, a, c, h, chunk);
     } else {
         const WalkSlot ws{smem + kOpenBatchWalk};
         *walk_word(ws, 2) = 0;
         bool more = walk_open(c, chunk, ws);
         while (more) {
-            switch (cursor_class(c, walk_cursor(ws)) >> 1) {  // the GHASH pass does not touch the plaintext side
-            case 0: more = open_ghash_class<0>(smem, a, c, h, ws); break;
-            case 1: more = open_ghash_class<1>(smem, a, c, h, ws); break;
-            case 2: more = open_ghash_class<2>(smem, a, c, h, ws); break;
-            case 3: more = open_ghash_class<3>(smem, a, c, h, ws); break;
-            default: more = open_ghash_class<4>(smem, a, c, h, ws); break;
+            switch (ghash_load_class<SEAL>(a, c, walk_cursor(ws))) {  // the GHASH pass reads only the frames
+            case 0: more = ghash_class<SEAL, 0>(smem, a, c, h, ws, pass); break;
+            case 1: more = ghash_class<SEAL, 1>(smem, a, c, h, ws, pass); break;
+            case 2: more = ghash_class<SEAL, 2>(smem, a, c, h, ws, pass); break;
+            case 3: more = ghash_class<SEAL, 3>(smem, a, c, h, ws, pass); break;
+            default: more = ghash_class<SEAL, 4>(smem, a, c, h, ws, pass); break;
             }
         }
     }
     handoff_failed(h, c);
+}
+
+__global__ void __launch_bounds__(kSealThreads, 1) open_ghash_batch_kernel(const BatchArgs a)
+{
+    ghash_batch_cta<false>(a, 0);
+}
+
+__global__ void __launch_bounds__(kSealThreads, 1) seal_ghash_batch_kernel(const BatchArgs a)
+{
+    ghash_batch_cta<true>(a, 1);
 }
 
 // Gated CTR over the same row space (rows of kCtrThreads = kHornerThreads

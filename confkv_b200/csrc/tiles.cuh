@@ -36,8 +36,10 @@ struct SealTile {
 //
 // SQ selects the ciphertext store: 4 = ciphertext pointer 16-B aligned;
 // 0..3 = word part of the funnel that builds an aligned 16-B chunk from this
-// lane's block and the next lane's (byte part in t.store_r).
-template <int SQ, bool PT_ALIGNED>
+// lane's block and the next lane's (byte part in t.store_r). GH = false
+// leaves out the GHASH chain (the batched seal's CTR pass; its GHASH pass
+// reads the ciphertext back) and returns zero.
+template <int SQ, bool PT_ALIGNED, bool GH = true>
 __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk, const uint4* pow2, int tid,
                                            int lane)
 {
@@ -87,7 +89,9 @@ __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk
         aes_rounds_smem<kSealAes>(x, rk, lb);
         const uint4 c = mask_bytes(make_uint4(p.x ^ x[0], p.y ^ x[1], p.z ^ x[2], p.w ^ x[3]), nb);
         store_ct_block<SQ>(t.ct, i, c, nb, P, s, fsel, lane);
-        chain_push_dyn<kSealGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
+        if constexpr (GH) {
+            chain_push_dyn<kSealGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
+        }
     };
 
     // Rows below r_pad hold no block of the object (tile 0's leading
@@ -127,14 +131,16 @@ __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk
                     pg1 = ld(nx + kRowBytes + 16);
                 }
             }
-            const uint4 m0 = gh_mul_rep<kSealGh>(ch.q[0], lb_lo, lb_hi);
+            const uint4 m0 = GH ? gh_mul_rep<kSealGh>(ch.q[0], lb_lo, lb_hi) : make_uint4(0, 0, 0, 0);
             uint32_t x[4], y[4];
             aes_ctr2_cached<kSealAes>(x, y, ctr, ctr + static_cast<uint32_t>(T), cc, t.s012, rk3x, rk, lb);
             const uint4 c0 = make_uint4(p0.x ^ x[0], p0.y ^ x[1], p0.z ^ x[2], p0.w ^ x[3]);
             const uint4 c1 = make_uint4(p1.x ^ y[0], p1.y ^ y[1], p1.z ^ y[2], p1.w ^ y[3]);
             store_ct_interior<SQ>(cp, c0, s, fsel, lane);
             store_ct_interior<SQ>(cp + kRowBytes, c1, s, fsel, lane);
-            if constexpr (R == 1) {
+            if constexpr (!GH) {
+                (void)m0;
+            } else if constexpr (R == 1) {
                 ch.q[0] = xor4(gh_mul_rep<kSealGh>(xor4(m0, c0), lb_lo, lb_hi), c1);
             } else {
                 const uint4 m1 = gh_mul_rep<kSealGh>(ch.q[1], lb_lo, lb_hi);

@@ -113,3 +113,41 @@ def test_seal_each_d2h_host_frames_match_openssl(gpu_lib, oracle):
         work.open_each_from_host(side)
         s.synchronize()
         assert work.round_trip_ok()
+
+
+SEAL_TWO_PASS_OFFSET = 60  # BatchHeader.seal_two_pass: the plan's choice of seal design
+
+
+@pytest.mark.parametrize("big,expect_two_pass", [((64 << 20) + 5, 1), ((1 << 20) + 3, 0)])
+def test_batched_seal_both_designs_match_openssl(gpu_lib, oracle, big, expect_two_pass):
+    """A batch of eight large objects with 300 small and mid objects mixed
+    in: with 64 MiB objects the plan picks the two-pass seal (CTR pass, then
+    the GHASH pass writes the tags), with 1 MiB objects the fused seal. Every
+    frame must equal OpenSSL's either way, and the opens must round-trip."""
+    rng = np.random.default_rng(big)
+    lens = [big] * 8 + [int(x) for x in rng.integers(0, 40 << 10, size=300)]
+    order = rng.permutation(len(lens))
+    lens = [lens[i] for i in order]
+    dev = torch.device("cuda", 0)
+    plain, offs = configs.random_plain(lens, seed=17, dev=dev, packed=True)
+    ivs = workloads.make_ivs(18, len(lens))
+    key = workloads.make_key(19)
+    s = torch.cuda.Stream()
+    with GpuAes128GcmKey(gpu_lib, key) as k:
+        work = configs.RankWork(gpu_lib, k, lens, plain, offs, s, ivs, packed=True)
+        torch.cuda.synchronize()
+        work.frames.fill_(0)
+        work.reset_outputs()
+        torch.cuda.synchronize()
+        work.seal_batched()
+        s.synchronize()
+        mode = int(work.bseal.workspace[SEAL_TWO_PASS_OFFSET:SEAL_TWO_PASS_OFFSET + 4].view(torch.int32).item())
+        assert mode == expect_two_pass
+        assert int(work.bseal.fault()) == 0
+        work.open_batched()
+        s.synchronize()
+        assert work.round_trip_ok()
+        frames = work.frames.cpu().numpy()
+        host_plain = [plain[a:a + n].cpu().numpy() for a, n in zip(offs, lens)]
+        got = [frames[o:o + n + 29] for o, n in zip(work.fr_off, lens)]
+        _assert_frames_match(oracle, key, ivs, host_plain, got)
