@@ -224,7 +224,7 @@ struct BatchArgs {
     unsigned long long wait_ns;
     uint32_t rk[44];
     KeyTables kt;
-    ClmulConst open_cm;  // the batched open's chain multiplier H^(4 T) for its integer-pipe chains
+    ClmulConst open_cm;  // the batched GHASH passes' chain multiplier for their integer-pipe chains
 };
 
 // Ciphertext store class of a frame: sq = word part of 16 - (ct & 15)
@@ -1306,7 +1306,7 @@ __device__ __forceinline__ void ghash_power_loop(const uint8_t* smem, const Batc
     }
 }
 
-// The GHASH pass's CTA: the single-object open layout (H^(4T) chain table,
+// The GHASH pass's CTA: the single-object open layout (the chain table,
 // fold tables H^1..H^512, compact H^512) plus the hand-off; `pass` = the
 // chunk queue this pass takes (open: the first pass, seal: the second).
 template <bool SEAL>
@@ -1324,7 +1324,7 @@ __device__ __forceinline__ void ghash_batch_cta(const BatchArgs& a, int pass)
             return;
         }
     }
-    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenBatchChainLog2 * 512);
+    fill_gh_smem(smem + kOpenGh, a.kt.gh_chain);
     fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kOpenFold), a.kt.gh_pow2);
     const Handoff h = handoff_at(smem, kOpenBatchHandoff, kOpenBatchSync);
     if (tid == 0) {

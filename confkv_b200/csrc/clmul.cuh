@@ -21,12 +21,16 @@
 // 64-bit halves, each Karatsuba over 32-bit words: 9 products, 144 IMAD.WIDE.
 //
 // Reduction: with a and b reflected, the integer carry-less product p
-// (255 bits) satisfies r = p << 1 = reflected(A(x) B(x)) on 256 bits, its
-// high half the powers 0..127 and its low half h the powers 128..254. With
-// x^128 = 1 + x + x^2 + x^7 and multiplication by x^k a right shift by k of
-// a reflected value, the powers h x^k pushes past x^127 are t = (h << 127) ^
-// (h << 126) ^ (h << 121) (mod 2^128); with g = h ^ t,
-//     A B mod P = r_hi ^ g ^ (g >> 1) ^ (g >> 2) ^ (g >> 7).
+// (255 bits, x^s at bit 254 - s) is the reflected 256-bit form of
+// A(x) B(x) x (x^s at bit 255 - s): its high half holds the powers 0..127
+// and its low half h the powers 128..255. With x^128 = 1 + x + x^2 + x^7 and
+// multiplication by x^k a right shift by k of a reflected value, the powers
+// h x^k pushes past x^127 are t = (h << 127) ^ (h << 126) ^ (h << 121)
+// (mod 2^128); with g = h ^ t,
+//     A B x mod P = p_hi ^ g ^ (g >> 1) ^ (g >> 2) ^ (g >> 7).
+// The multiplier is therefore prepared as M x^-1 (x^-1 = x^127 + x^6 + x + 1,
+// since x (x^127 + x^6 + x + 1) = x^128 + x^7 + x^2 + x = 1 mod P): the
+// product is A M with no shift of p.
 #pragma once
 
 #include <cstdint>
@@ -77,11 +81,26 @@ CONFKV_CLMUL_FN void clmul_parts(uint32_t v, uint32_t out[4])
     }
 }
 
-// Host: M (raw block words) -> its Karatsuba operands.
+// Host: M (raw block words) -> the Karatsuba operands of M x^-1. In the
+// reflected integer form, M x^-1 = (M << 1), plus x^-1 = x^127 + x^6 + x + 1
+// when the shift pushes out M's x^0 coefficient (bit 127).
 CONFKV_CLMUL_FN ClmulConst clmul_prepare(const uint32_t m_raw[4])
 {
-    const uint32_t b0 = clmul_bswap(m_raw[3]), b1 = clmul_bswap(m_raw[2]);
-    const uint32_t b2 = clmul_bswap(m_raw[1]), b3 = clmul_bswap(m_raw[0]);
+    uint32_t b[4];  // M's integer words, b[0] least significant
+    for (int w = 0; w < 4; ++w) {
+        b[w] = clmul_bswap(m_raw[3 - w]);
+    }
+    const uint32_t carry = b[3] >> 31;  // M's coefficient of x^0
+    for (int w = 3; w > 0; --w) {
+        b[w] = (b[w] << 1) | (b[w - 1] >> 31);
+    }
+    b[0] <<= 1;
+    // x^-1 reflected: x^0 at bit 127, x^1 at 126, x^6 at 121, x^127 at 0
+    const uint32_t xinv[4] = {0x00000001u, 0u, 0u, 0xC2000000u};
+    for (int w = 0; w < 4; ++w) {
+        b[w] ^= carry * xinv[w];
+    }
+    const uint32_t b0 = b[0], b1 = b[1], b2 = b[2], b3 = b[3];
     const uint32_t ops[9] = {b0, b1, b0 ^ b1, b2, b3, b2 ^ b3, b0 ^ b2, b1 ^ b3, b0 ^ b1 ^ b2 ^ b3};
     ClmulConst c{};
     for (int k = 0; k < 9; ++k) {
@@ -125,7 +144,8 @@ CONFKV_CLMUL_FN uint64_t clmul32(uint32_t x, const uint32_t y[4])
     const uint64_t z2 = (x0 * y2) ^ (x1 * y1) ^ (x2 * y0) ^ (x3 * y3);
     const uint64_t z3 = (x0 * y3) ^ (x1 * y2) ^ (x2 * y1) ^ (x3 * y0);
     constexpr uint64_t kH = 0x1111111111111111ull;
-    return (z0 & kH) | (z1 & (kH << 1)) | (z2 & (kH << 2)) | (z3 & (kH << 3));
+    // the four masked residues have no bit in common: adding them is their OR
+    return ((z0 & kH) + (z1 & (kH << 1))) + ((z2 & (kH << 2)) + (z3 & (kH << 3)));
 }
 
 // The 32 x 32 product of Karatsuba operand k of M: spacing-5 holes when H5.
@@ -162,14 +182,9 @@ CONFKV_CLMUL_FN void clmul_mul_int(const uint32_t x[4], const ClmulConst& c, uin
     clmul64<H5>(x[0], x[1], c, 0, lo);
     clmul64<H5>(x[2], x[3], c, 3, hi);
     clmul64<H5>(x[0] ^ x[2], x[1] ^ x[3], c, 6, s);
-    // p = hi << 128 ^ (s ^ lo ^ hi) << 64 ^ lo, then r = p << 1
-    const uint32_t p[8] = {lo[0], lo[1], lo[2] ^ s[0] ^ lo[0] ^ hi[0], lo[3] ^ s[1] ^ lo[1] ^ hi[1],
+    // p = hi << 128 ^ (s ^ lo ^ hi) << 64 ^ lo
+    const uint32_t r[8] = {lo[0], lo[1], lo[2] ^ s[0] ^ lo[0] ^ hi[0], lo[3] ^ s[1] ^ lo[1] ^ hi[1],
                            hi[0] ^ s[2] ^ lo[2] ^ hi[2], hi[1] ^ s[3] ^ lo[3] ^ hi[3], hi[2], hi[3]};
-    uint32_t r[8];
-    r[0] = p[0] << 1;
-    for (int w = 1; w < 8; ++w) {
-        r[w] = (p[w] << 1) | (p[w - 1] >> 31);
-    }
     // g = h ^ t, t = (h << 127) ^ (h << 126) ^ (h << 121): only the top word
     uint32_t g[4] = {r[0], r[1], r[2], r[3] ^ (r[0] << 31) ^ (r[0] << 30) ^ (r[0] << 25)};
     for (int w = 0; w < 3; ++w) {

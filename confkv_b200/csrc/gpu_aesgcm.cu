@@ -412,7 +412,8 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
     constexpr size_t kAesT = 4 * 256 * sizeof(uint32_t);
     constexpr size_t kTab = confkv::kGhashTableBytes;
     const size_t off_pow2 = kAesT;
-    const size_t off_slots = off_pow2 + kTab * confkv::kPow2Tables;
+    const size_t off_chain = off_pow2 + kTab * confkv::kPow2Tables;
+    const size_t off_slots = off_chain + kTab;
     const size_t total = off_slots + sizeof(dev::Slot) * kSlots;
 
     uint8_t* host = new (std::nothrow) uint8_t[total];
@@ -425,15 +426,18 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
     Gf128 p = H;
     for (int k = 0; k < confkv::kPow2Tables; ++k) {
         confkv::ghash_table(p, host + off_pow2 + kTab * k);
-        if (k == dev::kOpenBatchChainLog2) {
-            // the batched open's chain multiplier, for its integer-pipe chains
-            uint8_t pb[16];
-            uint32_t pw[4];
-            confkv::gf_store(pb, p);
-            std::memcpy(pw, pb, 16);
-            h->open_cm = confkv::clmul_prepare(pw);
-        }
         p = confkv::gf_mul(p, p);
+    }
+    {
+        // the batched GHASH passes' chain multiplier: its 4-bit table and
+        // its integer-pipe form
+        const Gf128 m = confkv::gf_pow(H, static_cast<uint64_t>(dev::kOpenBatchChains) * dev::kHornerThreads);
+        confkv::ghash_table(m, host + off_chain);
+        uint8_t pb[16];
+        uint32_t pw[4];
+        confkv::gf_store(pb, m);
+        std::memcpy(pw, pb, 16);
+        h->open_cm = confkv::clmul_prepare(pw);
     }
 
     if (cudaMalloc(&h->d_mem, total) != cudaSuccess) {
@@ -450,6 +454,7 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
     }
     h->kt.aes_t = reinterpret_cast<const uint32_t*>(h->d_mem);
     h->kt.gh_pow2 = reinterpret_cast<const uint4*>(h->d_mem + off_pow2);
+    h->kt.gh_chain = reinterpret_cast<const uint4*>(h->d_mem + off_chain);
     h->slots = reinterpret_cast<dev::Slot*>(h->d_mem + off_slots);
     *out = reinterpret_cast<lmcache_gpu_aesgcm_key_t>(h);
     return LMCACHE_GPU_AESGCM_OK;

@@ -26,7 +26,7 @@ struct KeyHandle {
     uint32_t rk[confkv::kRoundKeyWords];
     uint8_t* d_mem = nullptr;  // one allocation: tables + slots
     dev::KeyTables kt{};
-    confkv::ClmulConst open_cm{};  // the batched open's chain multiplier H^(4 T), integer-pipe form
+    confkv::ClmulConst open_cm{};  // the batched GHASH passes' chain multiplier, integer-pipe form
     dev::Slot* slots = nullptr;
     std::atomic<uint32_t> next_slot{0};
 };

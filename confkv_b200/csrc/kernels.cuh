@@ -22,19 +22,22 @@ constexpr int kSealChains = 1;                      // GHASH chains per thread i
 constexpr int kSealChainLog2 = kHornerLog2;         // chain multiplier H^kHornerThreads
 constexpr int kOpenChains = 2;                      // GHASH chains per thread in the per-object open
 constexpr int kOpenChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * kHornerThreads)
-// The batched open's GHASH pass runs four chains per thread (multiplier
-// H^(4 T)); the last kOpenBatchAluChains of them multiply on the integer
-// pipes (clmul.cuh) instead of the shared-memory tables, so the two share
-// the GHASH work. A table multiply costs 4 shared-memory wavefronts per
-// block and ~110 ALU instructions, an integer-pipe multiply ~310 ALU and
-// ~150 FMA-pipe instructions: with one chain in four on the integer pipes
-// neither unit exceeds the shared-memory pipe's rate (measured on B200, 32 x
-// 32 MiB: 502 -> 549 GB/s; one in two, or two in four, ran slower than tables
-// alone). The per-object open keeps two table chains: its tiles are a few
-// dozen rows, where four chains cost more in the edge rows and the combine
-// than they gain.
+// The batched GHASH passes (open, and the two-pass seal) run
+// kOpenBatchChains chains per thread (multiplier H^(kOpenBatchChains T), a
+// compact table of its own in the key tables); the last
+// kOpenBatchAluChains of them multiply on the integer pipes (clmul.cuh)
+// instead of the shared-memory tables, so the two share the GHASH work. A
+// table multiply costs 4 shared-memory wavefronts per block and ~110 ALU
+// instructions, an integer-pipe multiply ~310 ALU and ~150 FMA-pipe
+// instructions (ncu, B200). Measured on 32 x 32 MiB (open GB/s): tables
+// only 502; one chain in four 549; one in three 538 and two in five 511
+// (both lose although the shared-memory pipe still binds at one in four,
+// 3.40 wavefronts against 2.55 ALU clocks per block: with fewer table rows
+// between its steps the integer-pipe chain's latency shows); one in two 495.
+// The per-object open keeps two table chains: its tiles are a few dozen
+// rows, where more chains cost more in the edge rows and the combine than
+// they gain.
 constexpr int kOpenBatchChains = 4;
-constexpr int kOpenBatchChainLog2 = kHornerLog2 + 2;
 constexpr int kOpenBatchAluChains = 1;
 constexpr int kOpenBatchStepRows = 1;               // interior rows read (and prefetched) at a time
 constexpr int kPowerWarp = kHornerThreads / 32;     // warp index of the power warp
@@ -94,6 +97,7 @@ struct Slot {
 struct KeyTables {
     const uint32_t* aes_t;   // T0..T3, 4 x 256 words
     const uint4* gh_pow2;    // compact 4-bit tables (512 entries) for H^(2^k), k = 0..35
+    const uint4* gh_chain;   // compact 4-bit table of the batched GHASH passes' chain multiplier H^(kOpenBatchChains T)
 };
 
 struct SealArgs {

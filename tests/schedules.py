@@ -18,7 +18,7 @@ from __future__ import annotations
 T = 512              # kHornerThreads == kCtrThreads
 SEAL_PAIR = 2        # rows per interior iteration of seal_rows
 OPEN_R = 2           # kOpenChains: rows per interior group of the per-object open_ghash_rows
-OPEN_BATCH_R = 4     # kOpenBatchChains: the same for the batched open's GHASH pass
+OPEN_BATCH_R = 4     # kOpenBatchChains: the same for the batched GHASH passes
 CTR_PAIR = 2
 BATCH_MAX_SMS = 256  # kBatchMaxSms
 CHUNKS_PER_SM = 4    # kChunksPerSm

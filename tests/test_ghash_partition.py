@@ -78,7 +78,7 @@ def model_ghash(oracle, h: bytes, ct: bytes, num_sms: int, chains: int) -> bytes
     return xor(acc, mul(lenblk, h))
 
 
-@pytest.mark.parametrize("chains", [1, 2, 4])
+@pytest.mark.parametrize("chains", [1, 2, 3, 4])
 @pytest.mark.parametrize("size,num_sms", [(1, 148), (16, 148), (17, 4), (4096, 148), (16 * 700 + 5, 2),
                                           (16 * 1024, 4), (16 * 1537 + 9, 3), (16 * 3000, 2)])
 def test_partitioned_ghash_matches_serial(oracle, size, num_sms, chains):
