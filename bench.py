@@ -77,21 +77,71 @@ def load_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-def profile_summary(name: str) -> dict:
-    """`key: number` lines of a committed ncu summary under profiles/
-    (dram_bytes_per_launch, wavefronts_per_block), if present."""
+KERNEL_PROFILE = "batched_kernels_kv_llama8b.md"
+PIPE_RATES_PROFILE = "pipe_rates_b200.md"
+
+
+def kernel_profile(name: str = KERNEL_PROFILE) -> dict:
+    """Per-kernel costs per 16-byte block from a committed ncu summary under
+    profiles/: lines `kernel <name> call=<seal|open> wavefronts=<L1 data-pipe
+    wavefronts> alu=<ALU-pipe instructions> fma=<FMA-pipe busy SM clocks>
+    issue=<instructions> dram=<DRAM bytes>` (instructions in threads)."""
     p = ROOT / "profiles" / name
     out = {}
     if not p.exists():
         return out
     for line in p.read_text().splitlines():
-        for k in ("dram_bytes_per_launch", "wavefronts_per_block"):
-            if line.startswith(k + ":"):
-                try:
-                    out[k] = float(line.split(":", 1)[1].strip().split()[0])
-                except ValueError:
-                    pass
+        parts = line.strip().split()
+        if len(parts) < 3 or parts[0] != "kernel":
+            continue
+        rec = {}
+        for kv in parts[2:]:
+            k, _, v = kv.partition("=")
+            try:
+                rec[k] = float(v)
+            except ValueError:
+                rec[k] = v
+        out[parts[1]] = rec
     return out
+
+
+def committed_pipe_peaks() -> dict | None:
+    """`peak <unit>=<per SM per clock>` lines of the committed microbenchmark summary."""
+    p = ROOT / "profiles" / PIPE_RATES_PROFILE
+    if not p.exists():
+        return None
+    out = {}
+    for line in p.read_text().splitlines():
+        parts = line.strip().split()
+        if parts and parts[0] == "peak":
+            for kv in parts[1:]:
+                k, _, v = kv.partition("=")
+                out[k] = float(v)
+    return out or None
+
+
+def pipe_roofline(prof: dict, call: str, peaks: dict, n_sm: int, sm_hz: float, achieved_gbs: float) -> dict:
+    """Ceiling of one call (its kernels run one after another) from the
+    per-block costs of its kernels at the measured per-SM peaks: each kernel
+    needs max over units of (units per block / units per SM per clock) SM
+    clocks per block; the call needs their sum."""
+    kernels = {}
+    total = 0.0
+    for name, rec in prof.items():
+        if rec.get("call") != call:
+            continue
+        # fma: FMA-pipe busy clocks per block as ncu counts them (an IMAD.WIDE
+        # holds the pipe about two cycles, so instructions / rate would undercount)
+        clk = {"l1_wavefronts": rec["wavefronts"] / peaks["l1_wavefronts"], "alu": rec["alu"] / peaks["alu"],
+               "fma": rec["fma"], "issue": rec["issue"] / peaks["issue"]}
+        bind = max(clk, key=clk.get)
+        kernels[name] = {"clocks_per_block": {u: round(v, 3) for u, v in clk.items()}, "binding": bind}
+        total += clk[bind]
+    if total == 0.0:
+        return {}
+    ceiling = n_sm * sm_hz / total * 16 / 1e9
+    return {"kernels": kernels, "ceiling_plaintext_gbs": round(ceiling, 1),
+            "achieved_plaintext_gbs": round(achieved_gbs, 1), "frac": round(achieved_gbs / ceiling, 3)}
 
 
 # ----------------------------------------------------------------- ours
@@ -225,35 +275,45 @@ def run_ours(args, rank, world, local):
         ms_per_step = total_ms / args.steps
         value = gbs(total_ms, bytes_per_step)
         peak, peak_kind = load_peaks()
-        launches_per_step = (2 + 3) if head == "batched" else 3 * nobj
-        # Dominant kernel: the seal kernel. Batched: one seal_batch_kernel
-        # launch per step seals all nobj objects (the one-CTA plan kernel in
-        # the same timed call is a few microseconds); per object: one
-        # seal_kernel launch per object. Algorithmic bytes per object = read
-        # P + write P + 29.
-        kernel = "seal_batch_kernel" if head == "batched" else "seal_kernel"
+        launches_per_step = (3 + 3) if head == "batched" else 3 * nobj
+        # HBM roofline of the seal call. Batched: one seal_batch_async per
+        # step = the plan kernel, seal_batch_kernel (encrypts; for this
+        # workload the plan picks the two-pass seal) and seal_ghash_batch_kernel
+        # (hashes, writes tags), timed together by the events around the call;
+        # per object: one seal_kernel launch per object. Algorithmic bytes per
+        # object: read P + write P + 29.
+        kernel = ("seal_batch_async: batch_plan_kernel + seal_batch_kernel + seal_ghash_batch_kernel"
+                  if head == "batched" else "seal_kernel")
         objs_per_launch = nobj if head == "batched" else 1
         launch_ms = seal_sum / args.steps / (1 if head == "batched" else nobj)
         achieved = objs_per_launch * (2 * P + 29) / (launch_ms * 1e-3) / 1e9
-        prof = profile_summary(f"{kernel}_kv_llama8b.txt")
-        traffic = prof.get("dram_bytes_per_launch")
-        # The path is bound by the L1 data pipe, not by HBM: every block costs
-        # a fixed number of shared-memory wavefronts (AES T-table and GHASH
-        # table lookups) and the pipe retires one per SM per clock. That rate
-        # at the kernel's measured wavefronts per block (ncu summary under
-        # profiles/) and the clock sampled during the run is `lsu_roofline`.
-        # `int_roofline` is the integer-op bound of a table-free formulation
-        # (bitsliced AES-128 758 + CTR xor 4 + Karatsuba GHASH 400 = 1162
-        # two-input ops per 16-B block) at the measured LOP3 issue rate (64
-        # lanes per SM per clock): these kernels replace most of those ops by
-        # table lookups, so they run above it (frac > 1).
-        wpb = prof.get("wavefronts_per_block", 9.02)
+        prof = kernel_profile()
+        blocks = objs_per_launch * (P // 16)
+        traffic = None
+        if head == "batched" and prof:
+            traffic = round(sum(r["dram"] for r in prof.values() if r.get("call") == "seal") * blocks)
         sm_hz = (clk["sm_mhz"] if clk else 1965.0) * 1e6
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
-        seal_gbs_dev = objs_per_launch * P / (launch_ms * 1e-3) / 1e9
-        lsu_ceiling_gbs = n_sm * sm_hz / wpb * 16 / 1e9
-        int_peak = 64 * n_sm * sm_hz
-        int_ach = seal_gbs_dev * 1e9 / 16 * 1162
+        seal_gbs_dev = nobj * P / (seal_sum / args.steps * 1e-3) / 1e9
+        open_gbs_dev = nobj * P / (open_sum / args.steps * 1e-3) / 1e9
+        peaks, peaks_src = None, None
+        try:
+            from confkv_b200 import pipe_rates
+
+            peaks = pipe_rates.model_peaks(pipe_rates.measure())
+            peaks_src = "measured in this run (confkv_b200.pipe_rates)"
+        except Exception as exc:  # noqa: BLE001 - fall back to the committed measurement
+            peaks = committed_pipe_peaks()
+            peaks_src = f"profiles/{PIPE_RATES_PROFILE} ({exc.__class__.__name__} live)"
+        pipes = {}
+        if head == "batched" and prof and peaks:
+            pipes = {"unit": "plaintext GB/s", "per_sm_clk_peaks": {k: round(v, 2) for k, v in peaks.items()},
+                     "peaks_source": peaks_src, "costs_source": f"profiles/{KERNEL_PROFILE}",
+                     "sm_mhz": sm_hz / 1e6,
+                     "seal": pipe_roofline(prof, "seal", peaks, n_sm, sm_hz, seal_gbs_dev),
+                     "open": pipe_roofline(prof, "open", peaks, n_sm, sm_hz, open_gbs_dev)}
+            binds = [k["binding"] for c in ("seal", "open") for k in pipes[c].get("kernels", {}).values()]
+            pipes["bound"] = max(set(binds), key=binds.count) if binds else None
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -280,18 +340,10 @@ def run_ours(args, rank, world, local):
                          "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6.65 TB/s",
                          "algorithmic_bytes_per_launch": objs_per_launch * (2 * P + 29),
-                         "traffic": traffic},
-            "int_roofline": {"bound": "int", "kernel": kernel, "ops_per_block": 1162,
-                             "achieved": round(int_ach / 1e12, 3), "peak": round(int_peak / 1e12, 3),
-                             "unit": "Tops/s", "frac": round(int_ach / int_peak, 3),
-                             "peak_source": "measured LOP3 rate 64 lanes/SM/clk x SMs x sampled SM clock",
-                             "note": "op count of a table-free (bitsliced AES + Karatsuba GHASH) formulation; "
-                                     "the lookup kernels execute far fewer ALU ops, so frac > 1 is expected "
-                                     "and lsu_roofline is the binding bound"},
-            "lsu_roofline": {"bound": "l1_wavefronts", "kernel": kernel, "wavefronts_per_block": wpb,
-                             "ceiling_plaintext_gbs": round(lsu_ceiling_gbs, 1),
-                             "achieved_plaintext_gbs": round(seal_gbs_dev, 1),
-                             "frac": round(seal_gbs_dev / lsu_ceiling_gbs, 3)},
+                         "traffic": traffic,
+                         "traffic_source": f"profiles/{KERNEL_PROFILE}: DRAM bytes per block of the call's kernels "
+                                           "x blocks" if traffic is not None else None},
+            "pipe_roofline": pipes,
             "e2e": {"value": round(e2e["gbs"] * world, 2) if world == 1 else
                     round(2 * nobj * P * world / (e2e_ms * 1e-3) / 1e9, 2),
                     "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],

@@ -340,9 +340,22 @@ void horner_grid(uint64_t n, int num_sms, uint32_t& iters, uint32_t& grid)
     grid = static_cast<uint32_t>((n + span - 1) / span);
 }
 
-dev::Slot* take_slot(KeyHandle* h)
+// The slot of `s` on this handle: the stream's own, assigned on its first
+// call; nullptr once kSlots other streams hold one (the call then fails with
+// ERR_ALLOC instead of sharing a slot with unordered work).
+dev::Slot* take_slot(KeyHandle* h, cudaStream_t s)
 {
-    return h->slots + (h->next_slot.fetch_add(1, std::memory_order_relaxed) % kSlots);
+    std::lock_guard<std::mutex> lock(h->slot_mu);
+    const auto it = h->stream_slot.find(s);
+    if (it != h->stream_slot.end()) {
+        return h->slots + it->second;
+    }
+    if (h->stream_slot.size() >= static_cast<size_t>(kSlots)) {
+        return nullptr;
+    }
+    const uint32_t k = static_cast<uint32_t>(h->stream_slot.size());
+    h->stream_slot.emplace(s, k);
+    return h->slots + k;
 }
 
 template <int SQ, bool A>
@@ -524,7 +537,10 @@ extern "C" int lmcache_gpu_aes128gcm_seal_async(lmcache_gpu_aesgcm_key_t key, co
         return cuda_rc(launch_pdl(dev::seal_empty_kernel, 1, 32, 0, s, args));
     }
     horner_grid(n, h->num_sms, args.iters, args.grid);
-    args.slot = take_slot(h);
+    args.slot = take_slot(h, s);
+    if (args.slot == nullptr) {
+        return LMCACHE_GPU_AESGCM_ERR_ALLOC;
+    }
 
     const uintptr_t ct = reinterpret_cast<uintptr_t>(dst) + 13u;
     const uint32_t off = static_cast<uint32_t>(ct & 15u);
@@ -591,7 +607,10 @@ extern "C" int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, co
         return cuda_rc(launch_pdl(dev::open_empty_kernel, 1, 32, 0, s, oa));
     }
     horner_grid(n, h->num_sms, oa.iters, oa.grid);
-    oa.slot = take_slot(h);
+    oa.slot = take_slot(h, s);
+    if (oa.slot == nullptr) {
+        return LMCACHE_GPU_AESGCM_ERR_ALLOC;
+    }
 
     const uintptr_t ct = reinterpret_cast<uintptr_t>(src) + 13u;
     const uint32_t off = static_cast<uint32_t>(ct & 15u);

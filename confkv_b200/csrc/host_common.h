@@ -4,8 +4,9 @@
 
 #include <cuda_runtime.h>
 
-#include <atomic>
 #include <cstdint>
+#include <mutex>
+#include <unordered_map>
 #include <utility>
 
 #include "gpu_aesgcm_api.h"
@@ -17,7 +18,7 @@ namespace host {
 
 constexpr size_t kFrameOverhead = 29;
 constexpr uint64_t kMaxBlocks = 0xfffffffeull;
-constexpr int kSlots = 1024;  // per-call accumulation slots of a key handle (a ring)
+constexpr int kSlots = 1024;  // accumulation slots of a key handle: one per stream it is used on
 constexpr int kMaxDevices = 64;
 
 struct KeyHandle {
@@ -28,7 +29,11 @@ struct KeyHandle {
     dev::KeyTables kt{};
     confkv::ClmulConst open_cm{};  // the batched GHASH passes' chain multiplier, integer-pipe form
     dev::Slot* slots = nullptr;
-    std::atomic<uint32_t> next_slot{0};
+    // Stream -> its slot. Calls on one stream never overlap on the device
+    // (each kernel touches the slot only after griddepcontrol.wait, i.e.
+    // after the previous call's kernels completed), so they share it.
+    std::mutex slot_mu;
+    std::unordered_map<cudaStream_t, uint32_t> stream_slot;
 };
 
 // Makes `target` the current device for the scope of a call and restores

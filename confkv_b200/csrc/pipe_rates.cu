@@ -20,7 +20,7 @@ namespace {
 
 enum PipeOp : int {
     kLop3 = 0,      // lop3.b32 (xor of three)
-    kIadd = 1,      // add.u32
+    kIadd = 1,      // add.u32 (ptxas merges two dependent adds into one IADD3: per IADD3, half this rate)
     kPrmt = 2,      // prmt.b32 with a register selector
     kShf = 3,       // shf.l.wrap.b32
     kImad = 4,      // mad.lo.u32
@@ -28,7 +28,8 @@ enum PipeOp : int {
     kImadHi = 6,    // mul.hi.u32
     kLds32 = 7,     // ld.shared.u32, 32 lanes on 32 banks (one wavefront)
     kLds128 = 8,    // ld.shared.v4.u32, 32 lanes x 16 B (four wavefronts)
-    kOps = 9,
+    kMixed = 9,     // lop3.b32 on half the chains, mad.lo.u32 on the other half (ALU and FMA pipes: issue rate)
+    kOps = 10,
 };
 
 constexpr int kThreads = 1024;
@@ -52,9 +53,18 @@ __device__ __forceinline__ void step(uint32_t (&x)[kChains], unsigned long long 
         } else if constexpr (OP == kImad) {
             asm volatile("mad.lo.u32 %0, %0, %1, %2;" : "+r"(x[c]) : "r"(a), "r"(b));
         } else if constexpr (OP == kImadWide) {
-            asm volatile("mad.wide.u32 %0, %1, %2, %0;" : "+l"(w[c]) : "r"(a), "r"(b + static_cast<uint32_t>(c)));
+            // the multiplicand is the accumulator's low word, so no product can be hoisted
+            asm volatile("{\n\t.reg .u32 lo;\n\tcvt.u32.u64 lo, %0;\n\tmad.wide.u32 %0, lo, %1, %0;\n\t}"
+                         : "+l"(w[c])
+                         : "r"(b));
         } else if constexpr (OP == kImadHi) {
             asm volatile("mul.hi.u32 %0, %0, %1;" : "+r"(x[c]) : "r"(a));
+        } else if constexpr (OP == kMixed) {
+            if (c & 1) {
+                asm volatile("mad.lo.u32 %0, %0, %1, %2;" : "+r"(x[c]) : "r"(a), "r"(b));
+            } else {
+                asm volatile("lop3.b32 %0, %0, %1, %2, 0x96;" : "+r"(x[c]) : "r"(a), "r"(b));
+            }
         } else if constexpr (OP == kLds32) {
             uint32_t v;
             asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(s32 + 128u * static_cast<uint32_t>(c)));
@@ -154,7 +164,8 @@ extern "C" int pipe_rates_run(int op, int iters, double* per_sm_clk, double* mea
         case kImadWide: e = launch<kImadWide>(sms, iters, d_cycles, d_sink); break;
         case kImadHi: e = launch<kImadHi>(sms, iters, d_cycles, d_sink); break;
         case kLds32: e = launch<kLds32>(sms, iters, d_cycles, d_sink); break;
-        default: e = launch<kLds128>(sms, iters, d_cycles, d_sink); break;
+        case kLds128: e = launch<kLds128>(sms, iters, d_cycles, d_sink); break;
+        default: e = launch<kMixed>(sms, iters, d_cycles, d_sink); break;
         }
         if (e == cudaSuccess) {
             e = cudaDeviceSynchronize();

@@ -18,7 +18,7 @@ import json
 
 from . import build
 
-OPS = ("lop3", "iadd", "prmt", "shf", "imad", "imad_wide", "imad_hi", "lds32", "lds128")
+OPS = ("lop3", "iadd", "prmt", "shf", "imad", "imad_wide", "imad_hi", "lds32", "lds128", "lop3_imad_mix")
 
 
 def _lib():
@@ -47,3 +47,13 @@ if __name__ == "__main__":
 
     props = torch.cuda.get_device_properties(torch.cuda.current_device())
     print(json.dumps({"gpu": props.name, "sms": props.multi_processor_count, "rates": measure()}))
+
+
+def model_peaks(rates: dict) -> dict:
+    """Per-SM-per-clock peaks of the units the seal/open kernels load, from
+    measured rates: shared-memory wavefronts (one LDS.32 warp instruction on
+    32 banks is one wavefront), ALU-pipe instructions (LOP3), FMA-pipe
+    instructions (IMAD) and issued instructions (LOP3 and IMAD interleaved),
+    all in threads (one warp instruction = 32)."""
+    r = {k: v["per_sm_clk"] for k, v in rates.items()}
+    return {"l1_wavefronts": r["lds32"] / 32.0, "alu": r["lop3"], "fma": r["imad"], "issue": r["lop3_imad_mix"]}

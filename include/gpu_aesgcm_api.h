@@ -52,9 +52,9 @@ int lmcache_gpu_aes128gcm_key_destroy(lmcache_gpu_aesgcm_key_t key);
 
 /*
  * Pre-size per-call workspace for objects up to max_plaintext_len bytes
- * (reference gpu_aesgcm_api.h:35-44). The workspace here is a fixed-size
- * per-handle ring (1024 accumulation slots) that key_create already
- * allocates, so this only validates the handle and the size limit;
+ * (reference gpu_aesgcm_api.h:35-44). The workspace here is a fixed set of
+ * per-handle accumulation slots (1024, one per stream) that key_create
+ * already allocates, so this only validates the handle;
  * seal/open never call cudaMalloc.
  */
 int lmcache_gpu_aes128gcm_reserve(lmcache_gpu_aesgcm_key_t key, size_t max_plaintext_len);
@@ -68,10 +68,14 @@ int lmcache_gpu_aes128gcm_reserve(lmcache_gpu_aesgcm_key_t key, size_t max_plain
  * rc reports only enqueue errors; the caller synchronises.
  *
  * Concurrency (lifts the reference's one-stream-per-handle rule): several
- * streams and host threads may use one handle at once. Each seal/open call
- * takes the next entry of the handle's 1024-entry ring of accumulation
- * slots, so at most 1024 calls may be outstanding across different streams
- * at a time; calls on one stream are ordered and never collide.
+ * streams and host threads may use one handle at once, with any number of
+ * calls outstanding. Each stream a handle is used on gets one of the handle's
+ * 1024 accumulation slots at its first seal_async / open_async; the calls of
+ * one stream share it (they are ordered on the device). A call on a 1025th
+ * distinct stream returns ERR_ALLOC. A stream destroyed with calls still
+ * pending should not be replaced by a new stream on the same handle before
+ * those calls complete (the new stream may get the old one's handle value,
+ * and with it its slot).
  */
 int lmcache_gpu_aes128gcm_seal_async(lmcache_gpu_aesgcm_key_t key, const void* src,
                                      size_t plaintext_len, void* dst, size_t dst_capacity,
@@ -126,7 +130,7 @@ int lmcache_gpu_aes128gcm_seal_noalloc(const uint8_t* key, size_t key_len, const
  * callers enqueue one seal_async / open_async per object.
  *
  * One call covers `count` objects of any sizes (0 included) and alignments
- * with a fixed number of launches (seal 2, open 3), so thousands of small
+ * with a fixed number of launches (3 each), so thousands of small
  * objects cost one pass over the GPU instead of one launch sequence each.
  * Frames, tags and open's gating are exactly those of seal_async/open_async.
  *
