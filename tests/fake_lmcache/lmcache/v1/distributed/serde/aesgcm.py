@@ -9,8 +9,8 @@ serde type and its backend switch LMCACHE_AESGCM_BACKEND
 * native - the reference's OpenSSL backend lmcache_aes128gcm_seal/open
            (integration/native_aesgcm_serde.py), library from
            LMCACHE_AESGCM_NATIVE_LIB or oracle/_ref/libcpu_seal.so
-* gpu    - the B200 engine (confkv_b200.serde), the value this build adds;
-           the fork's real aesgcm.py gains the same branch.
+* gpu    - the B200 engine (confkv_b200.serde); the fork's real aesgcm.py
+           gains the same branch.
 """
 
 import ctypes
