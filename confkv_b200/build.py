@@ -21,7 +21,7 @@ LIB_NAME = "libgpu_aesgcm.so"
 LIB_PATH = PKG / LIB_NAME
 
 SOURCES = [CSRC / "gpu_aesgcm.cu", CSRC / "batch.cu", CSRC / "host_crypto.cpp"]
-HEADERS = [CSRC / "kernels.cuh", CSRC / "clmul.cuh", CSRC / "tiles.cuh", CSRC / "batch.cuh", CSRC / "small.cuh", CSRC / "host_common.h",
+HEADERS = [CSRC / "kernels.cuh", CSRC / "clmul.cuh", CSRC / "gh5.cuh", CSRC / "tiles.cuh", CSRC / "batch.cuh", CSRC / "small.cuh", CSRC / "host_common.h",
            CSRC / "host_crypto.h", INCLUDE / "gpu_aesgcm_api.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -91,12 +91,20 @@ constexpr uint32_t kSealBatchWalk = kSealBatchSync + kHandoffSyncBytes;
 constexpr uint32_t kSealBatchSmem = kSealBatchWalk + kWalkBytes;
 static_assert(kSealBatchFold == kSmallFold, "the small-object path reads the seal fold slots");
 static_assert(kSealBatchSmem <= 227u * 1024u, "batched seal shared memory exceeds the per-block limit");
-// Batched open-GHASH shared memory: the single-object layout up to the
-// compact H^512 table, then the hand-off.
-constexpr uint32_t kOpenBatchHandoff = kOpenHt + 8192u;
+// Shared memory of the batched GHASH passes (open, two-pass seal): the
+// replicated table of the chain multiplier (5-bit windows when
+// kGhashTable5: 26 lookups of 16 B per multiply instead of 32, i.e. 3.25
+// shared-memory wavefronts per block instead of 4), the fold tables H^1 ..
+// H^512 (the last one doubles as the chain combine's H^512), the hand-off.
+constexpr bool kGhashTable5 = true;
+constexpr uint32_t kGhPassGh = 0;
+constexpr uint32_t kGhPassFold = kGhPassGh + (kGhashTable5 ? static_cast<uint32_t>(kGh5RepBytes) : kGhBytes);
+constexpr uint32_t kGhPassHt = kGhPassFold + kFoldBytes;
+constexpr uint32_t kOpenBatchHandoff = kGhPassHt + 8192u;
 constexpr uint32_t kOpenBatchSync = kOpenBatchHandoff + kHandoffBytes;
 constexpr uint32_t kOpenBatchWalk = kOpenBatchSync + kHandoffSyncBytes;
 constexpr uint32_t kOpenBatchSmem = kOpenBatchWalk + kWalkBytes;
+static_assert(kOpenBatchSmem <= 227u * 1024u, "batched GHASH shared memory exceeds the per-block limit");
 
 // Alignment classes: 2 v + p, v = the frame's ciphertext class (seal: store
 // funnel word part 0..3, 4 = aligned; open: load funnel word part, same
@@ -1220,7 +1228,7 @@ template <bool SEAL, int LQ>
 __device__ __forceinline__ bool ghash_class(uint8_t* smem, const BatchArgs& a, const BatchCta& c, const Handoff& h,
                                             const WalkSlot& ws, int pass)
 {
-    const uint4* ft = reinterpret_cast<const uint4*>(smem + kOpenFold);
+    const uint4* ft = reinterpret_cast<const uint4*>(smem + kGhPassFold);
     for (;;) {
         uint4 q;
         {
@@ -1236,8 +1244,8 @@ __device__ __forceinline__ bool ghash_class(uint8_t* smem, const BatchArgs& a, c
             (void)lq;
             const OpenTile t{frame, it->capacity, P, segment_base(sg, P), static_cast<int64_t>(sg.r1 - sg.r0),
                              load_r};
-            q = open_ghash_rows<LQ, kOpenBatchChains, kOpenBatchAluChains, kOpenBatchStepRows>(
-                t, reinterpret_cast<const uint4*>(smem + kOpenHt), &a.open_cm, c.tid, c.lane);
+            q = open_ghash_rows<LQ, kOpenBatchChains, kOpenBatchAluChains, kOpenBatchStepRows, kGhashTable5, kGhPassGh>(
+                t, reinterpret_cast<const uint4*>(smem + kGhPassHt), &a.open_cm, c.tid, c.lane);
         }
         const bool chunk_done = *walk_word(ws, 1) == kChunkEnd;
         uint32_t taken = 0;
@@ -1268,7 +1276,7 @@ template <bool SEAL>
 __device__ __forceinline__ void ghash_power_loop(const uint8_t* smem, const BatchArgs& a, const BatchCta& c,
                                                  const Handoff& h, uint32_t chunk)
 {
-    const uint4* t4 = reinterpret_cast<const uint4*>(smem + kOpenFold) + 4 * 512;
+    const uint4* t4 = reinterpret_cast<const uint4*>(smem + kGhPassFold) + 4 * 512;
     Cursor cur;
     bool more = cursor_open(c, chunk, cur) && (!SEAL || a.stall == 0u);
     for (uint32_t j = 0; more; ++j) {
@@ -1324,8 +1332,12 @@ __device__ __forceinline__ void ghash_batch_cta(const BatchArgs& a, int pass)
             return;
         }
     }
-    fill_gh_smem(smem + kOpenGh, a.kt.gh_chain);
-    fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kOpenFold), a.kt.gh_pow2);
+    if constexpr (kGhashTable5) {
+        fill_gh5_smem(smem + kGhPassGh, a.kt.gh_chain5);
+    } else {
+        fill_gh_smem(smem + kGhPassGh, a.kt.gh_chain);
+    }
+    fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kGhPassFold), a.kt.gh_pow2);
     const Handoff h = handoff_at(smem, kOpenBatchHandoff, kOpenBatchSync);
     if (tid == 0) {
         handoff_init(h, a.wait_ns);

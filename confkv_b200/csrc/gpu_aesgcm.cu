@@ -426,7 +426,8 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
     constexpr size_t kTab = confkv::kGhashTableBytes;
     const size_t off_pow2 = kAesT;
     const size_t off_chain = off_pow2 + kTab * confkv::kPow2Tables;
-    const size_t off_slots = off_chain + kTab;
+    const size_t off_chain5 = off_chain + kTab;
+    const size_t off_slots = off_chain5 + confkv::kGh5CompactBytes;
     const size_t total = off_slots + sizeof(dev::Slot) * kSlots;
 
     uint8_t* host = new (std::nothrow) uint8_t[total];
@@ -446,6 +447,7 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
         // its integer-pipe form
         const Gf128 m = confkv::gf_pow(H, static_cast<uint64_t>(dev::kOpenBatchChains) * dev::kHornerThreads);
         confkv::ghash_table(m, host + off_chain);
+        confkv::ghash_table5(m, host + off_chain5);
         uint8_t pb[16];
         uint32_t pw[4];
         confkv::gf_store(pb, m);
@@ -468,6 +470,7 @@ extern "C" int lmcache_gpu_aes128gcm_key_create(const uint8_t* key, size_t key_l
     h->kt.aes_t = reinterpret_cast<const uint32_t*>(h->d_mem);
     h->kt.gh_pow2 = reinterpret_cast<const uint4*>(h->d_mem + off_pow2);
     h->kt.gh_chain = reinterpret_cast<const uint4*>(h->d_mem + off_chain);
+    h->kt.gh_chain5 = reinterpret_cast<const uint4*>(h->d_mem + off_chain5);
     h->slots = reinterpret_cast<dev::Slot*>(h->d_mem + off_slots);
     *out = reinterpret_cast<lmcache_gpu_aesgcm_key_t>(h);
     return LMCACHE_GPU_AESGCM_OK;

@@ -240,4 +240,27 @@ void ghash_table(Gf128 m, uint8_t* out)
     }
 }
 
+void ghash_table5(Gf128 m, uint8_t* out)
+{
+    Gf128 basis[128];  // basis[e] = x^e * m
+    basis[0] = m;
+    for (int b = 1; b < 128; ++b) {
+        basis[b] = gf_mul_x(basis[b - 1]);
+    }
+    for (int g = 0; g < kGh5Groups; ++g) {
+        for (int v = 0; v < kGh5Values; ++v) {
+            Gf128 acc{0, 0};
+            for (int b = 0; b < 5; ++b) {
+                const int r = 5 * g + b;
+                if (((v >> b) & 1) != 0 && r < 128) {
+                    const Gf128 e = basis[gh5_gcm_index(r)];
+                    acc.hi ^= e.hi;
+                    acc.lo ^= e.lo;
+                }
+            }
+            gf_store(out + (g * kGh5Values + v) * 16, acc);
+        }
+    }
+}
+
 }  // namespace confkv

@@ -6,6 +6,8 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "gh5.cuh"
+
 namespace confkv {
 
 // GF(2^128) element in the SP 800-38D convention: hi holds bytes 0..7 of the
@@ -50,5 +52,9 @@ Gf128 gf_pow(Gf128 h, uint64_t e);
 
 // Fill `out` (kGhashTableBytes) with the 4-bit table for multiplier m.
 void ghash_table(Gf128 m, uint8_t* out);
+
+// Fill `out` (kGh5CompactBytes, gh5.cuh) with the 5-bit-window table for m:
+// entry (g, v) at (g * 32 + v) * 16.
+void ghash_table5(Gf128 m, uint8_t* out);
 
 }  // namespace confkv

@@ -9,8 +9,10 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 
 #include "clmul.cuh"
+#include "gh5.cuh"
 
 namespace confkv {
 namespace dev {
@@ -98,6 +100,7 @@ struct KeyTables {
     const uint32_t* aes_t;   // T0..T3, 4 x 256 words
     const uint4* gh_pow2;    // compact 4-bit tables (512 entries) for H^(2^k), k = 0..35
     const uint4* gh_chain;   // compact 4-bit table of the batched GHASH passes' chain multiplier H^(kOpenBatchChains T)
+    const uint4* gh_chain5;  // the same multiplier's 5-bit-window table (gh5.cuh)
 };
 
 struct SealArgs {
@@ -659,6 +662,99 @@ __device__ __forceinline__ uint4 gh_mul_rep(uint4 x, uint32_t lb_lo, uint32_t lb
     return make_uint4(a0, a1, a2, a3);
 }
 
+// Fill the replicated 5-bit-window table region (kGh5RepBytes at gh) from its
+// compact table: 16-byte slot i holds compact entry i >> 3.
+__device__ __forceinline__ void fill_gh5_smem(uint8_t* gh, const uint4* compact)
+{
+    constexpr int kN = kGh5RepBytes / 16;
+    constexpr int kBatch = 4;  // loads in flight per thread
+    for (int i0 = static_cast<int>(threadIdx.x); i0 < kN; i0 += kBatch * static_cast<int>(blockDim.x)) {
+        uint4 e[kBatch];
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+            const int i = i0 + k * static_cast<int>(blockDim.x);
+            e[k] = i < kN ? __ldg(compact + (i >> 3)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+            const int i = i0 + k * static_cast<int>(blockDim.x);
+            if (i < kN) {
+                reinterpret_cast<uint4*>(gh)[i] = e[k];
+            }
+        }
+    }
+}
+
+// One group of gh_mul_rep5: XOR M's entry for field G of w into (a0..a3).
+// The field's shift, the mask and the replica offset are issued with the
+// load in one asm statement (the shift as gh5_field_at7 does it), so the
+// addresses are formed one group at a time.
+template <uint32_t GH, int G>
+__device__ __forceinline__ void gh5_acc(const uint32_t (&w)[4], uint32_t lb, uint32_t& a0, uint32_t& a1, uint32_t& a2,
+                                        uint32_t& a3)
+{
+    constexpr int r0 = 5 * G;
+    constexpr int wi = r0 >> 5;
+    constexpr int sh = r0 & 31;
+    constexpr uint32_t imm = kDynSmemBase + GH + static_cast<uint32_t>(G) * kGh5GroupStride;
+    uint4 e;
+    if constexpr (sh < 7) {
+        asm volatile(
+            "{\n\t.reg .b32 t;\n\tshl.b32 t, %4, %5;\n\tand.b32 t, t, 0xF80;\n\tor.b32 t, t, %6;\n\t"
+            "ld.shared.v4.u32 {%0, %1, %2, %3}, [t+%7];\n\t}"
+            : "=r"(e.x), "=r"(e.y), "=r"(e.z), "=r"(e.w)
+            : "r"(w[wi]), "n"(7 - sh), "r"(lb), "n"(imm));
+    } else if constexpr (sh + 5 <= 32 || wi == 3) {
+        asm volatile(
+            "{\n\t.reg .b32 t;\n\tshr.b32 t, %4, %5;\n\tand.b32 t, t, 0xF80;\n\tor.b32 t, t, %6;\n\t"
+            "ld.shared.v4.u32 {%0, %1, %2, %3}, [t+%7];\n\t}"
+            : "=r"(e.x), "=r"(e.y), "=r"(e.z), "=r"(e.w)
+            : "r"(w[wi]), "n"(sh - 7), "r"(lb), "n"(imm));
+    } else {
+        asm volatile(
+            "{\n\t.reg .b32 t;\n\tshf.r.clamp.b32 t, %4, %5, %6;\n\tand.b32 t, t, 0xF80;\n\tor.b32 t, t, %7;\n\t"
+            "ld.shared.v4.u32 {%0, %1, %2, %3}, [t+%8];\n\t}"
+            : "=r"(e.x), "=r"(e.y), "=r"(e.z), "=r"(e.w)
+            : "r"(w[wi]), "r"(w[wi + 1]), "n"(sh - 7), "r"(lb), "n"(imm));
+    }
+    a0 ^= e.x;
+    a1 ^= e.y;
+    a2 ^= e.z;
+    a3 ^= e.w;
+}
+
+// Groups 2P and 2P+1 of gh_mul_rep5, XORed together before the accumulator.
+template <uint32_t GH, int P>
+__device__ __forceinline__ void gh5_acc_pair(const uint32_t (&w)[4], uint32_t lb, uint32_t& a0, uint32_t& a1,
+                                             uint32_t& a2, uint32_t& a3)
+{
+    uint32_t e0 = 0, e1 = 0, e2 = 0, e3 = 0;
+    gh5_acc<GH, 2 * P>(w, lb, e0, e1, e2, e3);
+    gh5_acc<GH, 2 * P + 1>(w, lb, e0, e1, e2, e3);
+    a0 ^= e0;
+    a1 ^= e1;
+    a2 ^= e2;
+    a3 ^= e3;
+}
+
+template <uint32_t GH, int... P>
+__device__ __forceinline__ uint4 gh5_mul_groups(const uint32_t (&w)[4], uint32_t lb, std::integer_sequence<int, P...>)
+{
+    uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+    (gh5_acc_pair<GH, P>(w, lb, a0, a1, a2, a3), ...);
+    return make_uint4(a0, a1, a2, a3);
+}
+
+// x * M using the replicated 5-bit-window table of M at dynamic offset GH
+// (26 LDS.128, no bank conflicts; lb = (lane & 7) << 4 picks the replica).
+template <uint32_t GH>
+__device__ __forceinline__ uint4 gh_mul_rep5(uint4 x, uint32_t lb)
+{
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+    static_assert(kGh5Groups % 2 == 0, "groups are taken in pairs");
+    return gh5_mul_groups<GH>(w, lb, std::make_integer_sequence<int, kGh5Groups / 2>{});
+}
+
 // x * M using a compact (non-replicated) table, shared or global memory.
 __device__ __forceinline__ uint4 gh_mul_compact(uint4 x, const uint4* tab)
 {
@@ -693,6 +789,26 @@ __device__ __forceinline__ void chain_push_dyn(Chains<R>& ch, int k, uint4 c, ui
         }
     }
     v = xor4(gh_mul_rep<GH>(v, lb_lo, lb_hi), c);
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+        if (k == j) {
+            ch.q[j] = v;
+        }
+    }
+}
+
+// chain_push_dyn with the replicated 5-bit-window table of M at GH.
+template <uint32_t GH, int R>
+__device__ __forceinline__ void chain_push_dyn5(Chains<R>& ch, int k, uint4 c, uint32_t lb)
+{
+    uint4 v = ch.q[0];
+#pragma unroll
+    for (int j = 1; j < R; ++j) {
+        if (k == j) {
+            v = ch.q[j];
+        }
+    }
+    v = xor4(gh_mul_rep5<GH>(v, lb), c);
 #pragma unroll
     for (int j = 0; j < R; ++j) {
         if (k == j) {

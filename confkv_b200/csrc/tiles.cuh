@@ -275,14 +275,15 @@ struct OpenTile {
 // Row warps of an open-GHASH tile: the thread's GHASH share over the
 // ciphertext at frame + 13 with R chains (multiplier M = H^(R T)), combined
 // with the compact H^T table `ht`. In the interior rows chains
-// k < R - NALU multiply with the replicated table of M at kOpenGh
-// (shared-memory pipe) and the others with clmul (integer pipes, M's
-// operands `cm` read from the kernel parameters), keeping their value in
-// clmul's integer domain until the interior rows end; S interior rows are
-// read at a time, the next S prefetched. Edge rows use the table for every
-// chain. Interior rows hold blocks 1 <= i < P/16, so both aligned chunks of
-// every block lie inside the frame and no checks are needed.
-template <int LQ, int R, int NALU, int S>
+// k < R - NALU multiply with the replicated table of M at shared offset GH
+// (shared-memory pipe; 4-bit table, or the 5-bit-window table when T5) and
+// the others with clmul (integer pipes, M's operands `cm` read from the
+// kernel parameters), keeping their value in clmul's integer domain until
+// the interior rows end; S interior rows are read at a time, the next S
+// prefetched. Edge rows use the table for every chain. Interior rows hold
+// blocks 1 <= i < P/16, so both aligned chunks of every block lie inside the
+// frame and no checks are needed.
+template <int LQ, int R, int NALU, int S, bool T5 = false, uint32_t GH = kOpenGh>
 __device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4* ht, const ClmulConst* cm, int tid,
                                                  int lane)
 {
@@ -312,7 +313,11 @@ __device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4*
     auto generic_row = [&](int64_t r) __attribute__((always_inline)) {
         const int64_t i = base + r * T + tid;
         const uint4 c = ct_finish<LQ>(ct_prefetch<LQ>(t.frame, t.frame_len, i, P), t.frame, i, P, fsel);
-        chain_push_dyn<kOpenGh, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
+        if constexpr (T5) {
+            chain_push_dyn5<GH, R>(ch, static_cast<int>(r % R), c, lb_lo);
+        } else {
+            chain_push_dyn<GH, R>(ch, static_cast<int>(r % R), c, lb_lo, lb_hi);
+        }
     };
 
     int64_t r = base < 0 ? (-base) / T : 0;  // rows below hold no block of the object
@@ -347,6 +352,11 @@ __device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4*
         for (int64_t g = 0; g < ngroups; ++g) {
 #pragma unroll
             for (int h = 0; h < R / S; ++h) {
+                if constexpr (T5) {
+                    // keeps the compiler from interleaving the steps' table
+                    // multiplies (26 loads each), which overflowed the registers
+                    __syncwarp();
+                }
                 uint4 cd[S], ce[S];
 #pragma unroll
                 for (int k = 0; k < S; ++k) {
@@ -368,7 +378,11 @@ __device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4*
                     const CtRaw raw{cd[k], ce[k], true};
                     const uint4 c = ct_finish<LQ>(raw, t.frame, 0, P, fsel);
                     if (chain < kTabChains) {
-                        ch.q[chain] = xor4(gh_mul_rep<kOpenGh>(ch.q[chain], lb_lo, lb_hi), c);
+                        if constexpr (T5) {
+                            ch.q[chain] = xor4(gh_mul_rep5<GH>(ch.q[chain], lb_lo), c);
+                        } else {
+                            ch.q[chain] = xor4(gh_mul_rep<GH>(ch.q[chain], lb_lo, lb_hi), c);
+                        }
                     } else {
                         const uint32_t craw[4] = {c.x, c.y, c.z, c.w};
                         uint32_t ci[4];

@@ -1,8 +1,9 @@
-"""The integer-pipe GF(2^128) multiply (confkv_b200/csrc/clmul.cuh), compiled
-for the host, against the oracle's bit-serial SP 800-38D multiply
-(reference gpu_aesgcm.cu:195-248) and GHASH. The GPU kernels compile the same
-header, so these CPU checks cover its arithmetic; the GPU tests cover the
-kernels that use it."""
+"""The integer-pipe GF(2^128) multiply (confkv_b200/csrc/clmul.cuh) and the
+5-bit-window tables (confkv_b200/csrc/gh5.cuh with the product's host table
+builder), compiled for the host, against the oracle's bit-serial SP 800-38D
+multiply (reference gpu_aesgcm.cu:195-248) and GHASH. The GPU kernels compile
+the same headers, so these CPU checks cover their arithmetic; the GPU tests
+cover the kernels that use them."""
 
 import ctypes
 import subprocess
@@ -82,3 +83,27 @@ def test_horner_chain_matches_ghash(clmul, oracle, h5):
         out = ctypes.create_string_buffer(16)
         clmul.clmul_check_ghash(h, data + length_block, nblocks + 1, out, h5)
         assert out.raw == oracle.ghash_ct(h, data)
+
+
+@pytest.fixture(scope="module")
+def gh5(tmp_path_factory):
+    so = tmp_path_factory.mktemp("gh5") / "libgh5_check.so"
+    csrc = ROOT / "confkv_b200" / "csrc"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wextra", "-I", str(csrc),
+                    str(ROOT / "tests" / "native" / "gh5_check.cpp"), str(csrc / "host_crypto.cpp"), "-o", str(so)],
+                   check=True)
+    lib = ctypes.CDLL(str(so))
+    lib.gh5_check_mul.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p]
+    lib.gh5_check_mul.restype = None
+    return lib
+
+
+def test_five_bit_window_tables_match_bit_serial_multiply(gh5, oracle):
+    rng = np.random.default_rng(55)
+    edges = list(_edge_blocks())
+    cases = [(rng.bytes(16), rng.bytes(16)) for _ in range(300)]
+    cases += [(a, m) for a in edges for m in edges[:6]]
+    for x, m in cases:
+        out = ctypes.create_string_buffer(16)
+        gh5.gh5_check_mul(x, m, out)
+        assert out.raw == oracle.gf_mul(x, m), (x.hex(), m.hex())
