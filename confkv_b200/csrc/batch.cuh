@@ -92,14 +92,18 @@ constexpr uint32_t kSealBatchSmem = kSealBatchWalk + kWalkBytes;
 static_assert(kSealBatchFold == kSmallFold, "the small-object path reads the seal fold slots");
 static_assert(kSealBatchSmem <= 227u * 1024u, "batched seal shared memory exceeds the per-block limit");
 // Shared memory of the batched GHASH passes (open, two-pass seal): the
-// replicated table of the chain multiplier (5-bit windows when
-// kGhashTable5: 26 lookups of 16 B per multiply instead of 32, i.e. 3.25
-// shared-memory wavefronts per block instead of 4), the fold tables H^1 ..
-// H^512 (the last one doubles as the chain combine's H^512), the hand-off.
+// replicated table of the chain multiplier (kGhW-bit windows when
+// kGhashTable5: 26 (W = 5) or 22 (W = 6) lookups of 16 B per multiply
+// instead of 32, i.e. 3.25 or 2.75 shared-memory wavefronts per block
+// instead of 4), the fold tables of H^1 .. H^8 (row warps) and, when room is
+// left, of H^16 .. H^256 (the power warp reads them from global memory
+// otherwise: the 176 KiB of a 6-bit table leave none), the compact table of
+// H^512 (the chain combine), the hand-off.
 constexpr bool kGhashTable5 = true;
+constexpr int kGhPassFoldLevels = (kGhashTable5 && kGhW > 5) ? 4 : kFoldLevels;
 constexpr uint32_t kGhPassGh = 0;
 constexpr uint32_t kGhPassFold = kGhPassGh + (kGhashTable5 ? static_cast<uint32_t>(kGh5RepBytes) : kGhBytes);
-constexpr uint32_t kGhPassHt = kGhPassFold + kFoldBytes;
+constexpr uint32_t kGhPassHt = kGhPassFold + static_cast<uint32_t>(kGhPassFoldLevels) * 8192u;
 constexpr uint32_t kOpenBatchHandoff = kGhPassHt + 8192u;
 constexpr uint32_t kOpenBatchSync = kOpenBatchHandoff + kHandoffBytes;
 constexpr uint32_t kOpenBatchWalk = kOpenBatchSync + kHandoffSyncBytes;
@@ -1276,7 +1280,9 @@ template <bool SEAL>
 __device__ __forceinline__ void ghash_power_loop(const uint8_t* smem, const BatchArgs& a, const BatchCta& c,
                                                  const Handoff& h, uint32_t chunk)
 {
-    const uint4* t4 = reinterpret_cast<const uint4*>(smem + kGhPassFold) + 4 * 512;
+    const uint4* t4 = (kGhPassFoldLevels == kFoldLevels ? reinterpret_cast<const uint4*>(smem + kGhPassFold)
+                                                         : a.kt.gh_pow2) +
+                      4 * 512;
     Cursor cur;
     bool more = cursor_open(c, chunk, cur) && (!SEAL || a.stall == 0u);
     for (uint32_t j = 0; more; ++j) {
@@ -1337,7 +1343,8 @@ __device__ __forceinline__ void ghash_batch_cta(const BatchArgs& a, int pass)
     } else {
         fill_gh_smem(smem + kGhPassGh, a.kt.gh_chain);
     }
-    fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kGhPassFold), a.kt.gh_pow2);
+    fill_smem<kGhPassFoldLevels * 512>(reinterpret_cast<uint4*>(smem + kGhPassFold), a.kt.gh_pow2);
+    fill_smem<512>(reinterpret_cast<uint4*>(smem + kGhPassHt), a.kt.gh_pow2 + kFoldLevels * 512);
     const Handoff h = handoff_at(smem, kOpenBatchHandoff, kOpenBatchSync);
     if (tid == 0) {
         handoff_init(h, a.wait_ns);

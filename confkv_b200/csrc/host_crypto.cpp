@@ -250,8 +250,8 @@ void ghash_table5(Gf128 m, uint8_t* out)
     for (int g = 0; g < kGh5Groups; ++g) {
         for (int v = 0; v < kGh5Values; ++v) {
             Gf128 acc{0, 0};
-            for (int b = 0; b < 5; ++b) {
-                const int r = 5 * g + b;
+            for (int b = 0; b < kGhW; ++b) {
+                const int r = kGhW * g + b;
                 if (((v >> b) & 1) != 0 && r < 128) {
                     const Gf128 e = basis[gh5_gcm_index(r)];
                     acc.hi ^= e.hi;

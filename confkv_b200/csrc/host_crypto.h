@@ -53,8 +53,8 @@ Gf128 gf_pow(Gf128 h, uint64_t e);
 // Fill `out` (kGhashTableBytes) with the 4-bit table for multiplier m.
 void ghash_table(Gf128 m, uint8_t* out);
 
-// Fill `out` (kGh5CompactBytes, gh5.cuh) with the 5-bit-window table for m:
-// entry (g, v) at (g * 32 + v) * 16.
+// Fill `out` (kGh5CompactBytes, gh5.cuh) with the kGhW-bit-window table for
+// m: entry (g, v) at (g * kGh5Values + v) * 16.
 void ghash_table5(Gf128 m, uint8_t* out);
 
 }  // namespace confkv

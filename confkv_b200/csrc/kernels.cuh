@@ -29,13 +29,15 @@ constexpr int kOpenChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * k
 // compact table of its own in the key tables); the last
 // kOpenBatchAluChains of them multiply on the integer pipes (clmul.cuh)
 // instead of the shared-memory tables, so the two share the GHASH work. A
-// table multiply costs 4 shared-memory wavefronts per block and ~110 ALU
-// instructions, an integer-pipe multiply ~310 ALU and ~150 FMA-pipe
-// instructions (ncu, B200). Measured on 32 x 32 MiB (open GB/s): tables
-// only 502; one chain in four 549; one in three 538 and two in five 511
-// (both lose although the shared-memory pipe still binds at one in four,
-// 3.40 wavefronts against 2.55 ALU clocks per block: with fewer table rows
-// between its steps the integer-pipe chain's latency shows); one in two 495.
+// table multiply costs 4 shared-memory wavefronts per block with 4-bit
+// tables, 2.75 with the 6-bit windows the batched passes use, and ~110 ALU
+// instructions; an integer-pipe multiply ~310 ALU and ~150 FMA-pipe
+// instructions (ncu, B200). Measured on 32 x 32 MiB (open GB/s) with 4-bit
+// tables: tables only 502; one chain in four 549; one in three 538 and two
+// in five 511 (both lose although the shared-memory pipe still binds at one
+// in four: with fewer table rows between its steps the integer-pipe chain's
+// latency shows); one in two 495. With 6-bit windows: one in four 585,
+// tables only 565, one in five 572, one in three 540, two in five 528.
 // The per-object open keeps two table chains: its tiles are a few dozen
 // rows, where more chains cost more in the edge rows and the combine than
 // they gain.
@@ -100,7 +102,7 @@ struct KeyTables {
     const uint32_t* aes_t;   // T0..T3, 4 x 256 words
     const uint4* gh_pow2;    // compact 4-bit tables (512 entries) for H^(2^k), k = 0..35
     const uint4* gh_chain;   // compact 4-bit table of the batched GHASH passes' chain multiplier H^(kOpenBatchChains T)
-    const uint4* gh_chain5;  // the same multiplier's 5-bit-window table (gh5.cuh)
+    const uint4* gh_chain5;  // the same multiplier's window table (kGhW bits, gh5.cuh)
 };
 
 struct SealArgs {
@@ -662,7 +664,7 @@ __device__ __forceinline__ uint4 gh_mul_rep(uint4 x, uint32_t lb_lo, uint32_t lb
     return make_uint4(a0, a1, a2, a3);
 }
 
-// Fill the replicated 5-bit-window table region (kGh5RepBytes at gh) from its
+// Fill the replicated window table region (kGh5RepBytes at gh) from its
 // compact table: 16-byte slot i holds compact entry i >> 3.
 __device__ __forceinline__ void fill_gh5_smem(uint8_t* gh, const uint4* compact)
 {
@@ -693,29 +695,30 @@ template <uint32_t GH, int G>
 __device__ __forceinline__ void gh5_acc(const uint32_t (&w)[4], uint32_t lb, uint32_t& a0, uint32_t& a1, uint32_t& a2,
                                         uint32_t& a3)
 {
-    constexpr int r0 = 5 * G;
+    constexpr int r0 = kGhW * G;
     constexpr int wi = r0 >> 5;
     constexpr int sh = r0 & 31;
     constexpr uint32_t imm = kDynSmemBase + GH + static_cast<uint32_t>(G) * kGh5GroupStride;
+    constexpr uint32_t mask = kGh5Mask7;
     uint4 e;
     if constexpr (sh < 7) {
         asm volatile(
-            "{\n\t.reg .b32 t;\n\tshl.b32 t, %4, %5;\n\tand.b32 t, t, 0xF80;\n\tor.b32 t, t, %6;\n\t"
+            "{\n\t.reg .b32 t;\n\tshl.b32 t, %4, %5;\n\tand.b32 t, t, %8;\n\tor.b32 t, t, %6;\n\t"
             "ld.shared.v4.u32 {%0, %1, %2, %3}, [t+%7];\n\t}"
             : "=r"(e.x), "=r"(e.y), "=r"(e.z), "=r"(e.w)
-            : "r"(w[wi]), "n"(7 - sh), "r"(lb), "n"(imm));
-    } else if constexpr (sh + 5 <= 32 || wi == 3) {
+            : "r"(w[wi]), "n"(7 - sh), "r"(lb), "n"(imm), "n"(mask));
+    } else if constexpr (sh + kGhW <= 32 || wi == 3) {
         asm volatile(
-            "{\n\t.reg .b32 t;\n\tshr.b32 t, %4, %5;\n\tand.b32 t, t, 0xF80;\n\tor.b32 t, t, %6;\n\t"
+            "{\n\t.reg .b32 t;\n\tshr.b32 t, %4, %5;\n\tand.b32 t, t, %8;\n\tor.b32 t, t, %6;\n\t"
             "ld.shared.v4.u32 {%0, %1, %2, %3}, [t+%7];\n\t}"
             : "=r"(e.x), "=r"(e.y), "=r"(e.z), "=r"(e.w)
-            : "r"(w[wi]), "n"(sh - 7), "r"(lb), "n"(imm));
+            : "r"(w[wi]), "n"(sh - 7), "r"(lb), "n"(imm), "n"(mask));
     } else {
         asm volatile(
-            "{\n\t.reg .b32 t;\n\tshf.r.clamp.b32 t, %4, %5, %6;\n\tand.b32 t, t, 0xF80;\n\tor.b32 t, t, %7;\n\t"
+            "{\n\t.reg .b32 t;\n\tshf.r.clamp.b32 t, %4, %5, %6;\n\tand.b32 t, t, %9;\n\tor.b32 t, t, %7;\n\t"
             "ld.shared.v4.u32 {%0, %1, %2, %3}, [t+%8];\n\t}"
             : "=r"(e.x), "=r"(e.y), "=r"(e.z), "=r"(e.w)
-            : "r"(w[wi]), "r"(w[wi + 1]), "n"(sh - 7), "r"(lb), "n"(imm));
+            : "r"(w[wi]), "r"(w[wi + 1]), "n"(sh - 7), "r"(lb), "n"(imm), "n"(mask));
     }
     a0 ^= e.x;
     a1 ^= e.y;
@@ -745,8 +748,8 @@ __device__ __forceinline__ uint4 gh5_mul_groups(const uint32_t (&w)[4], uint32_t
     return make_uint4(a0, a1, a2, a3);
 }
 
-// x * M using the replicated 5-bit-window table of M at dynamic offset GH
-// (26 LDS.128, no bank conflicts; lb = (lane & 7) << 4 picks the replica).
+// x * M using the replicated kGhW-bit-window table of M at dynamic offset GH
+// (kGh5Groups LDS.128, no bank conflicts; lb = (lane & 7) << 4 picks the replica).
 template <uint32_t GH>
 __device__ __forceinline__ uint4 gh_mul_rep5(uint4 x, uint32_t lb)
 {
@@ -797,7 +800,7 @@ __device__ __forceinline__ void chain_push_dyn(Chains<R>& ch, int k, uint4 c, ui
     }
 }
 
-// chain_push_dyn with the replicated 5-bit-window table of M at GH.
+// chain_push_dyn with the replicated window table of M at GH.
 template <uint32_t GH, int R>
 __device__ __forceinline__ void chain_push_dyn5(Chains<R>& ch, int k, uint4 c, uint32_t lb)
 {

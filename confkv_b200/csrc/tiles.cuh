@@ -276,7 +276,7 @@ struct OpenTile {
 // ciphertext at frame + 13 with R chains (multiplier M = H^(R T)), combined
 // with the compact H^T table `ht`. In the interior rows chains
 // k < R - NALU multiply with the replicated table of M at shared offset GH
-// (shared-memory pipe; 4-bit table, or the 5-bit-window table when T5) and
+// (shared-memory pipe; 4-bit table, or the kGhW-bit window table when T5) and
 // the others with clmul (integer pipes, M's operands `cm` read from the
 // kernel parameters), keeping their value in clmul's integer domain until
 // the interior rows end; S interior rows are read at a time, the next S
@@ -354,7 +354,7 @@ __device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4*
             for (int h = 0; h < R / S; ++h) {
                 if constexpr (T5) {
                     // keeps the compiler from interleaving the steps' table
-                    // multiplies (26 loads each), which overflowed the registers
+                    // multiplies (kGh5Groups loads each), which overflowed the registers
                     __syncwarp();
                 }
                 uint4 cd[S], ce[S];

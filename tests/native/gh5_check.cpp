@@ -1,4 +1,4 @@
-// Host check of the 5-bit-window GHASH tables (test infrastructure, compiled
+// Host check of the window GHASH tables (kGhW bits) (test infrastructure, compiled
 // by tests/test_clmul.py with g++ together with the product's
 // confkv_b200/csrc/host_crypto.cpp): x * M from ghash_table5 and the field
 // extraction the kernels use (gh5_field_at7).
@@ -15,7 +15,7 @@ template <int... G>
 void xor_groups(const uint32_t (&w)[4], const uint8_t* tab, uint8_t out[16], std::integer_sequence<int, G...>)
 {
     auto one = [&](int g, uint32_t field7) {
-        const uint32_t v = (field7 & 0xF80u) >> 7;
+        const uint32_t v = (field7 & confkv::kGh5Mask7) >> 7;
         const uint8_t* e = tab + (g * confkv::kGh5Values + v) * 16;
         for (int b = 0; b < 16; ++b) {
             out[b] ^= e[b];

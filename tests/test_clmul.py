@@ -1,5 +1,5 @@
 """The integer-pipe GF(2^128) multiply (confkv_b200/csrc/clmul.cuh) and the
-5-bit-window tables (confkv_b200/csrc/gh5.cuh with the product's host table
+window tables of the batched GHASH passes (confkv_b200/csrc/gh5.cuh with the product's host table
 builder), compiled for the host, against the oracle's bit-serial SP 800-38D
 multiply (reference gpu_aesgcm.cu:195-248) and GHASH. The GPU kernels compile
 the same headers, so these CPU checks cover their arithmetic; the GPU tests
@@ -85,12 +85,13 @@ def test_horner_chain_matches_ghash(clmul, oracle, h5):
         assert out.raw == oracle.ghash_ct(h, data)
 
 
-@pytest.fixture(scope="module")
-def gh5(tmp_path_factory):
-    so = tmp_path_factory.mktemp("gh5") / "libgh5_check.so"
+@pytest.fixture(scope="module", params=[5, 6], ids=["window5", "window6"])
+def gh5(request, tmp_path_factory):
+    so = tmp_path_factory.mktemp("gh5") / f"libgh5_check_w{request.param}.so"
     csrc = ROOT / "confkv_b200" / "csrc"
     subprocess.run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wextra", "-I", str(csrc),
-                    str(ROOT / "tests" / "native" / "gh5_check.cpp"), str(csrc / "host_crypto.cpp"), "-o", str(so)],
+                    f"-DCONFKV_GH_WINDOW={request.param}", str(ROOT / "tests" / "native" / "gh5_check.cpp"),
+                    str(csrc / "host_crypto.cpp"), "-o", str(so)],
                    check=True)
     lib = ctypes.CDLL(str(so))
     lib.gh5_check_mul.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p]
@@ -98,7 +99,7 @@ def gh5(tmp_path_factory):
     return lib
 
 
-def test_five_bit_window_tables_match_bit_serial_multiply(gh5, oracle):
+def test_window_tables_match_bit_serial_multiply(gh5, oracle):
     rng = np.random.default_rng(55)
     edges = list(_edge_blocks())
     cases = [(rng.bytes(16), rng.bytes(16)) for _ in range(300)]
