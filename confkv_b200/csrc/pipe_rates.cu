@@ -29,7 +29,9 @@ enum PipeOp : int {
     kLds32 = 7,     // ld.shared.u32, 32 lanes on 32 banks (one wavefront)
     kLds128 = 8,    // ld.shared.v4.u32, 32 lanes x 16 B (four wavefronts)
     kMixed = 9,     // lop3.b32 on half the chains, mad.lo.u32 on the other half (ALU and FMA pipes: issue rate)
-    kOps = 10,
+    kShfl = 10,     // shfl.sync.idx.b32 from lane ^ 1
+    kLdsShfl = 11,  // ld.shared.u32 (one wavefront) on half the chains, shfl.sync on the other half
+    kOps = 12,
 };
 
 constexpr int kThreads = 1024;
@@ -38,7 +40,7 @@ constexpr int kUnroll = 16;
 
 template <int OP>
 __device__ __forceinline__ void step(uint32_t (&x)[kChains], unsigned long long (&w)[kChains], uint32_t a,
-                                     uint32_t b, uint32_t s32, uint32_t s128)
+                                     uint32_t b, uint32_t s32, uint32_t s128, uint32_t src_lane)
 {
 #pragma unroll
     for (int c = 0; c < kChains; ++c) {
@@ -65,7 +67,9 @@ __device__ __forceinline__ void step(uint32_t (&x)[kChains], unsigned long long 
             } else {
                 asm volatile("lop3.b32 %0, %0, %1, %2, 0x96;" : "+r"(x[c]) : "r"(a), "r"(b));
             }
-        } else if constexpr (OP == kLds32) {
+        } else if (OP == kShfl || (OP == kLdsShfl && (c & 1))) {  // c is unrolled: folds at compile time
+            asm volatile("shfl.sync.idx.b32 %0, %0, %1, 31, 0xffffffff;" : "+r"(x[c]) : "r"(src_lane));
+        } else if constexpr (OP == kLds32 || OP == kLdsShfl) {
             uint32_t v;
             asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(s32 + 128u * static_cast<uint32_t>(c)));
             x[c] ^= v;
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1) pipe_kernel(int iters, unsigned l
     for (int it = 0; it < iters; ++it) {
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            step<OP>(x, w, a, b, s32, s128);
+            step<OP>(x, w, a, b, s32, s128, lane ^ 1u);
         }
     }
     __syncthreads();
@@ -165,6 +169,8 @@ extern "C" int pipe_rates_run(int op, int iters, double* per_sm_clk, double* mea
         case kImadHi: e = launch<kImadHi>(sms, iters, d_cycles, d_sink); break;
         case kLds32: e = launch<kLds32>(sms, iters, d_cycles, d_sink); break;
         case kLds128: e = launch<kLds128>(sms, iters, d_cycles, d_sink); break;
+        case kShfl: e = launch<kShfl>(sms, iters, d_cycles, d_sink); break;
+        case kLdsShfl: e = launch<kLdsShfl>(sms, iters, d_cycles, d_sink); break;
         default: e = launch<kMixed>(sms, iters, d_cycles, d_sink); break;
         }
         if (e == cudaSuccess) {

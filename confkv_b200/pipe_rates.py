@@ -18,7 +18,8 @@ import json
 
 from . import build
 
-OPS = ("lop3", "iadd", "prmt", "shf", "imad", "imad_wide", "imad_hi", "lds32", "lds128", "lop3_imad_mix")
+OPS = ("lop3", "iadd", "prmt", "shf", "imad", "imad_wide", "imad_hi", "lds32", "lds128", "lop3_imad_mix", "shfl",
+       "lds32_shfl_mix")
 
 
 def _lib():
