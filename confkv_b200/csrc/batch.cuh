@@ -211,13 +211,18 @@ __host__ __device__ __forceinline__ uint32_t batch_chunk_count(unsigned long lon
 // which leaves the shared-memory pipe less loaded per block. Every segment
 // then pays its start-up and fold twice, and the second pass its own launch
 // tail, so two passes win only on batches with many rows per SM and long
-// tile objects. Measured on B200 (seal GB/s, fused -> two passes): 32 x
-// 32 MiB 494 -> 536, 64 x 10 MiB 490 -> 525, 128 x 2 MiB 467 -> 485, one
-// 1 GiB object 495 -> 540, 4 x 64 MiB 474 -> 497; but 64 x 2 MiB 442 -> 431,
-// 32 x 4 MiB 450 -> 438, 48 x 3 MiB 449 -> 446, 64 x 1 MiB 398 -> 374 and the
-// 4096-object ragged batch (23 rows per tile object) 368 -> 344.
-constexpr unsigned long long kTwoPassMinRowsPerSm = 192;
-constexpr unsigned long long kTwoPassMinRowsPerObject = 256;
+// tile objects (a row is kHornerThreads blocks, 8 KiB). Measured on B200
+// with the 6-bit-window GHASH pass (seal GB/s, fused -> two passes; rows per
+// SM, rows per object): 4 x 64 MiB 470 -> 518 (221, 8192); 8 x 32 MiB
+// 470 -> 506 (221, 4096); 64 x 2 MiB 436 -> 444 (110, 256); 128 x 1 MiB 429 -> 439 (110, 128); 192 x 768 KiB
+// 435 -> 438 (125, 96); 96 x 2 MiB 452 -> 477 (166, 256); ties at 112 x
+// 1 MiB 423 / 423 (97, 128), 56 x 2 MiB (97, 256) and 256 x 512 KiB (110,
+// 64); fused wins at 96 x 1 MiB 412 -> 409 (83), 80 x 1 MiB 405 -> 389 (69),
+// 64 x 1 MiB 385 -> 370 (55), 384 x 384 KiB 421 -> 417 (125, 48), 512 x
+// 256 KiB 405 -> 388 (110, 32), 1024 x 128 KiB 375 -> 338 (110, 16) and the
+// 4096-object ragged batch (~23 rows per tile object) 374 -> 355.
+constexpr unsigned long long kTwoPassMinRowsPerSm = 104;
+constexpr unsigned long long kTwoPassMinRowsPerObject = 96;
 
 __host__ __device__ __forceinline__ bool seal_two_pass_wins(unsigned long long R, uint32_t K, uint32_t sms)
 {
