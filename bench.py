@@ -79,6 +79,7 @@ def load_peaks() -> tuple[float, str]:
 
 KERNEL_PROFILE = "batched_kernels_kv_llama8b.md"
 PIPE_RATES_PROFILE = "pipe_rates_b200.md"
+SEAL_TWO_PASS_MIN_BYTES = 80 << 20  # kSealTwoPassMinBytes: per-object seals from this size take two launches
 
 
 def kernel_profile(name: str = KERNEL_PROFILE) -> dict:
@@ -361,7 +362,8 @@ def run_ours(args, rank, world, local):
                                   "ms_per_step": round(t / args.steps, 4),
                                   "seal_gbs": round(gbs(ss, nobj * P * world), 2),
                                   "open_gbs": round(gbs(os_, nobj * P * world), 2),
-                                  "round_trip_ok": okp, "gpu_launches": 3 * nobj * args.steps,
+                                  "round_trip_ok": okp,
+                                  "gpu_launches": ((2 if P >= SEAL_TWO_PASS_MIN_BYTES else 1) + 2) * nobj * args.steps,
                                   "api": "one seal_async + one open_async call per object (reference C-ABI)"}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args, plain_u8, key_bytes)

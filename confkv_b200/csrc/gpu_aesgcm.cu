@@ -103,6 +103,34 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
     }
 }
 
+// CTR pass of the per-object two-pass seal: the tiles of seal_kernel,
+// encryption and ciphertext stores only (no GHASH chain, no power warp, so
+// 16 warps of up to 128 registers); CTA 0 writes the header. The GHASH pass
+// (open_ghash_kernel<LQ, true, true>) follows on the stream.
+template <int SQ, bool PT_ALIGNED>
+__global__ void __launch_bounds__(kCtrThreads, 1) seal_ctr_kernel(const SealArgs a)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int tid = threadIdx.x;
+    pdl_release();
+    fill_aes_smem(smem + kSealAes, a.kt.aes_t);
+    pdl_wait();
+    if (blockIdx.x == 0 && tid == 0) {
+        a.frame[0] = 1;
+        for (int b = 0; b < 12; ++b) {
+            a.frame[1 + b] = static_cast<uint8_t>(a.ivw[b >> 2] >> (8 * (b & 3)));
+        }
+    }
+    __syncthreads();
+    const int64_t span = static_cast<int64_t>(a.iters) * kHornerThreads;
+    const SealTile tile{a.src, a.frame + 13, a.plen,
+                        static_cast<int64_t>(a.nblocks) - static_cast<int64_t>(a.grid - blockIdx.x) * span,
+                        static_cast<int64_t>(a.iters),
+                        {a.ivw[0] ^ a.rk[0], a.ivw[1] ^ a.rk[1], a.ivw[2] ^ a.rk[2]},
+                        a.store_r};
+    (void)seal_rows<SQ, PT_ALIGNED, false>(tile, a.rk, a.kt.gh_pow2, tid, tid & 31);
+}
+
 // Zero-length seal: header + tag = E_K(J0) (GHASH of nothing is 0).
 __global__ void seal_empty_kernel(const SealArgs a)
 {
@@ -123,30 +151,37 @@ __global__ void seal_empty_kernel(const SealArgs a)
 
 // ---------------------------------------------------- open: GHASH + verify
 //
-// Same tiles as seal_kernel over the ciphertext at frame + 13, with
-// kOpenChains chains per thread. Every fold table is in shared memory, so
-// the two-stage fold of the batched kernels (tiles.cuh) needs one barrier:
-// each row warp folds its partials with levels 0..3 and hands two values to
-// the power warp, which folds them with levels 4..8. (Seal keeps the block
-// fold: its levels 4..8 would read the key's global tables, five dependent
-// L2 round trips that cost 2 MiB objects 14 %.) The power warp computes
-// E_K(J0) and L*H up front; the last CTA compares the expected tag with the
-// frame's (16 bytes, OR-accumulated) and checks the version byte, then
-// writes *auth_ok.
-template <int LQ>
+// Same tiles as seal_kernel over the ciphertext at frame + 13, with the
+// chains of OpenLayout<WIN> (kernels.cuh). The two-stage fold of the batched
+// kernels (tiles.cuh) needs one barrier here: each row warp folds its
+// partials with levels 0..3 (shared tables) and hands two values to the
+// power warp, which folds them with levels 4..8 (shared or the key's global
+// tables). (Seal keeps the block fold: its levels 4..8 would read the key's
+// global tables, five dependent L2 round trips that cost 2 MiB objects
+// 14 %.) The power warp computes E_K(J0) and L*H up front; the last CTA
+// compares the expected tag with the frame's (16 bytes, OR-accumulated) and
+// checks the version byte, then writes *auth_ok; with SEAL (the GHASH pass
+// of the two-pass seal, frame = the sealed frame) it writes the tag.
+template <int LQ, bool WIN, bool SEAL = false>
 __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenArgs a)
 {
+    using L = OpenLayout<WIN>;
     extern __shared__ __align__(16) uint8_t smem[];
-    uint4* part = reinterpret_cast<uint4*>(smem + kOpenPart);  // the row warps' fold values V_0..V_31
-    const uint4* fold_tabs = reinterpret_cast<const uint4*>(smem + kOpenFold);
+    uint4* part = reinterpret_cast<uint4*>(smem + L::kPart);  // the row warps' fold values V_0..V_31
+    const uint4* fold_tabs = reinterpret_cast<const uint4*>(smem + L::kFold);
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
 
     pdl_release();
-    fill_gh_smem(smem + kOpenGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
-    fill_smem<(kFoldLevels + 1) * 512>(reinterpret_cast<uint4*>(smem + kOpenFold), a.kt.gh_pow2);  // H^(2^l), l <= 9
+    if constexpr (WIN) {
+        fill_gh5_smem(smem + L::kGh, a.kt.gh_chain5);
+    } else {
+        fill_gh_smem(smem + L::kGh, a.kt.gh_pow2 + kOpenChainLog2 * 512);
+    }
+    fill_smem<L::kFoldSmemLevels * 512>(reinterpret_cast<uint4*>(smem + L::kFold), a.kt.gh_pow2);  // H^(2^l)
+    fill_smem<512>(reinterpret_cast<uint4*>(smem + L::kHt), a.kt.gh_pow2 + kFoldLevels * 512);      // H^512
     pdl_wait();
     __syncthreads();
 
@@ -165,8 +200,8 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
         const OpenTile t{a.frame, a.frame_len, P,
                          static_cast<int64_t>(a.nblocks) - static_cast<int64_t>(a.grid - blockIdx.x) * span,
                          static_cast<int64_t>(a.iters), a.load_r};
-        const uint4 q = open_ghash_rows<LQ, kOpenChains, 0, kOpenChains>(t, reinterpret_cast<const uint4*>(smem + kOpenHt),
-                                                                        nullptr, tid, lane);
+        const uint4 q = open_ghash_rows<LQ, L::kChains, L::kAluChains, L::kStepRows, WIN, L::kGh>(
+            t, reinterpret_cast<const uint4*>(smem + L::kHt), &a.cm, tid, lane);
         const uint4 v = warp_fold_pairs<false>(q, fold_tabs, lane);
         if (lane < 2) {
             part[2 * warp + lane] = v;
@@ -175,10 +210,18 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     __syncthreads();
 
     if (warp == kPowerWarp) {
-        const uint4 fold = power_fold(part[lane], fold_tabs + 4 * 512, lane);
+        const uint4* t4 = (L::kFoldSmemLevels == kFoldLevels ? fold_tabs : a.kt.gh_pow2) + 4 * 512;
+        const uint4 fold = power_fold(part[lane], t4, lane);
         unsigned long long shi, slo;
-        if (cta_accumulate(a.slot, fold, uhi, ulo, lane, a.grid, shi, slo) && lane == 0) {
-            *a.auth_ok = open_verdict(a.frame, P, shi, slo, lh, ej0);
+        if (cta_accumulate(a.slot, fold, uhi, ulo, lane, a.grid, shi, slo)) {
+            if constexpr (SEAL) {
+                const uint4 tag = xor4(xor4(be_to_raw(shi, slo), lh), ej0);
+                if (lane < 16) {
+                    a.tag_out[13 + P + lane] = static_cast<uint8_t>(byte_of(tag, lane));
+                }
+            } else if (lane == 0) {
+                *a.auth_ok = open_verdict(a.frame, P, shi, slo, lh, ej0);
+            }
         }
     }
 }
@@ -272,20 +315,40 @@ cudaError_t confkv::host::configure_device(int device)
             }
         };
         chk(allow_smem(dev::seal_kernel<0, true>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<0, true>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<1, true>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<1, true>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<2, true>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<2, true>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<3, true>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<3, true>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<4, true>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<4, true>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<0, false>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<0, false>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<1, false>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<1, false>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<2, false>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<2, false>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<3, false>, dev::kSealSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<3, false>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<4, false>, dev::kSealSmem));
-        chk(allow_smem(dev::open_ghash_kernel<0>, dev::kOpenSmem));
-        chk(allow_smem(dev::open_ghash_kernel<1>, dev::kOpenSmem));
-        chk(allow_smem(dev::open_ghash_kernel<2>, dev::kOpenSmem));
-        chk(allow_smem(dev::open_ghash_kernel<3>, dev::kOpenSmem));
-        chk(allow_smem(dev::open_ghash_kernel<4>, dev::kOpenSmem));
+        chk(allow_smem(dev::seal_ctr_kernel<4, false>, dev::kCtrSmem));
+        chk(allow_smem(dev::open_ghash_kernel<0, false>, dev::OpenLayout<false>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<0, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<0, true, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<1, false>, dev::OpenLayout<false>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<1, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<1, true, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<2, false>, dev::OpenLayout<false>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<2, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<2, true, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<3, false>, dev::OpenLayout<false>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<3, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<3, true, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<4, false>, dev::OpenLayout<false>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<4, true>, dev::OpenLayout<true>::kSmem));
+        chk(allow_smem(dev::open_ghash_kernel<4, true, true>, dev::OpenLayout<true>::kSmem));
         chk(allow_smem(dev::open_ctr_kernel<0, true>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<1, true>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<2, true>, dev::kCtrSmem));
@@ -364,10 +427,28 @@ cudaError_t launch_seal_t(const dev::SealArgs& args, cudaStream_t s)
     return launch_pdl(dev::seal_kernel<SQ, A>, args.grid, dev::kSealThreads, dev::kSealSmem, s, args);
 }
 
+template <int SQ, bool A>
+cudaError_t launch_seal_ctr_t(const dev::SealArgs& args, cudaStream_t s)
+{
+    return launch_pdl(dev::seal_ctr_kernel<SQ, A>, args.grid, dev::kCtrThreads, dev::kCtrSmem, s, args);
+}
+
+template <int LQ>
+cudaError_t launch_seal_ghash_t(const dev::OpenArgs& args, cudaStream_t s)
+{
+    return launch_pdl(dev::open_ghash_kernel<LQ, true, true>, args.grid, dev::kSealThreads,
+                      dev::OpenLayout<true>::kSmem, s, args);
+}
+
 template <int LQ>
 cudaError_t launch_open_ghash_t(const dev::OpenArgs& args, cudaStream_t s)
 {
-    return launch_pdl(dev::open_ghash_kernel<LQ>, args.grid, dev::kSealThreads, dev::kOpenSmem, s, args);
+    if (args.plen >= dev::kOpenWindowMinBytes) {
+        return launch_pdl(dev::open_ghash_kernel<LQ, true>, args.grid, dev::kSealThreads, dev::OpenLayout<true>::kSmem,
+                          s, args);
+    }
+    return launch_pdl(dev::open_ghash_kernel<LQ, false>, args.grid, dev::kSealThreads, dev::OpenLayout<false>::kSmem, s,
+                      args);
 }
 
 template <int LQ, bool A>
@@ -502,6 +583,59 @@ extern "C" int lmcache_gpu_aes128gcm_reserve(lmcache_gpu_aesgcm_key_t key, size_
     return LMCACHE_GPU_AESGCM_OK;
 }
 
+// Large objects: CTR pass (seal_ctr_kernel), then the window-table GHASH
+// pass over the frame's ciphertext, which writes the tag; both on the tiles
+// and the accumulation slot of `args`.
+static int seal_two_pass(const KeyHandle* h, const dev::SealArgs& args, size_t dst_capacity, int sq, bool pt_aligned,
+                  cudaStream_t s)
+{
+    cudaError_t e;
+    if (pt_aligned) {
+        switch (sq) {
+        case 0: e = launch_seal_ctr_t<0, true>(args, s); break;
+        case 1: e = launch_seal_ctr_t<1, true>(args, s); break;
+        case 2: e = launch_seal_ctr_t<2, true>(args, s); break;
+        case 3: e = launch_seal_ctr_t<3, true>(args, s); break;
+        default: e = launch_seal_ctr_t<4, true>(args, s); break;
+        }
+    } else {
+        switch (sq) {
+        case 0: e = launch_seal_ctr_t<0, false>(args, s); break;
+        case 1: e = launch_seal_ctr_t<1, false>(args, s); break;
+        case 2: e = launch_seal_ctr_t<2, false>(args, s); break;
+        case 3: e = launch_seal_ctr_t<3, false>(args, s); break;
+        default: e = launch_seal_ctr_t<4, false>(args, s); break;
+        }
+    }
+    if (e != cudaSuccess) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    dev::OpenArgs oa{};
+    oa.frame = args.frame;
+    oa.frame_len = dst_capacity;
+    oa.plen = args.plen;
+    oa.nblocks = args.nblocks;
+    oa.iters = args.iters;
+    oa.grid = args.grid;
+    std::memcpy(oa.rk, h->rk, sizeof(oa.rk));
+    oa.kt = h->kt;
+    oa.slot = args.slot;
+    oa.cm = h->open_cm;
+    oa.tag_out = args.frame;
+    const uint32_t off = static_cast<uint32_t>((reinterpret_cast<uintptr_t>(args.frame) + 13u) & 15u);
+    const int lq = off == 0 ? 4 : static_cast<int>(off >> 2);
+    oa.load_r = off & 3u;
+    switch (lq) {
+    case 0: e = launch_seal_ghash_t<0>(oa, s); break;
+    case 1: e = launch_seal_ghash_t<1>(oa, s); break;
+    case 2: e = launch_seal_ghash_t<2>(oa, s); break;
+    case 3: e = launch_seal_ghash_t<3>(oa, s); break;
+    default: e = launch_seal_ghash_t<4>(oa, s); break;
+    }
+    std::memset(oa.rk, 0, sizeof(oa.rk));
+    return cuda_rc(e);
+}
+
 extern "C" int lmcache_gpu_aes128gcm_seal_async(lmcache_gpu_aesgcm_key_t key, const void* src,
                                                 size_t plaintext_len, void* dst, size_t dst_capacity,
                                                 const uint8_t* iv, void* stream_ptr)
@@ -554,6 +688,9 @@ extern "C" int lmcache_gpu_aes128gcm_seal_async(lmcache_gpu_aesgcm_key_t key, co
         sq = static_cast<int>(sh >> 2);
         args.store_r = sh & 3u;
     }
+    if (plaintext_len >= dev::kSealTwoPassMinBytes) {
+        return seal_two_pass(h, args, dst_capacity, sq, pt_aligned, s);
+    }
     cudaError_t e;
     if (pt_aligned) {
         switch (sq) {
@@ -605,6 +742,7 @@ extern "C" int lmcache_gpu_aes128gcm_open_async(lmcache_gpu_aesgcm_key_t key, co
     std::memcpy(oa.rk, h->rk, sizeof(oa.rk));
     oa.kt = h->kt;
     oa.auth_ok = auth_ok;
+    oa.cm = h->open_cm;
 
     if (n == 0) {
         return cuda_rc(launch_pdl(dev::open_empty_kernel, 1, 32, 0, s, oa));

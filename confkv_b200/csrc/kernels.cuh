@@ -22,8 +22,7 @@ constexpr int kHornerLog2 = 9;                      // log2(kHornerThreads)
 constexpr int kFoldLevels = kHornerLog2;
 constexpr int kSealChains = 1;                      // GHASH chains per thread in seal
 constexpr int kSealChainLog2 = kHornerLog2;         // chain multiplier H^kHornerThreads
-constexpr int kOpenChains = 2;                      // GHASH chains per thread in the per-object open
-constexpr int kOpenChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * kHornerThreads)
+constexpr int kOpenChainLog2 = kHornerLog2 + 1;     // per-object open, objects below kOpenWindowMinBytes: H^(2 T)
 // The batched GHASH passes (open, and the two-pass seal) run
 // kOpenBatchChains chains per thread (multiplier H^(kOpenBatchChains T), a
 // compact table of its own in the key tables); the last
@@ -38,9 +37,8 @@ constexpr int kOpenChainLog2 = kHornerLog2 + 1;     // chain multiplier H^(2 * k
 // in four: with fewer table rows between its steps the integer-pipe chain's
 // latency shows); one in two 495. With 6-bit windows: one in four 585,
 // tables only 565, one in five 572, one in three 540, two in five 528.
-// The per-object open keeps two table chains: its tiles are a few dozen
-// rows, where more chains cost more in the edge rows and the combine than
-// they gain.
+// The per-object open uses the same split for large objects and two 4-bit
+// table chains below kOpenWindowMinBytes (OpenLayout).
 constexpr int kOpenBatchChains = 4;
 constexpr int kOpenBatchAluChains = 1;
 constexpr int kOpenBatchStepRows = 1;               // interior rows read (and prefetched) at a time
@@ -71,12 +69,42 @@ constexpr uint32_t kSealFold = kSealPart + kPartBytes;
 constexpr uint32_t kSealMisc = kSealFold + kSealFoldSmemLevels * 8192u;
 constexpr uint32_t kSealSmem = kSealMisc + 64;
 
-constexpr uint32_t kOpenGh = 0;
-constexpr uint32_t kOpenFold = kOpenGh + kGhBytes;   // all fold tables, staged in the prologue
-constexpr uint32_t kOpenHt = kOpenFold + kFoldBytes;  // compact table of H^kHornerThreads (chain combine)
-constexpr uint32_t kOpenPart = kOpenHt + 8192u;
-constexpr uint32_t kOpenMisc = kOpenPart + kPartBytes;
-constexpr uint32_t kOpenSmem = kOpenMisc + 64;
+// Per-object open GHASH, two designs (OpenLayout<WIN>), chosen per call by
+// the object's size:
+//   WIN = false (objects under kOpenWindowMinBytes): two chains on the
+//     replicated 4-bit table of H^(2 T); every fold table in shared memory.
+//   WIN = true: the batched GHASH passes' split, kOpenBatchChains chains
+//     (multiplier H^(4 T)), the first on its replicated 6-bit window table
+//     (gh5.cuh), the last kOpenBatchAluChains on the integer pipes; the fold
+//     tables of levels 0..3 in shared memory, levels 4..8 from the key's
+//     global tables (the window table leaves no room for them).
+// The window table costs every CTA a 176 KiB fill, which small objects do
+// not earn back. Measured on B200, per-object open GB/s, 4-bit -> window:
+// 32 MiB 402 -> 388, 48 MiB 432 -> 431, 64 MiB 449 -> 465, 128 MiB 478 ->
+// 522, 256 MiB 496 -> 556, 1 GiB 510 -> 588.
+template <bool WIN>
+struct OpenLayout {
+    static constexpr int kChains = WIN ? kOpenBatchChains : 2;
+    static constexpr int kAluChains = WIN ? kOpenBatchAluChains : 0;
+    static constexpr int kStepRows = WIN ? kOpenBatchStepRows : 2;
+    static constexpr int kFoldSmemLevels = WIN ? 4 : kFoldLevels;
+    static constexpr uint32_t kGh = 0;
+    static constexpr uint32_t kFold = kGh + (WIN ? static_cast<uint32_t>(kGh5RepBytes) : kGhBytes);
+    static constexpr uint32_t kHt = kFold + static_cast<uint32_t>(kFoldSmemLevels) * 8192u;  // H^kHornerThreads
+    static constexpr uint32_t kPart = kHt + 8192u;
+    static constexpr uint32_t kSmem = kPart + kPartBytes + 64;
+    static_assert(kSmem <= 227u * 1024u, "per-object open shared memory exceeds the per-block limit");
+};
+constexpr uint64_t kOpenWindowMinBytes = 48ull << 20;
+// Per-object seal of objects from kSealTwoPassMinBytes on: a CTR-only pass
+// (seal_ctr_kernel, 512 threads), then the window-table GHASH kernel of the
+// per-object open over the frame's ciphertext, which writes the tag. The
+// second pass re-reads the ciphertext and adds a launch, which pays from
+// about 80 MiB. Measured on B200, per-object seal GB/s, fused -> two passes:
+// 48 MiB 441 -> 417, 64 MiB 452 -> 448, 96 MiB 466 -> 481, 128 MiB 476 ->
+// 495, 256 MiB 487 -> 537, 512 MiB 493 -> 556, 1 GiB 496 -> 569.
+constexpr uint64_t kSealTwoPassMinBytes = 80ull << 20;
+constexpr uint32_t kOpenGh = 0;  // shared offset of the chain table (both layouts)
 
 constexpr uint32_t kCtrSmem = kAesBytes;
 static_assert(kSealSmem <= 227u * 1024u, "seal shared memory exceeds the per-block limit");
@@ -131,6 +159,8 @@ struct OpenArgs {
     KeyTables kt;
     Slot* slot;
     int* auth_ok;
+    ClmulConst cm;      // the chain multiplier for the integer-pipe chain (OpenLayout<true>)
+    uint8_t* tag_out;   // two-pass seal: the frame whose tag the GHASH kernel writes (open: null)
 };
 
 struct CtrArgs {

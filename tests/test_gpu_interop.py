@@ -107,3 +107,39 @@ def test_grid_boundaries(gkey, oracle, size):
     frame = gkey.seal(pt, iv, dst_off=size % 16)
     assert frame == expected
     assert gkey.open(expected, size) == (1, pt.tobytes())
+
+
+# Per-object open switches its GHASH kernel at 48 MiB (kOpenWindowMinBytes:
+# two 4-bit table chains below, the window-table / integer-pipe split from
+# there on); both sides of the switch, every ciphertext alignment class and
+# the gating on a corrupted frame.
+@pytest.mark.parametrize("size,frame_off", [((48 << 20) - 1, 0), (48 << 20, 0), ((48 << 20) + 3, 5),
+                                            ((64 << 20) + 13, 3), ((96 << 20) + 5, 8), ((64 << 20) + 16, 1)])
+def test_large_object_open_both_ghash_designs(gkey, oracle, size, frame_off):
+    rng = np.random.default_rng(size + frame_off)
+    pt = rng.integers(0, 256, size=size, dtype=np.uint8)
+    iv = rng.bytes(12)
+    expected = oracle.evp_seal(KEY, iv, pt).tobytes()
+    assert gkey.open(expected, size, frame_off=frame_off) == (1, pt.tobytes())
+    if frame_off == 0:
+        assert gkey.seal(pt, iv, dst_off=3) == expected
+    zeros = bytes(size)
+    for pos in (13 + size // 2, 13 + size - 1, 13 + size + 15):   # ciphertext middle, last byte, tag
+        bad = bytearray(expected)
+        bad[pos] ^= 0x10
+        assert gkey.open(bytes(bad), size, frame_off=frame_off) == (0, zeros)
+
+
+# Per-object seal switches to two passes (CTR kernel, then the window-table
+# GHASH kernel writing the tag) at 80 MiB (kSealTwoPassMinBytes): both sides,
+# every ciphertext store class (dst offset 0, 1, 3, 7, 11, 15 -> frame + 13
+# at 13, 14, 0, 4, 8, 12 mod 16) and a misaligned plaintext.
+@pytest.mark.parametrize("size,src_off,dst_off", [((80 << 20) - 3, 0, 0), (80 << 20, 0, 3), ((80 << 20) + 1, 5, 0),
+                                                  ((96 << 20) + 13, 0, 1), ((96 << 20) + 7, 0, 7),
+                                                  ((96 << 20) + 16, 9, 11), ((112 << 20) + 5, 0, 15)])
+def test_large_object_seal_both_designs(gkey, oracle, size, src_off, dst_off):
+    rng = np.random.default_rng(size * 7 + dst_off)
+    pt = rng.integers(0, 256, size=size, dtype=np.uint8)
+    iv = rng.bytes(12)
+    expected = oracle.evp_seal(KEY, iv, pt).tobytes()
+    assert gkey.seal(pt, iv, src_off=src_off, dst_off=dst_off) == expected
