@@ -52,6 +52,7 @@ constexpr int kPlanThreads = 1024;
 constexpr uint64_t kBatchMaxBlocks = 0xfffffffeull;
 constexpr uint32_t kCtrBatchMisc = kSmallSmem;      // after the small-object tables
 constexpr uint32_t kCtrBatchSmem = kCtrBatchMisc + 64;
+static_assert(kCtrBatchSmem + kSmemGapToday <= kSmemOptInLimit, "batched CTR shared memory exceeds the per-block limit");
 // Small objects are handed out largest first, by size bucket: n <= 128,
 // <= 256, <= 512, <= 1024 blocks (up to 2, 4, 8, 16 KiB), and bucket 4 for
 // the mid objects (1025 .. kWarpMaxBlocks blocks, up to 32 KiB) when they take
@@ -90,7 +91,7 @@ constexpr uint32_t kSealBatchSync = kSealBatchHandoff + kHandoffBytes;
 constexpr uint32_t kSealBatchWalk = kSealBatchSync + kHandoffSyncBytes;
 constexpr uint32_t kSealBatchSmem = kSealBatchWalk + kWalkBytes;
 static_assert(kSealBatchFold == kSmallFold, "the small-object path reads the seal fold slots");
-static_assert(kSealBatchSmem <= 227u * 1024u, "batched seal shared memory exceeds the per-block limit");
+static_assert(kSealBatchSmem + kSmemGapToday <= kSmemOptInLimit, "batched seal shared memory exceeds the per-block limit");
 // Shared memory of the batched GHASH passes (open, two-pass seal): the
 // replicated table of the chain multiplier (kGhW-bit windows when
 // kGhashTable5: 26 (W = 5) or 22 (W = 6) lookups of 16 B per multiply
@@ -108,7 +109,7 @@ constexpr uint32_t kOpenBatchHandoff = kGhPassHt + 8192u;
 constexpr uint32_t kOpenBatchSync = kOpenBatchHandoff + kHandoffBytes;
 constexpr uint32_t kOpenBatchWalk = kOpenBatchSync + kHandoffSyncBytes;
 constexpr uint32_t kOpenBatchSmem = kOpenBatchWalk + kWalkBytes;
-static_assert(kOpenBatchSmem <= 227u * 1024u, "batched GHASH shared memory exceeds the per-block limit");
+static_assert(kOpenBatchSmem + kSmemGapToday <= kSmemOptInLimit, "batched GHASH shared memory exceeds the per-block limit");
 
 // Alignment classes: 2 v + p, v = the frame's ciphertext class (seal: store
 // funnel word part 0..3, 4 = aligned; open: load funnel word part, same
@@ -1136,7 +1137,7 @@ __device__ __forceinline__ void seal_power_loop(const BatchArgs& a, const BatchC
 
 __global__ void __launch_bounds__(kSealThreads, 1) seal_batch_kernel(const BatchArgs a)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* const smem = layout_smem();
     const int tid = threadIdx.x;
     pdl_release();
     fill_aes_smem(smem + kSealAes, a.kt.aes_t);
@@ -1331,7 +1332,7 @@ __device__ __forceinline__ void ghash_power_loop(const uint8_t* smem, const Batc
 template <bool SEAL>
 __device__ __forceinline__ void ghash_batch_cta(const BatchArgs& a, int pass)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* const smem = layout_smem();
     const int tid = threadIdx.x;
     pdl_release();
     if constexpr (SEAL) {
@@ -1442,7 +1443,7 @@ __device__ __forceinline__ bool ctr_class(uint8_t* smem, const BatchArgs& a, con
 
 __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_batch_kernel(const BatchArgs a)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* const smem = layout_smem();
     const int tid = threadIdx.x;
     pdl_release();
     fill_aes_smem(smem, a.kt.aes_t);

@@ -28,8 +28,9 @@
 namespace confkv {
 namespace dev {
 
-// Writes the shared-window address of the dynamic shared memory (checked
-// against kDynSmemBase once per device by configure_device).
+// Writes the shared-window address at which dynamic shared memory starts for
+// a kernel without static shared memory (every kernel with a shared layout is
+// one); read once per device by configure_device / noalloc_setup.
 __global__ void smem_base_probe_kernel(unsigned int* out)
 {
     extern __shared__ __align__(16) uint8_t probe_smem[];
@@ -49,7 +50,7 @@ __global__ void smem_base_probe_kernel(unsigned int* out)
 template <int SQ, bool PT_ALIGNED>
 __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* const smem = layout_smem();
     uint4* part = reinterpret_cast<uint4*>(smem + kSealPart);
 
     const int tid = threadIdx.x;
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
 template <int SQ, bool PT_ALIGNED>
 __global__ void __launch_bounds__(kCtrThreads, 1) seal_ctr_kernel(const SealArgs a)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* const smem = layout_smem();
     const int tid = threadIdx.x;
     pdl_release();
     fill_aes_smem(smem + kSealAes, a.kt.aes_t);
@@ -166,7 +167,7 @@ template <int LQ, bool WIN, bool SEAL = false>
 __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenArgs a)
 {
     using L = OpenLayout<WIN>;
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* const smem = layout_smem();
     uint4* part = reinterpret_cast<uint4*>(smem + L::kPart);  // the row warps' fold values V_0..V_31
     const uint4* fold_tabs = reinterpret_cast<const uint4*>(smem + L::kFold);
 
@@ -252,7 +253,7 @@ __global__ void open_empty_kernel(const OpenArgs a)
 template <int LQ, bool PT_ALIGNED>
 __global__ void __launch_bounds__(kCtrThreads, 1) open_ctr_kernel(const CtrArgs a)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* const smem = layout_smem();
     constexpr int64_t T = kCtrThreads;
     const int tid = threadIdx.x;
     const int64_t row_begin = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta;
@@ -299,6 +300,30 @@ bool alloc_fault_injected()
 
 }  // namespace
 
+namespace {
+// Window address of dynamic shared memory as the probe read it (-1: not yet).
+std::atomic<int64_t> g_window_base{-1};
+}  // namespace
+
+uint32_t confkv::host::layout_pad()
+{
+    const int64_t b = g_window_base.load(std::memory_order_acquire);
+    return b < 0 ? 0u : dev::kSmemLayoutBase - static_cast<uint32_t>(b);
+}
+
+bool confkv::host::record_layout_base(unsigned int window_base)
+{
+    if (window_base > dev::kSmemLayoutBase || (window_base & 15u) != 0) {
+        return false;
+    }
+    int64_t expected = -1;
+    if (g_window_base.compare_exchange_strong(expected, static_cast<int64_t>(window_base),
+                                              std::memory_order_acq_rel)) {
+        return true;
+    }
+    return expected == static_cast<int64_t>(window_base);
+}
+
 // Opt every kernel instantiation into its dynamic shared memory once per device.
 cudaError_t confkv::host::configure_device(int device)
 {
@@ -314,6 +339,22 @@ cudaError_t confkv::host::configure_device(int device)
                 e = r;
             }
         };
+        // Where dynamic shared memory starts on this device decides the gap
+        // each launch requests before the kernels' layouts (layout_pad).
+        {
+            unsigned int* d = nullptr;
+            unsigned int base = 0;
+            chk(cudaMalloc(&d, sizeof(unsigned int)));
+            if (e == cudaSuccess) {
+                dev::smem_base_probe_kernel<<<1, 32, 1024>>>(d);
+                chk(cudaGetLastError());
+                chk(cudaMemcpy(&base, d, sizeof(base), cudaMemcpyDeviceToHost));
+                cudaFree(d);
+                if (e == cudaSuccess && !record_layout_base(base)) {
+                    e = cudaErrorNotSupported;
+                }
+            }
+        }
         chk(allow_smem(dev::seal_kernel<0, true>, dev::kSealSmem));
         chk(allow_smem(dev::seal_ctr_kernel<0, true>, dev::kCtrSmem));
         chk(allow_smem(dev::seal_kernel<1, true>, dev::kSealSmem));
@@ -360,22 +401,6 @@ cudaError_t confkv::host::configure_device(int device)
         chk(allow_smem(dev::open_ctr_kernel<3, false>, dev::kCtrSmem));
         chk(allow_smem(dev::open_ctr_kernel<4, false>, dev::kCtrSmem));
         chk(configure_batch_kernels());
-        // The hot loops address shared memory as (offset + kDynSmemBase) with
-        // the base folded into the load instruction; check it on this device.
-        if (e == cudaSuccess) {
-            unsigned int* d = nullptr;
-            unsigned int base = 0;
-            chk(cudaMalloc(&d, sizeof(unsigned int)));
-            if (e == cudaSuccess) {
-                dev::smem_base_probe_kernel<<<1, 32, 1024>>>(d);
-                chk(cudaGetLastError());
-                chk(cudaMemcpy(&base, d, sizeof(base), cudaMemcpyDeviceToHost));
-                cudaFree(d);
-                if (e == cudaSuccess && base != dev::kDynSmemBase) {
-                    e = cudaErrorNotSupported;
-                }
-            }
-        }
         results[device] = e;
     });
     return results[device];
@@ -903,9 +928,9 @@ struct NoAllocDevice {
 NoAllocDevice g_noalloc_dev[kMaxDevices];
 
 // Once per device, with that device current: resolve the array's device
-// address, opt the seal kernels into their shared memory, copy in the
-// key-independent AES T-tables and check the shared-memory layout with the
-// probe kernel writing into the array. Synchronous; allocates nothing.
+// address, read where dynamic shared memory starts (the probe kernel writes
+// into the array), opt the seal kernels into their shared memory and copy in
+// the key-independent AES T-tables. Synchronous; allocates nothing.
 int noalloc_setup(int device, NoAllocDevice& st)
 {
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&st.scratch), g_noalloc_scratch) != cudaSuccess ||
@@ -915,6 +940,18 @@ int noalloc_setup(int device, NoAllocDevice& st)
     if (cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
         st.num_sms <= 0) {
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    // The seal kernels' launches request the gap before their shared layout
+    // (layout_pad), so where dynamic shared memory starts is read first.
+    unsigned int* probe = reinterpret_cast<unsigned int*>(st.scratch + kNoAllocSlotOffset + 128);
+    dev::smem_base_probe_kernel<<<1, 32, 1024>>>(probe);
+    unsigned int base = 0;
+    if (cudaGetLastError() != cudaSuccess ||
+        cudaMemcpy(&base, probe, sizeof(base), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        return LMCACHE_GPU_AESGCM_ERR_CUDA;
+    }
+    if (!record_layout_base(base)) {
+        return LMCACHE_GPU_AESGCM_ERR_INTERNAL;
     }
     cudaError_t e = cudaSuccess;
     auto chk = [&e](cudaError_t r) {
@@ -940,14 +977,7 @@ int noalloc_setup(int device, NoAllocDevice& st)
     if (cudaMemcpy(st.scratch, aes_t, kNoAllocAesBytes, cudaMemcpyHostToDevice) != cudaSuccess) {
         return LMCACHE_GPU_AESGCM_ERR_CUDA;
     }
-    unsigned int* probe = reinterpret_cast<unsigned int*>(st.scratch + kNoAllocSlotOffset + 128);
-    dev::smem_base_probe_kernel<<<1, 32, 1024>>>(probe);
-    unsigned int base = 0;
-    if (cudaGetLastError() != cudaSuccess ||
-        cudaMemcpy(&base, probe, sizeof(base), cudaMemcpyDeviceToHost) != cudaSuccess) {
-        return LMCACHE_GPU_AESGCM_ERR_CUDA;
-    }
-    return base == dev::kDynSmemBase ? LMCACHE_GPU_AESGCM_OK : LMCACHE_GPU_AESGCM_ERR_INTERNAL;
+    return LMCACHE_GPU_AESGCM_OK;
 }
 
 // Plain (not programmatic) launch: the kernel starts only after everything
@@ -956,7 +986,7 @@ int noalloc_setup(int device, NoAllocDevice& st)
 template <int SQ, bool A>
 cudaError_t launch_seal_plain(const dev::SealArgs& args, cudaStream_t s)
 {
-    dev::seal_kernel<SQ, A><<<args.grid, dev::kSealThreads, dev::kSealSmem, s>>>(args);
+    dev::seal_kernel<SQ, A><<<args.grid, dev::kSealThreads, launch_smem(dev::kSealSmem), s>>>(args);
     return cudaGetLastError();
 }
 

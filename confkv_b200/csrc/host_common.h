@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 #include <unordered_map>
@@ -72,14 +73,37 @@ inline int cuda_rc(cudaError_t e)
     return e == cudaSuccess ? LMCACHE_GPU_AESGCM_OK : LMCACHE_GPU_AESGCM_ERR_CUDA;
 }
 
+// Bytes between the start of a block's dynamic shared memory and
+// dev::kSmemLayoutBase, where every kernel's shared layout begins
+// (dev::layout_smem). Set from the probe kernel's reading on the first
+// configured device: 1 KiB on sm_100a with this driver, where dynamic shared
+// memory starts at window address 0x400.
+uint32_t layout_pad();
+
+// Records the window address of dynamic shared memory read by
+// smem_base_probe_kernel on a device. False (the device is refused) when it
+// lies above dev::kSmemLayoutBase, is not 16-byte aligned, or differs from
+// the address another device reported.
+bool record_layout_base(unsigned int window_base);
+
+// Shared bytes to request for a kernel whose layout takes `layout_bytes`
+// (0 for kernels without a shared layout).
+inline uint32_t launch_smem(uint32_t layout_bytes)
+{
+    return layout_bytes == 0 ? 0u : layout_bytes + layout_pad();
+}
+
+// Opts `kernel` into the dynamic shared memory of a layout of `bytes` plus the gap.
 template <class K>
 cudaError_t allow_smem(K kernel, uint32_t bytes)
 {
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(launch_smem(bytes)));
 }
 
 // Launch with programmatic stream serialization (see pdl_release/pdl_wait):
 // the kernel may start while the previous kernel on the stream drains.
+// `smem` is the kernel's layout size; the gap before the layout is added here.
 template <class... KArgs, class... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, uint32_t smem, cudaStream_t s,
                        Args&&... args)
@@ -87,7 +111,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = launch_smem(smem);
     cfg.stream = s;
     cudaLaunchAttribute attr{};
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -46,7 +46,20 @@ constexpr int kPowerWarp = kHornerThreads / 32;     // warp index of the power w
 constexpr int kSealThreads = kHornerThreads + 32;
 constexpr int kCtrThreads = 512;
 
-// Shared-memory regions (byte offsets from the dynamic shared base).
+// Shared-window address at which every kernel's shared-memory layout begins.
+// Dynamic shared memory starts after the block's reserved bytes (1 KiB on
+// sm_100a with this driver); a kernel skips from there to kSmemLayoutBase
+// (layout_smem), and the host adds that gap to every launch (layout_pad in
+// host_common.h). Hot-loop table loads put kSmemLayoutBase in the LDS
+// immediate field, so the PRMT-formed offset needs no add, whatever the
+// reserve is, up to kSmemLayoutBase. Adding a base register to each lookup
+// instead would put 133 more ALU instructions on every AES-CTR block.
+constexpr uint32_t kSmemLayoutBase = 0x800;
+constexpr uint32_t kSmemOptInLimit = 227u * 1024u;
+// Room for the gap of today's 1 KiB reserve in every kernel's budget.
+constexpr uint32_t kSmemGapToday = kSmemLayoutBase - 0x400u;
+
+// Shared-memory regions (byte offsets from the start of the layout).
 // AES T-tables: two 64 KiB regions; row x (256 B) of region 0 holds T0[x] for
 // lanes 0..31 then T1[x] for lanes 0..31; region 1 holds T2 and T3. A lookup
 // address is formed by one PRMT: byte 0 = table half + lane, byte 1 = index.
@@ -93,7 +106,7 @@ struct OpenLayout {
     static constexpr uint32_t kHt = kFold + static_cast<uint32_t>(kFoldSmemLevels) * 8192u;  // H^kHornerThreads
     static constexpr uint32_t kPart = kHt + 8192u;
     static constexpr uint32_t kSmem = kPart + kPartBytes + 64;
-    static_assert(kSmem <= 227u * 1024u, "per-object open shared memory exceeds the per-block limit");
+    static_assert(kSmem + kSmemGapToday <= kSmemOptInLimit, "per-object open shared memory exceeds the per-block limit");
 };
 constexpr uint64_t kOpenWindowMinBytes = 48ull << 20;
 // Per-object seal of objects from kSealTwoPassMinBytes on: a CTR-only pass
@@ -107,14 +120,7 @@ constexpr uint64_t kSealTwoPassMinBytes = 80ull << 20;
 constexpr uint32_t kOpenGh = 0;  // shared offset of the chain table (both layouts)
 
 constexpr uint32_t kCtrSmem = kAesBytes;
-static_assert(kSealSmem <= 227u * 1024u, "seal shared memory exceeds the per-block limit");
-
-// Shared-window address at which dynamic shared memory starts for a kernel
-// without static shared memory on sm_100a (the first 1 KiB of each block's
-// window is reserved). Hot-loop table loads put this base in the LDS immediate
-// field so the PRMT-formed offset needs no add. configure_device() launches
-// smem_base_probe_kernel once per device and refuses to run if it differs.
-constexpr uint32_t kDynSmemBase = 0x400;
+static_assert(kSealSmem + kSmemGapToday <= kSmemOptInLimit, "seal shared memory exceeds the per-block limit");
 
 // Per-call accumulation slot (32 bytes). The last CTA of a call resets
 // acc_hi, acc_lo and ticket. Batched calls keep one slot per object and its
@@ -212,6 +218,15 @@ constexpr uint32_t kWaitLimitPolls = 1u << 30;
 __device__ __forceinline__ uint32_t smem_u32(const void* p)
 {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// The start of the kernel's shared layout: window address kSmemLayoutBase,
+// inside the block's dynamic shared memory because the host sized the launch
+// to include the gap (layout_pad). A constant shared address, so every
+// region's address folds into its instructions' immediates.
+__device__ __forceinline__ uint8_t* layout_smem()
+{
+    return static_cast<uint8_t*>(__cvta_shared_to_generic(kSmemLayoutBase));
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
@@ -359,7 +374,7 @@ template <uint32_t BASE>
 __device__ __forceinline__ uint32_t lds32(uint32_t off)
 {
     uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(off), "n"(kDynSmemBase + BASE));
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(off), "n"(kSmemLayoutBase + BASE));
     return v;
 }
 
@@ -369,7 +384,7 @@ __device__ __forceinline__ uint4 lds128(uint32_t off)
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+%5];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(off), "n"(kDynSmemBase + BASE));
+                 : "r"(off), "n"(kSmemLayoutBase + BASE));
     return v;
 }
 
@@ -728,7 +743,7 @@ __device__ __forceinline__ void gh5_acc(const uint32_t (&w)[4], uint32_t lb, uin
     constexpr int r0 = kGhW * G;
     constexpr int wi = r0 >> 5;
     constexpr int sh = r0 & 31;
-    constexpr uint32_t imm = kDynSmemBase + GH + static_cast<uint32_t>(G) * kGh5GroupStride;
+    constexpr uint32_t imm = kSmemLayoutBase + GH + static_cast<uint32_t>(G) * kGh5GroupStride;
     constexpr uint32_t mask = kGh5Mask7;
     uint4 e;
     if constexpr (sh < 7) {
