@@ -569,6 +569,22 @@ def openssl_threads_run(lib, key: bytes, per: int, threads: int, P: int) -> tupl
     return ts.value, to.value
 
 
+SINGLE_CORE_OBJECTS = 4  # objects of the single-core sample (128 MiB each way at 32 MiB)
+
+
+def single_core(lib, objs, key: bytes) -> dict:
+    """The reference backend on one native thread over the first objects of
+    the step, sealed then opened (after one untimed pass): the figure the
+    reference's own single-core CPU table is comparable with."""
+    host = HostObjects(objs[:SINGLE_CORE_OBJECTS])
+    host.run(lib, key, 1)
+    ts, to = host.run(lib, key, 1)
+    nbytes = host.count * host.P
+    return {"seal_gbs": round(nbytes / ts / 1e9, 2), "open_gbs": round(nbytes / to / 1e9, 2),
+            "value": round(2 * nbytes / (ts + to) / 1e9, 2), "cores": 1,
+            "sample": f"{host.count} objects of {host.P} B sealed then opened on one native thread"}
+
+
 def cpu_baseline(args, plain_u8, key: bytes) -> dict:
     """The reference OpenSSL backend on all host threads, sealing then
     opening this rank's objects (copied to host memory), once: a bounded
@@ -585,7 +601,8 @@ def cpu_baseline(args, plain_u8, key: bytes) -> dict:
     return {"value": round(gbs, 2), "unit": UNIT, "cores": threads, "kind": "reference",
             "sample": f"the step's {host.count} objects of {host.P} B (bf16 KV, same bytes as the GPU run) sealed "
                       f"then opened once on {threads} native threads, reference lmcache_aes128gcm_seal/open "
-                      f"(OpenSSL EVP)"}
+                      f"(OpenSSL EVP)",
+            "single_core": single_core(lib, host.objs, key)}
 
 
 def cpu_sweep_sizes(lib, key: bytes, threads: int) -> None:
@@ -647,7 +664,8 @@ def run_reference(args, rank, world):
         "api": "reference lmcache_aes128gcm_seal / lmcache_aes128gcm_open, one call per object, native threads",
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": "reference",
                          "sample": f"all {host.count} objects of the step ({world} GPU(s) x {args.objects}) "
-                                   f"sealed then opened, object k on thread k mod {threads}"},
+                                   f"sealed then opened, object k on thread k mod {threads}",
+                         "single_core": single_core(lib, host.objs, key)},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
