@@ -29,10 +29,10 @@ struct SealTile {
 
 // Row warps of a seal tile: AES-CTR of the tile's blocks, ciphertext stores,
 // and the thread's GHASH share Q_t = sum_r C_(r,t) H^(T (J-1-r)) (returned).
-// Rows [r_a, r_a + 2 ngroups) hold only full blocks inside the object and
-// start at an even row: they run the check-free two-row loop. The others
-// (tile 0's leading padding, the row with the last partial block, leftovers)
-// take generic_row. Rows are visited in order.
+// Rows [r_a, r_a + 2 ngroups) hold only full blocks inside the object: they
+// run the check-free two-row loop. The others (tile 0's leading padding, the
+// row with the last partial block, leftovers) take generic_row. Rows are
+// visited in order.
 //
 // SQ selects the ciphertext store: 4 = ciphertext pointer 16-B aligned;
 // 0..3 = word part of the funnel that builds an aligned 16-B chunk from this
@@ -62,11 +62,11 @@ __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk
         ch.q[k] = make_uint4(0, 0, 0, 0);
     }
 
-    // The interior loop takes kPair = 2 rows per iteration; it starts on an
-    // even row so row r lands in chain r mod R (R divides kPair). A
-    // misaligned plaintext is read as the two aligned 16-byte chunks around
-    // each block, so its interior blocks are 1 .. n_full - 2 (both chunks
-    // inside the object).
+    // The interior loop takes kPair = 2 rows per iteration; with R > 1 chains
+    // it starts on an even row so row r lands in chain r mod R (R divides
+    // kPair). A misaligned plaintext is read as the two aligned 16-byte
+    // chunks around each block, so its interior blocks are 1 .. n_full - 2
+    // (both chunks inside the object).
     constexpr int64_t kPair = 2;
     static_assert(kPair % R == 0, "chains must divide the rows per iteration");
     constexpr int64_t kLoBlock = PT_ALIGNED ? 0 : 1;
@@ -77,7 +77,9 @@ __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk
     const uint32_t src_off = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(t.src) & 15u);
     const uint32_t src_q = src_off >> 2;
     const uint32_t src_fsel = funnel_sel(src_off & 3u);
-    int64_t r_a = (r_lo + kPair - 1) / kPair * kPair;
+    // With one chain (or none, GH = false) every row is in chain 0, so the
+    // loop starts at r_lo whatever its parity.
+    int64_t r_a = (R == 1 || !GH) ? r_lo : (r_lo + kPair - 1) / kPair * kPair;
     r_a = r_a > r_hi ? r_hi : r_a;
     const int64_t ngroups = r_hi > r_a ? (r_hi - r_a) / kPair : 0;
 

@@ -69,7 +69,8 @@ def seal_tile_rows(base, rows, P, pt_aligned=True):
     lo_block = 0 if pt_aligned else 1
     r_lo = 0 if base >= lo_block else _trunc_div(lo_block - base + T - 1, T)
     r_hi = min(_trunc_div(n_full - (0 if pt_aligned else 1) - base, T), rows)
-    r_a = min(_trunc_div(r_lo + SEAL_PAIR - 1, SEAL_PAIR) * SEAL_PAIR, r_hi)
+    # one GHASH chain (kSealChains = 1): the two-row loop starts at r_lo
+    r_a = min(r_lo, r_hi)
     ngroups = _trunc_div(r_hi - r_a, SEAL_PAIR) if r_hi > r_a else 0
     return _split(pad_rows(base), r_a, SEAL_PAIR * ngroups, rows)
 
