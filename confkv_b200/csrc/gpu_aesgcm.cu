@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kSealThreads, 1) seal_kernel(const SealArgs a)
     if (warp == kPowerWarp) {
         const unsigned long long d = static_cast<unsigned long long>(a.grid - 1 - blockIdx.x) *
                                          static_cast<unsigned long long>(span) + 2ull;
-        seal_power(a.ivw, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
+        seal_power<true>(a.ivw, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
     } else {
         const SealTile t{a.src, ct, P,
                          static_cast<int64_t>(a.nblocks) - static_cast<int64_t>(a.grid - blockIdx.x) * span,
@@ -183,6 +183,9 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     }
     fill_smem<L::kFoldSmemLevels * 512>(reinterpret_cast<uint4*>(smem + L::kFold), a.kt.gh_pow2);  // H^(2^l)
     fill_smem<512>(reinterpret_cast<uint4*>(smem + L::kHt), a.kt.gh_pow2 + kFoldLevels * 512);      // H^512
+    if constexpr (!WIN) {
+        fill_smem<256>(reinterpret_cast<uint4*>(smem + L::kAesC), reinterpret_cast<const uint4*>(a.kt.aes_t));
+    }
     pdl_wait();
     __syncthreads();
 
@@ -196,7 +199,8 @@ __global__ void __launch_bounds__(kSealThreads, 1) open_ghash_kernel(const OpenA
     if (warp == kPowerWarp) {
         const unsigned long long d = static_cast<unsigned long long>(a.grid - 1 - blockIdx.x) *
                                          static_cast<unsigned long long>(span) + 2ull;
-        open_power(a.frame, a.kt.aes_t, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
+        const uint32_t* aes_c = WIN ? a.kt.aes_t : reinterpret_cast<const uint32_t*>(smem + L::kAesC);
+        open_power<true, !WIN>(a.frame, aes_c, a.rk, P, d, a.kt.gh_pow2, lane, ej0, lh, uhi, ulo);
     } else {
         const OpenTile t{a.frame, a.frame_len, P,
                          static_cast<int64_t>(a.nblocks) - static_cast<int64_t>(a.grid - blockIdx.x) * span,

@@ -105,7 +105,9 @@ struct OpenLayout {
     static constexpr uint32_t kFold = kGh + (WIN ? static_cast<uint32_t>(kGh5RepBytes) : kGhBytes);
     static constexpr uint32_t kHt = kFold + static_cast<uint32_t>(kFoldSmemLevels) * 8192u;  // H^kHornerThreads
     static constexpr uint32_t kPart = kHt + 8192u;
-    static constexpr uint32_t kSmem = kPart + kPartBytes + 64;
+    // the compact AES T-tables for the power warp's E_K(J0) (4-bit layout only)
+    static constexpr uint32_t kAesC = kPart + kPartBytes + 64;
+    static constexpr uint32_t kSmem = kAesC + (WIN ? 0u : 4096u);
     static_assert(kSmem + kSmemGapToday <= kSmemOptInLimit, "per-object open shared memory exceeds the per-block limit");
 };
 constexpr uint64_t kOpenWindowMinBytes = 48ull << 20;
@@ -573,15 +575,18 @@ __device__ __forceinline__ void warp_ctr_keystream(uint32_t x[4], uint32_t ctr, 
 }
 
 // Same cipher reading the compact T-tables from global memory (one-off blocks).
-__device__ inline uint4 aes_encrypt_gmem(const uint32_t* T, const uint32_t* rk, uint4 in)
+// GMEM: T is global memory, read through the read-only path; otherwise T
+// is a copy of the compact tables in shared memory.
+template <bool GMEM>
+__device__ inline uint4 aes_encrypt_compact(const uint32_t* T, const uint32_t* rk, uint4 in)
 {
+    auto ld = [T](uint32_t i) __attribute__((always_inline)) { return GMEM ? __ldg(T + i) : T[i]; };
     uint32_t w[4] = {in.x ^ rk[0], in.y ^ rk[1], in.z ^ rk[2], in.w ^ rk[3]};
     for (int r = 1; r < 10; ++r) {
         uint32_t n[4];
         for (int c = 0; c < 4; ++c) {
-            n[c] = __ldg(T + (w[c] & 0xffu)) ^ __ldg(T + 256 + ((w[(c + 1) & 3] >> 8) & 0xffu)) ^
-                   __ldg(T + 512 + ((w[(c + 2) & 3] >> 16) & 0xffu)) ^
-                   __ldg(T + 768 + (w[(c + 3) & 3] >> 24)) ^ rk[4 * r + c];
+            n[c] = ld(w[c] & 0xffu) ^ ld(256 + ((w[(c + 1) & 3] >> 8) & 0xffu)) ^
+                   ld(512 + ((w[(c + 2) & 3] >> 16) & 0xffu)) ^ ld(768 + (w[(c + 3) & 3] >> 24)) ^ rk[4 * r + c];
         }
         for (int c = 0; c < 4; ++c) {
             w[c] = n[c];
@@ -589,14 +594,19 @@ __device__ inline uint4 aes_encrypt_gmem(const uint32_t* T, const uint32_t* rk, 
     }
     uint32_t n[4];
     for (int c = 0; c < 4; ++c) {
-        const uint32_t e0 = __ldg(T + 512 + (w[c] & 0xffu));
-        const uint32_t e1 = __ldg(T + 768 + ((w[(c + 1) & 3] >> 8) & 0xffu));
-        const uint32_t e2 = __ldg(T + ((w[(c + 2) & 3] >> 16) & 0xffu));
-        const uint32_t e3 = __ldg(T + 256 + (w[(c + 3) & 3] >> 24));
+        const uint32_t e0 = ld(512 + (w[c] & 0xffu));
+        const uint32_t e1 = ld(768 + ((w[(c + 1) & 3] >> 8) & 0xffu));
+        const uint32_t e2 = ld((w[(c + 2) & 3] >> 16) & 0xffu);
+        const uint32_t e3 = ld(256 + (w[(c + 3) & 3] >> 24));
         n[c] = __byte_perm(__byte_perm(e0, e1, 0x0050u), __byte_perm(e2, e3, 0x7200u), 0x7610u) ^
                rk[40 + c];
     }
     return make_uint4(n[0], n[1], n[2], n[3]);
+}
+
+__device__ inline uint4 aes_encrypt_gmem(const uint32_t* T, const uint32_t* rk, uint4 in)
+{
+    return aes_encrypt_compact<true>(T, rk, in);
 }
 
 // Fill the 128 KiB replicated T-table region from the compact global tables.
@@ -1019,6 +1029,41 @@ __device__ inline void warp_generic_mul(uint4 f_raw, unsigned long long uhi, uns
     }
     rhi = ahi;
     rlo = alo;
+}
+
+// H^d (raw bytes) on the integer pipes, for d < 2^32 (larger d: warp_h_pow).
+// Lane k loads M_k = H^(2^k) when bit k of d is set (entry 24 of the compact
+// table of M is M itself: the identity block has only the high nibble of byte
+// 0 set, to 8), so all factors arrive in one memory round trip; the product
+// then takes one warp_generic_mul by the lane basis of each further factor.
+// warp_h_pow instead waits for one global-table lookup per set bit, which in
+// a per-object call of a few rows per tile outlasts the rows.
+__device__ inline uint4 warp_h_pow_alu(const uint4* pow2, unsigned long long d, int lane)
+{
+    if ((d >> 32) != 0ull) {
+        return warp_h_pow(pow2, d, lane);
+    }
+    uint4 mine = make_uint4(0, 0, 0, 0);
+    if ((d >> lane) & 1ull) {
+        mine = __ldg(pow2 + static_cast<size_t>(lane) * 512 + 24);
+    }
+    uint4 m = make_uint4(0x80u, 0, 0, 0);  // identity
+    bool first = true;
+    while (d) {
+        const int k = __ffsll(static_cast<long long>(d)) - 1;
+        d &= d - 1ull;
+        const uint4 f = shfl4(mine, k);
+        if (first) {
+            m = f;
+            first = false;
+            continue;
+        }
+        unsigned long long uhi, ulo, rhi, rlo;
+        warp_lane_basis(f, lane, uhi, ulo);
+        warp_generic_mul(m, uhi, ulo, lane, rhi, rlo);
+        m = be_to_raw(rhi, rlo);
+    }
+    return m;
 }
 
 // Power-warp epilogue of seal/open GHASH: scale the CTA's fold by H^(d_c)

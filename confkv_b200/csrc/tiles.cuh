@@ -168,6 +168,9 @@ __device__ __forceinline__ uint4 seal_rows(const SealTile& t, const uint32_t* rk
 
 // Power warp of a seal tile: E_K(J0) from the shared T-tables, L*H for the
 // length block, and lane p's U_p = H^d x^(4p) with d = (G-1-c) J T + 2.
+// ALU_POW: H^d on the integer pipes (warp_h_pow_alu), for the per-object
+// kernels, whose tiles can be a single row.
+template <bool ALU_POW = false>
 __device__ __forceinline__ void seal_power(const uint32_t ivw[3], const uint32_t* rk, uint64_t P,
                                            unsigned long long d, const uint4* pow2, int lane, uint4& ej0,
                                            uint4& lh, unsigned long long& uhi, unsigned long long& ulo)
@@ -178,7 +181,7 @@ __device__ __forceinline__ void seal_power(const uint32_t ivw[3], const uint32_t
     aes_rounds_smem<kSealAes>(w, rk, lb);
     ej0 = make_uint4(w[0], w[1], w[2], w[3]);
     lh = warp_gh_mul_global(be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull), pow2, lane);
-    warp_lane_basis(warp_h_pow(pow2, d, lane), lane, uhi, ulo);
+    warp_lane_basis(ALU_POW ? warp_h_pow_alu(pow2, d, lane) : warp_h_pow(pow2, d, lane), lane, uhi, ulo);
 }
 
 // Shared-memory bytes of the fold tables that seal_fold stores over the
@@ -411,15 +414,17 @@ __device__ __forceinline__ uint4 open_ghash_rows(const OpenTile& t, const uint4*
 }
 
 // Power warp of an open-GHASH tile: E_K(J0) (IV read from the frame, cipher
-// from the compact global T-tables), L*H and U_p = H^d x^(4p).
+// from the compact T-tables aes_t: global memory, or a shared copy when
+// AES_SMEM), L*H and U_p = H^d x^(4p) (on the integer pipes when ALU_POW).
+template <bool ALU_POW = false, bool AES_SMEM = false>
 __device__ __forceinline__ void open_power(const uint8_t* frame, const uint32_t* aes_t, const uint32_t* rk,
                                            uint64_t P, unsigned long long d, const uint4* pow2, int lane,
                                            uint4& ej0, uint4& lh, unsigned long long& uhi, unsigned long long& ulo)
 {
     const uint4 iv = load_bytes(frame + 1, 12);
-    ej0 = aes_encrypt_gmem(aes_t, rk, make_uint4(iv.x, iv.y, iv.z, bswap32(1u)));
+    ej0 = aes_encrypt_compact<!AES_SMEM>(aes_t, rk, make_uint4(iv.x, iv.y, iv.z, bswap32(1u)));
     lh = warp_gh_mul_global(be_to_raw(0ull, static_cast<unsigned long long>(P) * 8ull), pow2, lane);
-    warp_lane_basis(warp_h_pow(pow2, d, lane), lane, uhi, ulo);
+    warp_lane_basis(ALU_POW ? warp_h_pow_alu(pow2, d, lane) : warp_h_pow(pow2, d, lane), lane, uhi, ulo);
 }
 
 // Tag check of open: 1 when the version byte is 1 and the frame's tag equals
