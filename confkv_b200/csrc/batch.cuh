@@ -184,20 +184,25 @@ __host__ __device__ __forceinline__ uint32_t chunk_of(unsigned long long x, unsi
 }
 
 // Chunks for R rows of K tile objects on `sms` SMs. With at least
-// kChunksPerSm tile objects per SM the per-object cost estimate is least
-// exact (mixed sizes and alignments) and more chunks let the queue even out
-// the SMs: kChunksPerSm per SM; otherwise kChunksPerSmFew, since every chunk
-// boundary inside an object adds a segment (fold, hand-off, pipeline
-// restart): on B200 one chunk per SM ran batches of a few large objects
-// 0.4-0.9 % faster than two, and two 0.8 % faster than four. Fewer while a chunk would be shorter than kMinChunkRows, at
-// least one per SM, never more than R (so no chunk is empty).
-__host__ __device__ __forceinline__ uint32_t batch_chunk_count(unsigned long long R, uint32_t K, uint32_t sms)
+// kChunksPerSm tile objects per SM of mixed sizes the per-object cost
+// estimate is least exact and more chunks let the queue even out the SMs:
+// kChunksPerSm per SM; otherwise kChunksPerSmFew, since every chunk boundary
+// inside an object adds a segment (fold, hand-off, pipeline restart): on
+// B200 one chunk per SM ran batches of a few large objects 0.4-0.9 % faster
+// than two, and two 0.8 % faster than four. A batch is `uniform` when its
+// largest tile object has at most kUniformRowsRatio times the rows of its
+// smallest: equal chunks then already balance the SMs. Fewer while a chunk
+// would be shorter than kMinChunkRows, at least one per SM, never more than R
+// (so no chunk is empty).
+constexpr uint32_t kUniformRowsRatio = 2;
+__host__ __device__ __forceinline__ uint32_t batch_chunk_count(unsigned long long R, uint32_t K, uint32_t sms,
+                                                              bool uniform)
 {
     if (R == 0) {
         return 0;
     }
     const unsigned long long cap =
-        K >= static_cast<unsigned long long>(kChunksPerSm) * sms ? kChunksPerSm : kChunksPerSmFew;
+        K >= static_cast<unsigned long long>(kChunksPerSm) * sms && !uniform ? kChunksPerSm : kChunksPerSmFew;
     unsigned long long per = R / (static_cast<unsigned long long>(sms) * kMinChunkRows);
     per = per < 1 ? 1 : (per > cap ? cap : per);
     const unsigned long long m = per * sms;
@@ -357,6 +362,8 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     __shared__ unsigned int mid_objs[kClasses];
     __shared__ uint32_t route_mid;
     __shared__ unsigned int mid_max_n;
+    __shared__ unsigned int tile_min_rows;  // over the tile and mid objects
+    __shared__ unsigned int tile_max_rows;
     __shared__ unsigned long long total_rows_s;
     __shared__ uint32_t tile_objs_s;
     __shared__ uint32_t chunks_s;
@@ -384,6 +391,8 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
     }
     if (tid == 0) {
         mid_max_n = 0;
+        tile_min_rows = 0xffffffffu;
+        tile_max_rows = 0;
     }
     chunk_mark[tid] = 0;
     __syncthreads();
@@ -479,6 +488,12 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
         if (lane == 0 && warp_max_n != 0) {
             atomicMax(&mid_max_n, warp_max_n);
         }
+        const unsigned warp_min_rows = __reduce_min_sync(0xffffffffu, rows != 0 ? rows : 0xffffffffu);
+        const unsigned warp_max_rows = __reduce_max_sync(0xffffffffu, rows);
+        if (lane == 0 && warp_max_rows != 0) {
+            atomicMin(&tile_min_rows, warp_min_rows);
+            atomicMax(&tile_max_rows, warp_max_rows);
+        }
         const unsigned mpeers = __match_any_sync(0xffffffffu, mkey);
         const unsigned msum = __reduce_add_sync(mpeers, mkey >= 0 ? rows : 0u);
         if (mkey >= 0 && lane == __ffs(mpeers) - 1) {
@@ -524,7 +539,10 @@ __global__ void __launch_bounds__(kPlanThreads) batch_plan_kernel(BatchItem* ite
             K += class_objs[c] + (route ? 0u : mid_objs[c]);
             R += class_rows[c] + (route ? 0ull : mid_rows[c]);
         }
-        const uint32_t M = batch_chunk_count(R, K, sms);
+        const bool uniform =
+            K != 0 && static_cast<unsigned long long>(tile_max_rows) <=
+                          static_cast<unsigned long long>(kUniformRowsRatio) * tile_min_rows;
+        const uint32_t M = batch_chunk_count(R, K, sms, uniform);
         total_rows_s = R;
         tile_objs_s = K;
         chunks_s = M;

@@ -30,6 +30,7 @@ WARP_MAX_BLOCKS = 2048   # kWarpMaxBlocks
 MID_ALPHA_SEAL = 26      # kMidAlphaSeal
 MID_ALPHA_OPEN = 19      # kMidAlphaOpen
 SEGMENT_COST_ROWS = 5    # kSegmentCostRows
+UNIFORM_ROWS_RATIO = 2   # kUniformRowsRatio
 
 
 def cdiv(a, b):
@@ -112,11 +113,13 @@ def tile_base(n, J, G, c):
     return n - (G - c) * J * T
 
 
-def chunk_count(R, K, sms):
-    """batch_chunk_count: chunks for R rows of K tile objects on `sms` SMs."""
+def chunk_count(R, K, sms, uniform=False):
+    """batch_chunk_count: chunks for R rows of K tile objects on `sms` SMs
+    (`uniform`: the largest tile or mid object has at most UNIFORM_ROWS_RATIO
+    times the rows of the smallest)."""
     if R == 0:
         return 0
-    cap = CHUNKS_PER_SM if K >= CHUNKS_PER_SM * sms else CHUNKS_PER_SM_FEW
+    cap = CHUNKS_PER_SM if K >= CHUNKS_PER_SM * sms and not uniform else CHUNKS_PER_SM_FEW
     per = max(1, min(cap, R // (sms * MIN_CHUNK_ROWS)))
     return min(per * sms, R)
 
@@ -174,7 +177,10 @@ def chunk_plan(lens, sms, valid=None, classes=None, open_=False):
             objs.append((row, i, rows))
             row += rows
     R, K = row, len(objs)
-    M = chunk_count(R, K, sms)
+    sized = [tile_rows(P, ok) for P, ok in zip(lens, valid)]   # tile and mid objects, before routing
+    sized = [r for r in sized if r]
+    uniform = K != 0 and max(sized) <= UNIFORM_ROWS_RATIO * min(sized)
+    M = chunk_count(R, K, sms, uniform)
     o = SEGMENT_COST_ROWS if M and (R + SEGMENT_COST_ROWS * K) // M >= 2 * (SEGMENT_COST_ROWS + 1) else 0
     C = R + o * K
     chunk_first = [None] * M

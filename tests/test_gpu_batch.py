@@ -450,3 +450,57 @@ def test_batch_handoff_wait_runs_out_without_hanging(gpu_lib, monkeypatch):
         s.synchronize()
         assert int(batch.fault()) == 0
         assert torch.equal(d_batch, d_single)
+
+
+@pytest.mark.parametrize("mixed", [False, True])
+def test_batch_chunk_count_matches_replay(gpu_lib, oracle, mixed):
+    """A batch of many tile objects per SM takes one chunk per SM when its
+    objects are about the same size (the largest at most twice the rows of
+    the smallest) and four per SM when they are mixed; the device plan's chunk
+    count (BatchHeader.chunks, byte 8 of the workspace) must equal the CPU
+    replay's (tests/schedules.py). Both give OpenSSL's frames and open back."""
+    from schedules import chunk_plan
+
+    sms = min(torch.cuda.get_device_properties(0).multi_processor_count, 256)
+    count = 5 * sms
+    rng = np.random.default_rng(97 + mixed)
+    key = rng.bytes(16)
+    if mixed:
+        lens = np.array([(1 << 20) + int(rng.integers(0, 16)) if i % 2 else 65536 + int(rng.integers(1, 16))
+                         for i in range(count)], dtype=np.int64)
+    else:
+        # 64-65 rows each: enough rows for four chunks per SM, one for a uniform batch
+        lens = np.array([524288 + (i % 7) for i in range(count)], dtype=np.int64)
+    plan = chunk_plan(lens.tolist(), sms)
+    assert plan["M"] == (4 * sms if mixed else sms)
+    ivs = [rng.bytes(12) for _ in lens]
+    pts = [rng.integers(0, 256, size=int(n), dtype=np.uint8) for n in lens]
+    pt_off, pt_total = _packed(lens, align=256)
+    fr_off, fr_total = _packed(lens + 29, align=256)
+    d_plain = torch.zeros(pt_total + 16, dtype=torch.uint8, device="cuda")
+    d_plain[:pt_total].copy_(torch.from_numpy(np.concatenate(
+        [np.concatenate([p, np.zeros(int(pt_off[i + 1] - pt_off[i]) - len(p) if i + 1 < len(pts) else 0, np.uint8)])
+         for i, p in enumerate(pts)])))
+    d_frames = torch.zeros(fr_total + 16, dtype=torch.uint8, device="cuda")
+    d_out = torch.zeros(pt_total + 16, dtype=torch.uint8, device="cuda")
+    d_auth = torch.full((len(lens),), 7, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    batch = DeviceBatch(gpu_lib, len(lens))
+    with GpuAes128GcmKey(gpu_lib, key) as k:
+        batch.seal(k, _seal_entries(d_plain, pt_off, d_frames, fr_off, lens, ivs), s)
+        s.synchronize()
+        assert int(batch.fault()) == 0 and not batch.statuses().any()
+        chunks = int(batch.workspace[8:12].cpu().numpy().view(np.uint32)[0])
+        assert chunks == plan["M"]
+        frames = d_frames.cpu().numpy()
+        expected = oracle.evp_seal_many(key, ivs, pts)
+        for i in range(len(lens)):
+            assert np.array_equal(frames[fr_off[i]:fr_off[i] + lens[i] + 29], expected[i]), (i, lens[i])
+        batch.open(k, _open_entries(d_frames, fr_off, d_out, pt_off, lens, d_auth, range(len(lens))), s)
+        s.synchronize()
+        assert int(batch.fault()) == 0
+        assert int(batch.workspace[8:12].cpu().numpy().view(np.uint32)[0]) == plan["M"]
+        assert bool((d_auth == 1).all())
+        out = d_out.cpu().numpy()
+        for i in range(len(lens)):
+            assert np.array_equal(out[pt_off[i]:pt_off[i] + lens[i]], pts[i]), (i, lens[i])
